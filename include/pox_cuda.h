@@ -1,0 +1,152 @@
+/*
+ * pox_cuda.h -- C ABI of the B200 (sm_100a) CUDA backend for ParaOxidizer's decode hot path.
+ *
+ * Plain pointers and sizes only: no C++ or torch types cross this boundary, so the Rust side
+ * binds it with an `extern "C"` block (the binding a maintainer adds is shown in
+ * INTEGRATION.md). Every entry point cites the reference interface it replaces; paths are
+ * relative to the reference repository root.
+ *
+ * Layout contract: all weight buffers are the unchanged `.pox` payloads
+ * (crates/paraoxidizer-format/src/pox.rs:434-495): INT4 = packed nibbles (low nibble = even
+ * column, kernels.rs:15-23) per row of ceil(cols/2) bytes, scale_data = per (row, group) an
+ * f16 scale then an f16 min (kernels.rs:57-62); INT8 = int8 per element plus one f32
+ * per-tensor scale (kernels.rs:131-154); outliers = u32 count | u32 flat indices | f16 values
+ * (outlier.rs:99-110), whose values REPLACE the dequantized weight (kernels.rs:211-219).
+ *
+ * Errors: every call returns a pox_status. The reference returns Result<(), PoxError>; a
+ * caller maps POX_ERR_LAYOUT to PoxError::Quantization and the rest to PoxError::Runtime
+ * (crates/paraoxidizer-core/src/error.rs:25-26,50-51). pox_cuda_last_error() gives the message
+ * of the last failure on the calling thread.
+ *
+ * Threading: a context may be shared by threads (the engine is shared through Arc across
+ * spawn_blocking tasks, crates/paraoxidizer-serve/src/server.rs:136); calls on one context
+ * are serialized internally. Synchronous calls return after the result is in host memory.
+ */
+#ifndef POX_CUDA_H
+#define POX_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    POX_OK = 0,
+    POX_ERR_LAYOUT = 1,      /* buffer sizes / dimensions inconsistent (PoxError::Quantization) */
+    POX_ERR_UNSUPPORTED = 2, /* valid input this backend does not handle: caller uses the CPU path */
+    POX_ERR_CUDA = 3,        /* CUDA runtime failure (PoxError::Runtime) */
+    POX_ERR_NCCL = 4,        /* collective failure */
+    POX_ERR_TIMEOUT = 5,     /* a bounded wait ran out */
+    POX_ERR_OOM = 6,         /* device memory or paged-KV blocks exhausted */
+    POX_ERR_INVALID = 7      /* null pointer, bad handle or argument */
+} pox_status;
+
+/* DType codes, crates/paraoxidizer-core/src/tensor.rs:4-20 */
+typedef enum { POX_F32 = 0, POX_F16 = 1, POX_BF16 = 2, POX_I8 = 3, POX_I4 = 4 } pox_dtype;
+
+typedef struct pox_cuda_ctx pox_cuda_ctx;
+typedef struct pox_tensor pox_tensor;
+
+/* ---- library / context ------------------------------------------------------------------ */
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* pox_cuda_last_error(void);
+/* Library version string. */
+const char* pox_cuda_version(void);
+/* Number of CUDA devices visible (0 when there is no GPU). */
+int pox_cuda_device_count(int* out);
+
+/* Replaces MetalBackend::new() -> Option<Arc<Self>> (crates/paraoxidizer-runtime/src/
+ * metal_backend.rs:64-82; the non-macOS stub returning None is :193-195). On failure *out is
+ * NULL and the caller keeps the CPU path, as the engine does with None (engine.rs:97,174-207). */
+int pox_cuda_create(int device, pox_cuda_ctx** out);
+/* Frees every device buffer the context owns (resident tensors included). */
+void pox_cuda_destroy(pox_cuda_ctx* ctx);
+/* Waits for all work issued on the context's stream. */
+int pox_cuda_synchronize(pox_cuda_ctx* ctx);
+/* The context's CUDA stream (a cudaStream_t), for callers that chain async calls. */
+void* pox_cuda_stream(pox_cuda_ctx* ctx);
+
+/* ---- reference-shaped GEMV entry points (host slices, synchronous) ---------------------- */
+
+/* Replaces MetalBackend::gemv_int4(&self, packed_weights, scale_data, rows, cols, group_size,
+ * x, y) (metal_backend.rs:85-181): y[r] = sum_c (min_g + q*scale_g) * x[c].
+ * rows == 0 || cols == 0 -> POX_OK with nothing written (:95-97).
+ * scale_len < rows*ceil(cols/gs)*4 or packed_len < rows*ceil(cols/2) -> POX_ERR_LAYOUT
+ * (:99-108). x needs cols floats, y rows floats (else POX_ERR_LAYOUT).
+ * If (packed, scale_data) were registered by pox_cuda_tensor_upload, the resident copy is
+ * used and only x and y cross the bus; otherwise the weights are copied for this call only,
+ * as the Metal backend does (:111-129). */
+int pox_cuda_gemv_int4(pox_cuda_ctx* ctx, const uint8_t* packed_weights, size_t packed_len,
+                       const uint8_t* scale_data, size_t scale_len, size_t rows, size_t cols,
+                       size_t group_size, const float* x, size_t x_len, float* y, size_t y_len);
+
+/* Replaces quant::gemv_int4(packed, scale_data, group_size, rows, cols, outliers, x, y)
+ * (crates/paraoxidizer-quant/src/kernels.rs:177-226) with the outlier table given in its
+ * serialized .pox form (outlier.rs:99-110; NULL/len < 4 = no outliers, outlier.rs:113-115).
+ * A table whose count runs past outlier_len -> POX_ERR_LAYOUT (from_bytes Err, :116-124).
+ * Entries whose flat index is >= rows*cols are ignored, duplicates: the last entry wins. */
+int pox_cuda_gemv_int4_outliers(pox_cuda_ctx* ctx, const uint8_t* packed_weights, size_t packed_len,
+                                const uint8_t* scale_data, size_t scale_len, size_t group_size,
+                                size_t rows, size_t cols, const uint8_t* outlier_data,
+                                size_t outlier_len, const float* x, size_t x_len, float* y,
+                                size_t y_len);
+
+/* Replaces quant::gemv_int8(q_weights, scale_data, rows, cols, x, y) (kernels.rs:229-255):
+ * y[r] = sum_c q*scale*x[c] with the single f32 per-tensor scale. x_len < cols, y_len < rows,
+ * q_len < rows*cols or scale_len < 4 -> POX_ERR_LAYOUT (:237-241). The runtime's I8 path
+ * ignores outlier tables (engine.rs:232-234), so this entry point takes none. */
+int pox_cuda_gemv_int8(pox_cuda_ctx* ctx, const uint8_t* q_weights, size_t q_len,
+                       const uint8_t* scale_data, size_t scale_len, size_t rows, size_t cols,
+                       const float* x, size_t x_len, float* y, size_t y_len);
+
+/* ---- resident tensors: upload once, then call with device pointers ---------------------- */
+
+/* One .pox tensor (TensorMeta, crates/paraoxidizer-core/src/tensor.rs:116-128, plus the three
+ * payload slices PoxFile::get_{tensor,scale,outlier}_data return, pox.rs:311-353). */
+typedef struct {
+    int dtype;            /* POX_I4, POX_I8 or POX_F16 */
+    size_t rows, cols;    /* shape [rows, cols] (meta.shape.dims()[0..2]) */
+    size_t group_size;    /* INT4 group size (meta.group_size), ignored otherwise */
+    const uint8_t* data;  size_t data_len;
+    const uint8_t* scales; size_t scale_len;   /* may be NULL for F16 */
+    const uint8_t* outliers; size_t outlier_len; /* may be NULL; ignored for I8 (engine.rs:232) */
+} pox_tensor_desc;
+
+/* Uploads the tensor to HBM once, in the backend's device layout (INT4/INT8 weights re-tiled
+ * for 128-bit loads and tensor-core fragments; outlier table turned into a per-row CSR with
+ * precomputed corrections). Replaces the per-call copies of metal_backend.rs:111-129 and the
+ * per-call SparseOutlierTable::from_bytes of engine.rs:150-151. The host pointers are
+ * remembered so that pox_cuda_gemv_int4* calls on the same slices reuse the resident copy:
+ * the caller must not modify those host bytes while the tensor is alive (they are an
+ * immutable mmap in the reference, pox.rs:171-175). */
+int pox_cuda_tensor_upload(pox_cuda_ctx* ctx, const pox_tensor_desc* desc, pox_tensor** out);
+/* Frees a resident tensor (NULL is a no-op). */
+int pox_cuda_tensor_free(pox_cuda_ctx* ctx, pox_tensor* t);
+/* Shape and footprint of a resident tensor; any out pointer may be NULL. */
+int pox_cuda_tensor_info(const pox_tensor* t, size_t* rows, size_t* cols, size_t* outlier_count,
+                         size_t* device_bytes);
+
+/* y[b][r] = sum_c W[r][c] * x[b][c] for b < batch, on device pointers, asynchronously on
+ * `stream` (a cudaStream_t; NULL = the context's stream). x: [batch][cols] f32, y:
+ * [batch][rows] f32, both device memory. Replaces project_tensor's per-dtype GEMV
+ * (crates/paraoxidizer-runtime/src/engine.rs:131-291) for a resident weight. */
+int pox_cuda_tensor_gemv(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x_dev, size_t batch,
+                         float* y_dev, void* stream);
+/* Same with host x/y: copies x in and y out, synchronous. */
+int pox_cuda_tensor_gemv_host(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x, size_t batch,
+                              float* y);
+/* Dequantizes a resident tensor into out_dev ([rows][cols] f32, device), bit-exact with
+ * dequantize_int4_group / dequantize_int8_symmetric (kernels.rs:85-128,157-173) followed by
+ * SparseOutlierTable::apply_to (outlier.rs:88-95). Asynchronous on `stream`. */
+int pox_cuda_tensor_dequant(pox_cuda_ctx* ctx, const pox_tensor* t, float* out_dev, void* stream);
+/* Host-output variant of pox_cuda_tensor_dequant, synchronous; out holds rows*cols floats. */
+int pox_cuda_tensor_dequant_host(pox_cuda_ctx* ctx, const pox_tensor* t, float* out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* POX_CUDA_H */

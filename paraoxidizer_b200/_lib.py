@@ -1,0 +1,113 @@
+"""ctypes binding of libpox_cuda.so (the C ABI declared in include/pox_cuda.h).
+
+The library is required: importing the GPU entry points without it raises immediately
+(there is no CPU fallback in this package).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "libpox_cuda.so")
+HEADER = os.path.join(os.path.dirname(_PKG), "include", "pox_cuda.h")
+
+POX_OK, POX_ERR_LAYOUT, POX_ERR_UNSUPPORTED, POX_ERR_CUDA = 0, 1, 2, 3
+POX_ERR_NCCL, POX_ERR_TIMEOUT, POX_ERR_OOM, POX_ERR_INVALID = 4, 5, 6, 7
+STATUS_NAMES = {0: "OK", 1: "LAYOUT", 2: "UNSUPPORTED", 3: "CUDA", 4: "NCCL", 5: "TIMEOUT", 6: "OOM", 7: "INVALID"}
+
+# DType codes (crates/paraoxidizer-core/src/tensor.rs:4-20)
+POX_F32, POX_F16, POX_BF16, POX_I8, POX_I4 = 0, 1, 2, 3, 4
+
+
+class PoxError(Exception):
+    """Mirror of crates/paraoxidizer-core/src/error.rs:6-58 for the codes this backend returns."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"{STATUS_NAMES.get(code, code)}: {msg}")
+        self.code = code
+
+
+class QuantizationError(PoxError):
+    """PoxError::Quantization (layout / dimension mismatch, error.rs:25-26)."""
+
+
+class RuntimeBackendError(PoxError):
+    """PoxError::Runtime (error.rs:50-51)."""
+
+
+class TensorDesc(C.Structure):
+    _fields_ = [("dtype", C.c_int), ("rows", C.c_size_t), ("cols", C.c_size_t), ("group_size", C.c_size_t),
+                ("data", C.c_void_p), ("data_len", C.c_size_t), ("scales", C.c_void_p), ("scale_len", C.c_size_t),
+                ("outliers", C.c_void_p), ("outlier_len", C.c_size_t)]
+
+
+_lib = None
+
+
+def declared_symbols() -> list[str]:
+    """Every function name include/pox_cuda.h declares."""
+    with open(HEADER) as f:
+        src = f.read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(pox_cuda_\w+)\s*\(", src)))
+
+
+def _declare(L):
+    vp, sz, i32 = C.c_void_p, C.c_size_t, C.c_int
+    sig = {
+        "pox_cuda_last_error": (C.c_char_p, []),
+        "pox_cuda_version": (C.c_char_p, []),
+        "pox_cuda_device_count": (i32, [C.POINTER(C.c_int)]),
+        "pox_cuda_create": (i32, [i32, C.POINTER(vp)]),
+        "pox_cuda_destroy": (None, [vp]),
+        "pox_cuda_synchronize": (i32, [vp]),
+        "pox_cuda_stream": (vp, [vp]),
+        "pox_cuda_gemv_int4": (i32, [vp, vp, sz, vp, sz, sz, sz, sz, vp, sz, vp, sz]),
+        "pox_cuda_gemv_int4_outliers": (i32, [vp, vp, sz, vp, sz, sz, sz, sz, vp, sz, vp, sz, vp, sz]),
+        "pox_cuda_gemv_int8": (i32, [vp, vp, sz, vp, sz, sz, sz, vp, sz, vp, sz]),
+        "pox_cuda_tensor_upload": (i32, [vp, C.POINTER(TensorDesc), C.POINTER(vp)]),
+        "pox_cuda_tensor_free": (i32, [vp, vp]),
+        "pox_cuda_tensor_info": (i32, [vp, C.POINTER(sz), C.POINTER(sz), C.POINTER(sz), C.POINTER(sz)]),
+        "pox_cuda_tensor_gemv": (i32, [vp, vp, vp, sz, vp, vp]),
+        "pox_cuda_tensor_gemv_host": (i32, [vp, vp, vp, sz, vp]),
+        "pox_cuda_tensor_dequant": (i32, [vp, vp, vp, vp]),
+        "pox_cuda_tensor_dequant_host": (i32, [vp, vp, vp]),
+    }
+    for name, (res, args) in sig.items():
+        if hasattr(L, name):
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+    try:
+        from . import _lib_ext
+        _lib_ext.declare(L)
+    except ImportError:
+        pass
+
+
+def lib():
+    """Load libpox_cuda.so (raises if it has not been built: no silent fallback)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing: build it with `python -m paraoxidizer_b200.build`")
+        L = C.CDLL(LIB_PATH)
+        _declare(L)
+        _lib = L
+    return _lib
+
+
+def last_error() -> str:
+    m = lib().pox_cuda_last_error()
+    return m.decode() if m else ""
+
+
+def check(rc: int) -> None:
+    if rc == POX_OK:
+        return
+    msg = last_error()
+    if rc == POX_ERR_LAYOUT:
+        raise QuantizationError(rc, msg)
+    raise RuntimeBackendError(rc, msg)

@@ -1,0 +1,61 @@
+// api_internal.h -- host-side structures shared by the C ABI translation units.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <mutex>
+#include <vector>
+
+#include "../../include/pox_cuda.h"
+
+struct pox_tensor {
+    int dtype = POX_I4;
+    size_t rows = 0, cols = 0, gs = 0;
+    int groups = 0;
+    bool tiled = false;        // re-tiled device layout (tensor-core GEMV) vs raw .pox layout
+    void* w = nullptr;         // tiles or raw payload
+    void* scales_dev = nullptr;
+    float i8_scale = 0.f;
+    uint32_t* row_ptr = nullptr;  // outlier CSR by row (raw layout): entries = (col, corr)
+    uint32_t* item_ptr = nullptr; // outlier CSR by streamed item (tiled): entries = (col<<4 | row%16, corr)
+    uint2* entries = nullptr;     // corr = f32 bits of v - dequant(q)
+    uint16_t* vals = nullptr;     // f16 outlier values (dequantization path)
+    size_t nnz = 0;
+    void* scratch = nullptr;      // split-K partials + row-tile counters of the streaming GEMV
+    size_t scratch_bytes = 0;
+    size_t bytes = 0;
+    // host slices the tensor was uploaded from (registry key of the host-slice entry points)
+    const uint8_t* h_data = nullptr;
+    size_t h_data_len = 0;
+    const uint8_t* h_scales = nullptr;
+    size_t h_scale_len = 0;
+    const uint8_t* h_outliers = nullptr;
+    size_t h_outlier_len = 0;
+};
+
+struct pox_cuda_ctx {
+    int device = 0;
+    int num_sms = 148;
+    cudaStream_t stream = nullptr;
+    std::mutex mu;
+    std::vector<pox_tensor*> tensors;
+    void* scratch_x = nullptr;
+    size_t scratch_x_bytes = 0;
+    void* scratch_y = nullptr;
+    size_t scratch_y_bytes = 0;
+    int* err_host = nullptr;  // kernel error flag (host-mapped); nonzero = a bounded wait expired
+    int* err_dev = nullptr;
+    void* extras = nullptr;  // owned by other translation units (decode engine state)
+};
+
+namespace pox {
+int set_error(int code, const char* fmt, ...);
+int cuda_error(cudaError_t e, const char* what);
+int ensure_scratch(pox_cuda_ctx* ctx, size_t xbytes, size_t ybytes);
+int upload_tensor_locked(pox_cuda_ctx* ctx, const pox_tensor_desc* d, pox_tensor** out, bool keep);
+int gemv_launch(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x, size_t batch, float* y, cudaStream_t st);
+void destroy_ctx_extras(pox_cuda_ctx* ctx);
+// After a synchronize: turns a raised kernel error flag into POX_ERR_TIMEOUT (and clears it).
+int take_kernel_error(pox_cuda_ctx* ctx);
+}  // namespace pox

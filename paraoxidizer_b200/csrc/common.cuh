@@ -1,0 +1,132 @@
+// common.cuh -- shared device helpers for the sm_100a kernels of the decode hot path.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace pox {
+
+// Device layout constants of the re-tiled quantized weights.
+// One tile = 16 rows x one k-block, 1 KiB: the 32 lanes of a warp own 32 contiguous bytes each
+// (16 bytes of row g and 16 bytes of row g+8, g = lane/4), in the order the m16n8k16 A fragment
+// consumes them, so that a tile is read with two fully coalesced 512-byte warp loads.
+constexpr int kTileRows = 16;
+constexpr int kTileBytes = 1024;
+constexpr int kI4KBlock = 128;  // k per INT4 tile (4 bits x 16 rows x 128 = 1 KiB)
+constexpr int kI8KBlock = 64;   // k per INT8 tile (8 bits x 16 rows x 64 = 1 KiB)
+
+__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t c) {
+    // (a & b) | c
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+
+__device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+__device__ __forceinline__ uint32_t hfma2_u32(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// Four INT4 nibbles of one word -> four exact f16 pairs, using the exponent-bias trick:
+// (v & 0x000F000F) | 0x6400_6400 is the f16 pair (1024+q_lo, 1024+q_hi), so subtracting 1024
+// gives q exactly; the 0x00F0 nibbles give 1024+16q, scaled by 1/16 and shifted by -64.
+// Word bit layout (see the repacking kernel): nibble positions (0,4)->r0, (1,5)->r1,
+// (2,6)->r2, (3,7)->r3, each pair being two consecutive k of one MMA fragment register.
+__device__ __forceinline__ void i4x8_to_f16x8(uint32_t v, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                              uint32_t& r3) {
+    const uint32_t kMagic = 0x64006400u;
+    const uint32_t k1024 = 0x64006400u;  // f16 pair (1024, 1024)
+    const uint32_t kSixteenth = 0x2C002C00u;  // f16 pair (1/16, 1/16)
+    const uint32_t kNeg64 = 0xD400D400u;      // f16 pair (-64, -64)
+    uint32_t v8 = v >> 8;
+    r0 = hsub2_u32(lop3_and_or(v, 0x000F000Fu, kMagic), k1024);
+    r1 = hfma2_u32(lop3_and_or(v, 0x00F000F0u, kMagic), kSixteenth, kNeg64);
+    r2 = hsub2_u32(lop3_and_or(v8, 0x000F000Fu, kMagic), k1024);
+    r3 = hfma2_u32(lop3_and_or(v8, 0x00F000F0u, kMagic), kSixteenth, kNeg64);
+}
+
+// Four INT8 values of one word (bytes b0..b3, k order) -> two exact f16 pairs (b0,b1), (b2,b3):
+// flip the sign bit to get u = q+128, place u under the f16 exponent of 1024 with PRMT, and
+// subtract 1152.
+__device__ __forceinline__ void i8x4_to_f16x4(uint32_t v, uint32_t& r0, uint32_t& r1) {
+    const uint32_t u = v ^ 0x80808080u;
+    const uint32_t k1152 = 0x64806480u;  // f16 pair (1152, 1152)
+    r0 = hsub2_u32(prmt(u, 0x64646464u, 0x4140u), k1152);
+    r1 = hsub2_u32(prmt(u, 0x64646464u, 0x4342u), k1152);
+}
+
+// D = A(16x16 f16, row) * B(16x8 f16, col) + C, f32 accumulate.
+__device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                          uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// D += A(16x32 u8, row) * B(32x8 s8, col), s32 accumulate (exact integer arithmetic).
+__device__ __forceinline__ void imma_16832_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                                uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// D += A(16x32 s8, row) * B(32x8 s8, col), s32 accumulate.
+__device__ __forceinline__ void imma_16832_s8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                                uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// 128-bit streaming load that does not allocate in L1 (weights are read exactly once).
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t ldg_u32_nc(const void* p) {
+    uint32_t r;
+    asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(r) : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ uint2 lds_u64(const void* p) {
+    uint2 r;
+    uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(p));
+    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "r"(a));
+    return r;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float half_bits_to_float(uint32_t bits16) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16 & 0xFFFFu)));
+}
+
+}  // namespace pox

@@ -1,0 +1,694 @@
+// pox_api.cu -- the C ABI of include/pox_cuda.h: contexts, resident tensors (upload once, device
+// re-tiling, outlier CSR), and the reference-shaped GEMV / dequantization entry points.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/pox_cuda.h"
+#include "api_internal.h"
+#include "common.cuh"
+#include "gemv.cuh"
+
+using namespace pox;
+
+// ------------------------------------------------------------------------------------------
+// errors
+// ------------------------------------------------------------------------------------------
+static thread_local std::string t_last_error;
+
+int pox::set_error(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    t_last_error = buf;
+    return code;
+}
+
+int pox::cuda_error(cudaError_t e, const char* what) {
+    if (e == cudaErrorMemoryAllocation)
+        return set_error(POX_ERR_OOM, "%s: %s", what, cudaGetErrorString(e));
+    return set_error(POX_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define CK(call, what)                               \
+    do {                                             \
+        cudaError_t _e = (call);                     \
+        if (_e != cudaSuccess) return cuda_error(_e, what); \
+    } while (0)
+
+extern "C" const char* pox_cuda_last_error(void) { return t_last_error.c_str(); }
+extern "C" const char* pox_cuda_version(void) { return "pox_cuda 0.1.0 (sm_100a)"; }
+
+extern "C" int pox_cuda_device_count(int* out) {
+    if (!out) return set_error(POX_ERR_INVALID, "out is NULL");
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+    }
+    *out = n;
+    return POX_OK;
+}
+
+// ------------------------------------------------------------------------------------------
+// context
+// ------------------------------------------------------------------------------------------
+extern "C" int pox_cuda_create(int device, pox_cuda_ctx** out) {
+    if (!out) return set_error(POX_ERR_INVALID, "out is NULL");
+    *out = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+        cudaGetLastError();
+        return set_error(POX_ERR_UNSUPPORTED, "no CUDA device available");
+    }
+    if (device < 0 || device >= n) return set_error(POX_ERR_INVALID, "device %d out of range (%d devices)", device, n);
+    CK(cudaSetDevice(device), "cudaSetDevice");
+    cudaDeviceProp prop;
+    CK(cudaGetDeviceProperties(&prop, device), "cudaGetDeviceProperties");
+    if (prop.major != 10)
+        return set_error(POX_ERR_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a", device,
+                         prop.major, prop.minor);
+    auto* c = new pox_cuda_ctx();
+    c->device = device;
+    c->num_sms = prop.multiProcessorCount;
+    cudaError_t e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+        delete c;
+        return cuda_error(e, "cudaStreamCreate");
+    }
+    // kernel error flag (bounded waits that expired), mapped so the host reads it without a copy
+    e = cudaHostAlloc((void**)&c->err_host, sizeof(int), cudaHostAllocMapped);
+    if (e == cudaSuccess) e = cudaHostGetDevicePointer((void**)&c->err_dev, c->err_host, 0);
+    if (e != cudaSuccess) {
+        cudaStreamDestroy(c->stream);
+        delete c;
+        return cuda_error(e, "cudaHostAlloc(error flag)");
+    }
+    *c->err_host = 0;
+    *out = c;
+    return POX_OK;
+}
+
+static void free_tensor_mem(pox_tensor* t) {
+    if (!t) return;
+    cudaFree(t->w);
+    cudaFree(t->scales_dev);
+    cudaFree(t->row_ptr);
+    cudaFree(t->item_ptr);
+    cudaFree(t->entries);
+    cudaFree(t->vals);
+    cudaFree(t->scratch);
+    t->scratch = nullptr;
+    t->w = t->scales_dev = nullptr;
+    t->row_ptr = nullptr;
+    t->item_ptr = nullptr;
+    t->entries = nullptr;
+    t->vals = nullptr;
+}
+
+extern "C" void pox_cuda_destroy(pox_cuda_ctx* ctx) {
+    if (!ctx) return;
+    {
+        std::lock_guard<std::mutex> lk(ctx->mu);
+        cudaSetDevice(ctx->device);
+        cudaStreamSynchronize(ctx->stream);
+        for (pox_tensor* t : ctx->tensors) {
+            free_tensor_mem(t);
+            delete t;
+        }
+        ctx->tensors.clear();
+        cudaFree(ctx->scratch_x);
+        cudaFree(ctx->scratch_y);
+        cudaFreeHost(ctx->err_host);
+        cudaStreamDestroy(ctx->stream);
+    }
+    pox::destroy_ctx_extras(ctx);
+    delete ctx;
+}
+
+int pox::take_kernel_error(pox_cuda_ctx* ctx) {
+    const int f = *(volatile int*)ctx->err_host;
+    if (f == 0) return POX_OK;
+    *(volatile int*)ctx->err_host = 0;
+    return set_error(POX_ERR_TIMEOUT, "a kernel's bounded wait expired (flag 0x%x); results of that call are invalid", f);
+}
+
+extern "C" int pox_cuda_synchronize(pox_cuda_ctx* ctx) {
+    if (!ctx) return set_error(POX_ERR_INVALID, "ctx is NULL");
+    CK(cudaSetDevice(ctx->device), "cudaSetDevice");
+    CK(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+    return take_kernel_error(ctx);
+}
+
+extern "C" void* pox_cuda_stream(pox_cuda_ctx* ctx) { return ctx ? (void*)ctx->stream : nullptr; }
+
+int pox::ensure_scratch(pox_cuda_ctx* ctx, size_t xbytes, size_t ybytes) {
+    if (xbytes > ctx->scratch_x_bytes) {
+        cudaFree(ctx->scratch_x);
+        ctx->scratch_x = nullptr;
+        ctx->scratch_x_bytes = 0;
+        CK(cudaMalloc(&ctx->scratch_x, xbytes), "cudaMalloc(x scratch)");
+        ctx->scratch_x_bytes = xbytes;
+    }
+    if (ybytes > ctx->scratch_y_bytes) {
+        cudaFree(ctx->scratch_y);
+        ctx->scratch_y = nullptr;
+        ctx->scratch_y_bytes = 0;
+        CK(cudaMalloc(&ctx->scratch_y, ybytes), "cudaMalloc(y scratch)");
+        ctx->scratch_y_bytes = ybytes;
+    }
+    return POX_OK;
+}
+
+// ------------------------------------------------------------------------------------------
+// tensors
+// ------------------------------------------------------------------------------------------
+static inline size_t div_ceil(size_t a, size_t b) { return (a + b - 1) / b; }
+
+static float h2f(uint16_t b) {
+    __half_raw r;
+    r.x = b;
+    return __half2float(__half(r));
+}
+
+// Validation shared by the upload and the host-slice entry points (metal_backend.rs:95-108,
+// kernels.rs:237-241).
+static int validate_desc(const pox_tensor_desc* d) {
+    if (!d) return set_error(POX_ERR_INVALID, "desc is NULL");
+    if (d->rows == 0 || d->cols == 0) return POX_OK;
+    if (!d->data) return set_error(POX_ERR_INVALID, "data is NULL");
+    if (d->rows > 0x7FFFFFFF || d->cols > 0x7FFFFFFF)
+        return set_error(POX_ERR_UNSUPPORTED, "dimension beyond 2^31");
+    switch (d->dtype) {
+        case POX_I4: {
+            if (d->group_size == 0) return set_error(POX_ERR_LAYOUT, "INT4 group_size is 0");
+            if (d->group_size % 2 != 0)
+                return set_error(POX_ERR_UNSUPPORTED, "odd INT4 group size %zu", d->group_size);
+            const size_t req_s = d->rows * div_ceil(d->cols, d->group_size) * 4;
+            const size_t req_w = d->rows * div_ceil(d->cols, 2);
+            if (d->scale_len < req_s || d->data_len < req_w || (!d->scales && req_s))
+                return set_error(POX_ERR_LAYOUT, "Buffer layout incompatible with 2D GEMV (need %zu weight bytes, %zu "
+                                 "scale bytes; got %zu, %zu)", req_w, req_s, d->data_len, d->scale_len);
+            return POX_OK;
+        }
+        case POX_I8:
+            if (d->data_len < d->rows * d->cols || d->scale_len < 4 || !d->scales)
+                return set_error(POX_ERR_LAYOUT, "GEMV INT8 dimension mismatch");
+            return POX_OK;
+        case POX_F16:
+            if (d->data_len < d->rows * d->cols * 2) return set_error(POX_ERR_LAYOUT, "F16 weight buffer too small");
+            return POX_OK;
+        default:
+            return set_error(POX_ERR_UNSUPPORTED, "dtype %d not supported", d->dtype);
+    }
+}
+
+// Builds the per-row CSR of an INT4 outlier table. Entries are applied in table order by the
+// reference (kernels.rs:211-219), so for a repeated slot the last entry wins. The stored
+// correction is v - dequant(q): adding corr * x to the tiled GEMV reproduces "replace".
+static int build_outlier_csr(const pox_tensor_desc* d, std::vector<uint32_t>& row_ptr, std::vector<uint32_t>& cols,
+                             std::vector<float>& corr, std::vector<uint16_t>& vals) {
+    row_ptr.assign(d->rows + 1, 0);
+    cols.clear();
+    corr.clear();
+    vals.clear();
+    if (!d->outliers || d->outlier_len < 4) return POX_OK;  // outlier.rs:113-115
+    const uint8_t* b = d->outliers;
+    const uint64_t count = (uint64_t)b[0] | ((uint64_t)b[1] << 8) | ((uint64_t)b[2] << 16) | ((uint64_t)b[3] << 24);
+    if (4 + 6 * count > d->outlier_len)
+        return set_error(POX_ERR_LAYOUT, "outlier table truncated: %llu entries need %llu bytes, have %zu",
+                         (unsigned long long)count, (unsigned long long)(4 + 6 * count), d->outlier_len);
+    const uint64_t numel = (uint64_t)d->rows * d->cols;
+    if (numel > 0xFFFFFFFFull && count)
+        return set_error(POX_ERR_UNSUPPORTED, "outlier indices of a tensor beyond 2^32 elements");
+    struct E { uint32_t row, col, order; uint16_t val; };
+    std::vector<E> es;
+    es.reserve(count);
+    for (uint64_t i = 0; i < count; i++) {
+        const uint8_t* p = b + 4 + 4 * i;
+        const uint32_t idx = (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+        const uint8_t* pv = b + 4 + 4 * count + 2 * i;
+        const uint16_t v = (uint16_t)(pv[0] | (pv[1] << 8));
+        if ((uint64_t)idx >= numel) continue;
+        es.push_back({(uint32_t)(idx / d->cols), (uint32_t)(idx % d->cols), (uint32_t)i, v});
+    }
+    std::sort(es.begin(), es.end(), [](const E& a, const E& b) {
+        if (a.row != b.row) return a.row < b.row;
+        if (a.col != b.col) return a.col < b.col;
+        return a.order < b.order;
+    });
+    const size_t row_bytes = div_ceil(d->cols, 2);
+    const size_t gpr = div_ceil(d->cols, d->group_size);
+    for (size_t i = 0; i < es.size(); i++) {
+        if (i + 1 < es.size() && es[i + 1].row == es[i].row && es[i + 1].col == es[i].col) continue;  // last wins
+        const E& e = es[i];
+        const uint8_t byte = d->data[(size_t)e.row * row_bytes + e.col / 2];
+        const uint32_t q = (e.col & 1) ? (byte >> 4) : (byte & 15u);
+        const uint8_t* sp = d->scales + ((size_t)e.row * gpr + e.col / d->group_size) * 4;
+        const float sc = h2f((uint16_t)(sp[0] | (sp[1] << 8)));
+        const float mn = h2f((uint16_t)(sp[2] | (sp[3] << 8)));
+        volatile float t = (float)q * sc;  // dequantize_int4_group: mul, then add (kernels.rs:118)
+        const float deq = mn + t;
+        row_ptr[e.row + 1]++;
+        cols.push_back(e.col);
+        corr.push_back(h2f(e.val) - deq);
+        vals.push_back(e.val);
+    }
+    for (size_t r = 0; r < d->rows; r++) row_ptr[r + 1] += row_ptr[r];
+    return POX_OK;
+}
+
+template <class T>
+static int upload_vec(const std::vector<T>& v, void** dst, size_t* bytes, cudaStream_t st) {
+    if (v.empty()) return POX_OK;
+    CK(cudaMalloc(dst, v.size() * sizeof(T)), "cudaMalloc(outliers)");
+    CK(cudaMemcpyAsync(*dst, v.data(), v.size() * sizeof(T), cudaMemcpyHostToDevice, st), "cudaMemcpy(outliers)");
+    *bytes += v.size() * sizeof(T);
+    return POX_OK;
+}
+
+int pox::upload_tensor_locked(pox_cuda_ctx* ctx, const pox_tensor_desc* d, pox_tensor** out, bool keep) {
+    int rc = validate_desc(d);
+    if (rc) return rc;
+    auto* t = new pox_tensor();
+    t->dtype = d->dtype;
+    t->rows = d->rows;
+    t->cols = d->cols;
+    t->gs = d->group_size;
+    t->h_data = d->data;
+    t->h_data_len = d->data_len;
+    t->h_scales = d->scales;
+    t->h_scale_len = d->scale_len;
+    t->h_outliers = d->outliers;
+    t->h_outlier_len = d->outlier_len;
+    if (d->rows == 0 || d->cols == 0) {
+        if (keep) ctx->tensors.push_back(t);
+        *out = t;
+        return POX_OK;
+    }
+    cudaStream_t st = ctx->stream;
+    const int N = (int)d->rows, K = (int)d->cols;
+    void* tmp = nullptr;
+    void* tmp_s = nullptr;
+    auto fail = [&](int code) {
+        cudaStreamSynchronize(st);
+        cudaFree(tmp);
+        cudaFree(tmp_s);
+        free_tensor_mem(t);
+        delete t;
+        return code;
+    };
+#define CKF(call, what)                                          \
+    do {                                                         \
+        cudaError_t _e = (call);                                 \
+        if (_e != cudaSuccess) return fail(cuda_error(_e, what)); \
+    } while (0)
+
+    if (d->dtype == POX_I4) {
+        const size_t raw_bytes = d->rows * div_ceil(d->cols, 2);
+        const size_t groups = div_ceil(d->cols, d->group_size);
+        const size_t sbytes = d->rows * groups * 4;
+        t->groups = (int)groups;
+        t->tiled = (K % 128 == 0) && (d->group_size % 128 == 0);
+        CKF(cudaMalloc(&tmp, raw_bytes), "cudaMalloc(raw)");
+        CKF(cudaMemcpyAsync(tmp, d->data, raw_bytes, cudaMemcpyHostToDevice, st), "cudaMemcpy(raw)");
+        if (t->tiled) {
+            const TileLayout TL(kKindI4, N, K);
+            CKF(cudaMalloc(&t->w, TL.bytes()), "cudaMalloc(blobs)");
+            CKF(cudaMemsetAsync(t->w, 0, TL.bytes(), st), "cudaMemset(blobs)");
+            CKF(launch_repack(kKindI4, (const uint8_t*)tmp, (uint8_t*)t->w, N, K, st), "repack_i4");
+            CKF(cudaMalloc(&tmp_s, sbytes), "cudaMalloc(raw scales)");
+            CKF(cudaMemcpyAsync(tmp_s, d->scales, sbytes, cudaMemcpyHostToDevice, st), "cudaMemcpy(scales)");
+            CKF(launch_repack_i4_scales((const uint8_t*)tmp_s, (uint8_t*)t->w, N, K, (int)d->group_size, st),
+                "repack_i4_scales");
+            t->bytes += TL.bytes();
+        } else {
+            t->w = tmp;
+            tmp = nullptr;
+            t->bytes += raw_bytes;
+            CKF(cudaMalloc(&t->scales_dev, sbytes), "cudaMalloc(scales)");
+            CKF(cudaMemcpyAsync(t->scales_dev, d->scales, sbytes, cudaMemcpyHostToDevice, st), "cudaMemcpy(scales)");
+            t->bytes += sbytes;
+        }
+        std::vector<uint32_t> rp, cols;
+        std::vector<float> corr;
+        std::vector<uint16_t> vals;
+        rc = build_outlier_csr(d, rp, cols, corr, vals);
+        if (rc) return fail(rc);
+        std::vector<uint32_t> ip;
+        std::vector<uint2> ent(cols.size());
+        std::vector<uint16_t> ivals;
+        if (!cols.empty() && t->tiled) {
+            // re-key by streamed item (row tile x k-chunk): the GEMV consumer that owns an item
+            // applies that item's outliers with x from its shared-memory window
+            const TileLayout TL(kKindI4, N, K);
+            std::vector<uint32_t> rows(cols.size());
+            for (size_t r = 0; r < d->rows; r++)
+                for (uint32_t e = rp[r]; e < rp[r + 1]; e++) rows[e] = (uint32_t)r;
+            auto item_of = [&](size_t e) {
+                return (uint32_t)((cols[e] / 128 / kChunkTiles) * TL.nT + rows[e] / 16);
+            };
+            std::vector<uint32_t> order(cols.size());
+            for (size_t e = 0; e < order.size(); e++) order[e] = (uint32_t)e;
+            std::stable_sort(order.begin(), order.end(),
+                             [&](uint32_t a, uint32_t b) { return item_of(a) < item_of(b); });
+            ip.assign((size_t)TL.items() + 1, 0);
+            ivals.resize(cols.size());
+            for (size_t i = 0; i < order.size(); i++) {
+                const uint32_t e = order[i];
+                uint32_t cb;
+                std::memcpy(&cb, &corr[e], 4);
+                ent[i] = make_uint2((cols[e] << 4) | (rows[e] & 15u), cb);
+                ivals[i] = vals[e];
+                ip[item_of(e) + 1]++;
+            }
+            for (size_t i = 0; i + 1 < ip.size(); i++) ip[i + 1] += ip[i];
+        } else {
+            for (size_t i = 0; i < cols.size(); i++) {
+                uint32_t cb;
+                std::memcpy(&cb, &corr[i], 4);
+                ent[i] = make_uint2(cols[i], cb);
+            }
+        }
+        if (!cols.empty()) {
+            t->nnz = cols.size();
+            if (t->tiled) {
+                if ((rc = upload_vec(ip, (void**)&t->item_ptr, &t->bytes, st))) return fail(rc);
+                if ((rc = upload_vec(ivals, (void**)&t->vals, &t->bytes, st))) return fail(rc);
+            } else {
+                if ((rc = upload_vec(rp, (void**)&t->row_ptr, &t->bytes, st))) return fail(rc);
+                if ((rc = upload_vec(vals, (void**)&t->vals, &t->bytes, st))) return fail(rc);
+            }
+            ent.push_back(make_uint2(0u, 0u));  // pad: entry copies are rounded up to 16-byte pairs
+            if ((rc = upload_vec(ent, (void**)&t->entries, &t->bytes, st))) return fail(rc);
+            // the host vectors must outlive the async copies
+            CKF(cudaStreamSynchronize(st), "cudaStreamSynchronize(upload)");
+        }
+    } else if (d->dtype == POX_I8) {
+        std::memcpy(&t->i8_scale, d->scales, 4);  // one f32 LE (kernels.rs:150-151)
+        const size_t raw_bytes = d->rows * d->cols;
+        t->tiled = (K % 64 == 0);
+        CKF(cudaMalloc(&tmp, raw_bytes), "cudaMalloc(raw)");
+        CKF(cudaMemcpyAsync(tmp, d->data, raw_bytes, cudaMemcpyHostToDevice, st), "cudaMemcpy(raw)");
+        if (t->tiled) {
+            const size_t tiles_bytes = TileLayout(kKindI8, N, K).bytes();
+            CKF(cudaMalloc(&t->w, tiles_bytes), "cudaMalloc(blobs)");
+            CKF(cudaMemsetAsync(t->w, 0, tiles_bytes, st), "cudaMemset(blobs)");
+            CKF(launch_repack(kKindI8, (const uint8_t*)tmp, (uint8_t*)t->w, N, K, st), "repack_i8");
+            t->bytes += tiles_bytes;
+        } else {
+            t->w = tmp;
+            tmp = nullptr;
+            t->bytes += raw_bytes;
+        }
+    } else {  // F16
+        const size_t raw_bytes = d->rows * d->cols * 2;
+        t->tiled = (K % 32 == 0);
+        CKF(cudaMalloc(&tmp, raw_bytes), "cudaMalloc(raw)");
+        CKF(cudaMemcpyAsync(tmp, d->data, raw_bytes, cudaMemcpyHostToDevice, st), "cudaMemcpy(raw)");
+        if (t->tiled) {
+            const size_t tiles_bytes = TileLayout(kKindF16, N, K).bytes();
+            CKF(cudaMalloc(&t->w, tiles_bytes), "cudaMalloc(blobs)");
+            CKF(cudaMemsetAsync(t->w, 0, tiles_bytes, st), "cudaMemset(blobs)");
+            CKF(launch_repack(kKindF16, (const uint8_t*)tmp, (uint8_t*)t->w, N, K, st), "repack_f16");
+            t->bytes += tiles_bytes;
+        } else {
+            t->w = tmp;
+            tmp = nullptr;
+            t->bytes += raw_bytes;
+        }
+    }
+    if (t->tiled) {
+        const int kind = d->dtype == POX_I4 ? kKindI4 : (d->dtype == POX_I8 ? kKindI8 : kKindF16);
+        const size_t sb = stream_scratch_bytes(kind, N, K);
+        CKF(cudaMalloc(&t->scratch, sb), "cudaMalloc(gemv scratch)");
+        CKF(cudaMemsetAsync(t->scratch, 0, sb, st), "cudaMemset(gemv scratch)");
+        t->scratch_bytes = sb;
+        t->bytes += sb;
+    }
+    CKF(cudaStreamSynchronize(st), "cudaStreamSynchronize(upload)");
+    cudaFree(tmp);
+    cudaFree(tmp_s);
+#undef CKF
+    if (keep) ctx->tensors.push_back(t);
+    *out = t;
+    return POX_OK;
+}
+
+extern "C" int pox_cuda_tensor_upload(pox_cuda_ctx* ctx, const pox_tensor_desc* desc, pox_tensor** out) {
+    if (!ctx || !out) return set_error(POX_ERR_INVALID, "ctx/out is NULL");
+    *out = nullptr;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    CK(cudaSetDevice(ctx->device), "cudaSetDevice");
+    return upload_tensor_locked(ctx, desc, out, true);
+}
+
+extern "C" int pox_cuda_tensor_free(pox_cuda_ctx* ctx, pox_tensor* t) {
+    if (!t) return POX_OK;
+    if (!ctx) return set_error(POX_ERR_INVALID, "ctx is NULL");
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    auto it = std::find(ctx->tensors.begin(), ctx->tensors.end(), t);
+    if (it == ctx->tensors.end()) return set_error(POX_ERR_INVALID, "tensor does not belong to this context");
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    ctx->tensors.erase(it);
+    free_tensor_mem(t);
+    delete t;
+    return POX_OK;
+}
+
+extern "C" int pox_cuda_tensor_info(const pox_tensor* t, size_t* rows, size_t* cols, size_t* outlier_count,
+                                    size_t* device_bytes) {
+    if (!t) return set_error(POX_ERR_INVALID, "tensor is NULL");
+    if (rows) *rows = t->rows;
+    if (cols) *cols = t->cols;
+    if (outlier_count) *outlier_count = t->nnz;
+    if (device_bytes) *device_bytes = t->bytes;
+    return POX_OK;
+}
+
+// ------------------------------------------------------------------------------------------
+// GEMV
+// ------------------------------------------------------------------------------------------
+int pox::gemv_launch(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x, size_t batch, float* y,
+                     cudaStream_t st) {
+    if (t->rows == 0 || t->cols == 0 || batch == 0) return POX_OK;
+    if (((uintptr_t)x & 15) != 0) return set_error(POX_ERR_INVALID, "x must be 16-byte aligned");
+    const int kind = t->dtype == POX_I4 ? kKindI4 : (t->dtype == POX_I8 ? kKindI8 : kKindF16);
+    const int N = (int)t->rows, K = (int)t->cols;
+    size_t done = 0;
+    while (done < batch) {
+        size_t b = std::min<size_t>(batch - done, 8);
+        const float* xb = x + done * t->cols;
+        float* yb = y + done * t->rows;
+        cudaError_t e;
+        if (t->tiled) {
+            const TileLayout TL(kind, N, K);
+            StreamArgs a = {};
+            a.blobs = (const unsigned char*)t->w;
+            a.i8_scale = t->i8_scale;
+            a.item_ptr = t->item_ptr;
+            a.entries = t->entries;
+            a.x = xb;
+            a.y = yb;
+            a.partial = (float*)t->scratch;
+            a.counters = (unsigned*)((char*)t->scratch + (size_t)TL.nT * TL.nchunks * 16 * kMaxBatch * 4);
+            a.err = ctx->err_dev;
+            a.N = N;
+            a.K = K;
+            a.B = (int)b;
+            e = launch_gemv_stream(kind, a, true, st);
+        } else {
+            GemvGenericArgs a;
+            a.raw = (const uint8_t*)t->w;
+            a.raw_scales = (const uint8_t*)t->scales_dev;
+            a.i8_scale = t->i8_scale;
+            a.row_ptr = t->row_ptr;
+            a.entries = t->entries;
+            a.x = xb;
+            a.y = yb;
+            a.N = N;
+            a.K = K;
+            a.B = (int)b;
+            a.gs = (int)t->gs;
+            a.groups = t->groups;
+            e = launch_gemv_generic(kind, a, st);
+        }
+        if (e != cudaSuccess) return cuda_error(e, "gemv launch");
+        done += b;
+    }
+    return POX_OK;
+}
+
+extern "C" int pox_cuda_tensor_gemv(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x_dev, size_t batch,
+                                    float* y_dev, void* stream) {
+    if (!ctx || !t) return set_error(POX_ERR_INVALID, "ctx/tensor is NULL");
+    if (batch && (!x_dev || !y_dev)) return set_error(POX_ERR_INVALID, "x/y is NULL");
+    CK(cudaSetDevice(ctx->device), "cudaSetDevice");
+    cudaStream_t st = stream ? (cudaStream_t)stream : ctx->stream;
+    return gemv_launch(ctx, t, x_dev, batch, y_dev, st);
+}
+
+// Host x in, host y out, synchronous. Caller holds ctx->mu.
+static int gemv_host_locked(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x, size_t batch, float* y) {
+    if (t->rows == 0 || t->cols == 0 || batch == 0) return POX_OK;
+    const size_t xb = batch * t->cols * sizeof(float), yb = batch * t->rows * sizeof(float);
+    int rc = ensure_scratch(ctx, xb, yb);
+    if (rc) return rc;
+    CK(cudaMemcpyAsync(ctx->scratch_x, x, xb, cudaMemcpyHostToDevice, ctx->stream), "cudaMemcpy(x)");
+    rc = gemv_launch(ctx, t, (const float*)ctx->scratch_x, batch, (float*)ctx->scratch_y, ctx->stream);
+    if (rc) return rc;
+    CK(cudaMemcpyAsync(y, ctx->scratch_y, yb, cudaMemcpyDeviceToHost, ctx->stream), "cudaMemcpy(y)");
+    CK(cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+    return take_kernel_error(ctx);
+}
+
+extern "C" int pox_cuda_tensor_gemv_host(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x, size_t batch,
+                                         float* y) {
+    if (!ctx || !t) return set_error(POX_ERR_INVALID, "ctx/tensor is NULL");
+    if (batch && (!x || !y)) return set_error(POX_ERR_INVALID, "x/y is NULL");
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    CK(cudaSetDevice(ctx->device), "cudaSetDevice");
+    return gemv_host_locked(ctx, t, x, batch, y);
+}
+
+static pox_tensor* find_registered(pox_cuda_ctx* ctx, const pox_tensor_desc& d) {
+    for (pox_tensor* t : ctx->tensors)
+        if (t->dtype == d.dtype && t->h_data == d.data && t->h_data_len == d.data_len && t->h_scales == d.scales &&
+            t->h_scale_len == d.scale_len && t->rows == d.rows && t->cols == d.cols &&
+            (d.dtype != POX_I4 || (t->gs == d.group_size && t->h_outliers == d.outliers &&
+                                   t->h_outlier_len == d.outlier_len)))
+            return t;
+    return nullptr;
+}
+
+// Shared body of the reference-shaped host-slice entry points.
+static int host_slice_gemv(pox_cuda_ctx* ctx, const pox_tensor_desc& d, const float* x, size_t x_len, float* y,
+                           size_t y_len) {
+    if (!ctx) return set_error(POX_ERR_INVALID, "ctx is NULL");
+    if (d.rows == 0 || d.cols == 0) return POX_OK;  // metal_backend.rs:95-97
+    int rc = validate_desc(&d);
+    if (rc) return rc;
+    if (!x || !y) return set_error(POX_ERR_INVALID, "x/y is NULL");
+    if (x_len < d.cols || y_len < d.rows)
+        return set_error(POX_ERR_LAYOUT, "GEMV dimension mismatch (x %zu < cols %zu or y %zu < rows %zu)", x_len,
+                         d.cols, y_len, d.rows);
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    CK(cudaSetDevice(ctx->device), "cudaSetDevice");
+    pox_tensor* t = find_registered(ctx, d);
+    if (t) return gemv_host_locked(ctx, t, x, 1, y);
+    pox_tensor* tmp = nullptr;
+    rc = upload_tensor_locked(ctx, &d, &tmp, false);
+    if (rc) return rc;
+    rc = gemv_host_locked(ctx, tmp, x, 1, y);
+    cudaStreamSynchronize(ctx->stream);
+    free_tensor_mem(tmp);
+    delete tmp;
+    return rc;
+}
+
+extern "C" int pox_cuda_gemv_int4(pox_cuda_ctx* ctx, const uint8_t* packed_weights, size_t packed_len,
+                                  const uint8_t* scale_data, size_t scale_len, size_t rows, size_t cols,
+                                  size_t group_size, const float* x, size_t x_len, float* y, size_t y_len) {
+    pox_tensor_desc d = {};
+    d.dtype = POX_I4;
+    d.rows = rows;
+    d.cols = cols;
+    d.group_size = group_size;
+    d.data = packed_weights;
+    d.data_len = packed_len;
+    d.scales = scale_data;
+    d.scale_len = scale_len;
+    return host_slice_gemv(ctx, d, x, x_len, y, y_len);
+}
+
+extern "C" int pox_cuda_gemv_int4_outliers(pox_cuda_ctx* ctx, const uint8_t* packed_weights, size_t packed_len,
+                                           const uint8_t* scale_data, size_t scale_len, size_t group_size,
+                                           size_t rows, size_t cols, const uint8_t* outlier_data, size_t outlier_len,
+                                           const float* x, size_t x_len, float* y, size_t y_len) {
+    pox_tensor_desc d = {};
+    d.dtype = POX_I4;
+    d.rows = rows;
+    d.cols = cols;
+    d.group_size = group_size;
+    d.data = packed_weights;
+    d.data_len = packed_len;
+    d.scales = scale_data;
+    d.scale_len = scale_len;
+    d.outliers = outlier_data;
+    d.outlier_len = outlier_data ? outlier_len : 0;
+    return host_slice_gemv(ctx, d, x, x_len, y, y_len);
+}
+
+extern "C" int pox_cuda_gemv_int8(pox_cuda_ctx* ctx, const uint8_t* q_weights, size_t q_len,
+                                  const uint8_t* scale_data, size_t scale_len, size_t rows, size_t cols,
+                                  const float* x, size_t x_len, float* y, size_t y_len) {
+    pox_tensor_desc d = {};
+    d.dtype = POX_I8;
+    d.rows = rows;
+    d.cols = cols;
+    d.data = q_weights;
+    d.data_len = q_len;
+    d.scales = scale_data;
+    d.scale_len = scale_len;
+    if (rows && cols && (x_len < cols || y_len < rows || q_len < rows * cols))
+        return set_error(POX_ERR_LAYOUT, "GEMV INT8 dimension mismatch");
+    return host_slice_gemv(ctx, d, x, x_len, y, y_len);
+}
+
+// ------------------------------------------------------------------------------------------
+// dequantization (K0)
+// ------------------------------------------------------------------------------------------
+static int dequant_launch(const pox_tensor* t, float* out, cudaStream_t st) {
+    if (t->rows == 0 || t->cols == 0) return POX_OK;
+    const int N = (int)t->rows, K = (int)t->cols;
+    cudaError_t e;
+    if (t->dtype == POX_I4) {
+        e = launch_dequant_i4(t->tiled, t->w, t->scales_dev, out, N, K, t->groups, (int)t->gs, st);
+        if (e == cudaSuccess && t->nnz)
+            e = t->tiled ? launch_apply_outliers_items(t->item_ptr, t->entries, t->vals, out, N, K, st)
+                         : launch_apply_outliers(t->row_ptr, t->entries, t->vals, out, N, K, st);
+    } else if (t->dtype == POX_I8) {
+        e = launch_dequant_i8(t->tiled, t->w, t->i8_scale, out, N, K, st);
+    } else {
+        return set_error(POX_ERR_UNSUPPORTED, "dequantization of dtype %d", t->dtype);
+    }
+    if (e != cudaSuccess) return cuda_error(e, "dequant launch");
+    return POX_OK;
+}
+
+extern "C" int pox_cuda_tensor_dequant(pox_cuda_ctx* ctx, const pox_tensor* t, float* out_dev, void* stream) {
+    if (!ctx || !t || !out_dev) return set_error(POX_ERR_INVALID, "NULL argument");
+    CK(cudaSetDevice(ctx->device), "cudaSetDevice");
+    return dequant_launch(t, out_dev, stream ? (cudaStream_t)stream : ctx->stream);
+}
+
+extern "C" int pox_cuda_tensor_dequant_host(pox_cuda_ctx* ctx, const pox_tensor* t, float* out) {
+    if (!ctx || !t || !out) return set_error(POX_ERR_INVALID, "NULL argument");
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    CK(cudaSetDevice(ctx->device), "cudaSetDevice");
+    const size_t n = t->rows * t->cols;
+    if (n == 0) return POX_OK;
+    float* d = nullptr;
+    CK(cudaMalloc(&d, n * sizeof(float)), "cudaMalloc(dequant)");
+    int rc = dequant_launch(t, d, ctx->stream);
+    if (rc == POX_OK) {
+        cudaError_t e = cudaMemcpyAsync(out, d, n * sizeof(float), cudaMemcpyDeviceToHost, ctx->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+        if (e != cudaSuccess) rc = cuda_error(e, "dequant copy");
+        else rc = take_kernel_error(ctx);
+    }
+    cudaStreamSynchronize(ctx->stream);
+    cudaFree(d);
+    return rc;
+}

@@ -15,14 +15,13 @@ struct pox_tensor {
     int groups = 0;
     bool tiled = false;        // re-tiled device layout (tensor-core GEMV) vs raw .pox layout
     void* w = nullptr;         // tiles or raw payload
-    void* scales_dev = nullptr;
+    void* scales_dev = nullptr;   // tiled INT4: scale words per tile; raw INT4: the .pox scale bytes
     float i8_scale = 0.f;
-    uint32_t* row_ptr = nullptr;  // outlier CSR by row (raw layout): entries = (col, corr)
-    uint32_t* item_ptr = nullptr; // outlier CSR by streamed item (tiled): entries = (col<<4 | row%16, corr)
-    uint2* entries = nullptr;     // corr = f32 bits of v - dequant(q)
+    uint32_t* row_ptr = nullptr;  // outlier CSR by row [rows+1]
+    uint2* entries = nullptr;     // (col, f32 bits of v - dequant(q))
     uint16_t* vals = nullptr;     // f16 outlier values (dequantization path)
     size_t nnz = 0;
-    void* scratch = nullptr;      // split-K partials + row-tile counters of the streaming GEMV
+    void* scratch = nullptr;      // prepared x of the tiled GEMV (up to 8 batch rows)
     size_t scratch_bytes = 0;
     size_t bytes = 0;
     // host slices the tensor was uploaded from (registry key of the host-slice entry points)

@@ -7,15 +7,6 @@
 
 namespace pox {
 
-// Device layout constants of the re-tiled quantized weights.
-// One tile = 16 rows x one k-block, 1 KiB: the 32 lanes of a warp own 32 contiguous bytes each
-// (16 bytes of row g and 16 bytes of row g+8, g = lane/4), in the order the m16n8k16 A fragment
-// consumes them, so that a tile is read with two fully coalesced 512-byte warp loads.
-constexpr int kTileRows = 16;
-constexpr int kTileBytes = 1024;
-constexpr int kI4KBlock = 128;  // k per INT4 tile (4 bits x 16 rows x 128 = 1 KiB)
-constexpr int kI8KBlock = 64;   // k per INT8 tile (8 bits x 16 rows x 64 = 1 KiB)
-
 __device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t c) {
     // (a & b) | c
     uint32_t d;
@@ -72,7 +63,7 @@ __device__ __forceinline__ void i8x4_to_f16x4(uint32_t v, uint32_t& r0, uint32_t
 // D = A(16x16 f16, row) * B(16x8 f16, col) + C, f32 accumulate.
 __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
                                           uint32_t a3, uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%0,%1,%2,%3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -82,7 +73,7 @@ __device__ __forceinline__ void mma_16816(float (&d)[4], uint32_t a0, uint32_t a
 // D += A(16x32 u8, row) * B(32x8 s8, col), s32 accumulate (exact integer arithmetic).
 __device__ __forceinline__ void imma_16832_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                                 uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
         : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
@@ -91,7 +82,7 @@ __device__ __forceinline__ void imma_16832_u8s8(int (&d)[4], uint32_t a0, uint32
 // D += A(16x32 s8, row) * B(32x8 s8, col), s32 accumulate.
 __device__ __forceinline__ void imma_16832_s8s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                                 uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
         : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));

@@ -5,73 +5,219 @@
 // Metal gemv_int4_kernel (crates/paraoxidizer-runtime/src/metal_backend.rs:11-54) and the F16
 // projection of project_tensor (crates/paraoxidizer-runtime/src/engine.rs:235-250).
 //
-// Streaming design (HBM-bound at batch <= 8):
-//  * Weights are re-tiled at upload into 1 KiB tiles (16 rows x one k-block) ordered
-//    chunk-major, so the GEMV is one contiguous byte stream cut into items (one row tile x one
-//    chunk of 8 k-blocks = 8 KiB). A persistent grid of one CTA per SM takes a contiguous range
-//    of items.
-//  * One producer thread streams the range with cp.async.bulk (TMA bulk copies) into a 16-stage
-//    shared-memory ring, completion signalled on mbarriers; 8 consumer warps each own every 8th
-//    item (two ring slots per warp: double buffering).
-//  * Nibbles / int8 / f16 become exact f16 MMA A fragments in registers (exponent-bias trick);
-//    mma.sync m16n8k16 does the q*x products with f32 accumulation. x (f32) enters as two f16
-//    columns, hi = f16(x) and lo = f16(x - hi), so products keep ~22 bits of x.
-//  * INT4: per 128-k block the MMA gives S = sum q*x; the epilogue adds scale*S + min*sum(x),
-//    i.e. sum (min + q*scale) * x regrouped.
-//  * Split-K partial sums go to a per-tensor scratch buffer; the warp that finishes the last
-//    chunk of a row tile (atomic counter) sums the partials in chunk order (deterministic),
-//    applies the outlier CSR correction y += sum (v - dequant(q)) * x[c] and writes y.
-//  * Every mbarrier wait is bounded (clock64 budget): on expiry the kernel raises an error flag
-//    and returns instead of hanging.
-//  * Programmatic dependent launch: the producer starts streaming weights before the previous
-//    kernel in the stream has finished; consumers wait (griddepcontrol.wait) before reading x.
+// Design (HBM-bound at batch <= 8):
+//  * x preparation (xprep_kernel): per 128-k block, x becomes a 15-bit fixed-point value split
+//    into two exact int8 limbs (hi, lo) plus (block scale, block sum); F16 weights take x as an
+//    exact f16 hi/lo pair instead.
+//  * One CTA = one row tile (16 rows) x one k-split; its W warps stride over the tile's k-blocks
+//    (tile kb = k0 + warp, + W, ...), so a CTA streams a contiguous byte range. Each warp loads
+//    four 1 KiB tiles at a time with 128-bit non-allocating loads straight into registers; the
+//    lane's bytes are already MMA A fragments (see TileLayout).
+//  * INT4: mma.sync m16n8k32 u8 x s8 -> s32. Low nibbles (w & 0x0F0F0F0F) and high nibbles
+//    (w & 0xF0F0F0F0 = 16 q) go to two MMAs, so unpacking costs one LOP3 per 4 weights. The
+//    s32 results are exact; the per-group affine map is applied once per tile:
+//    sum_c (min + q*scale) x_c = scale * sum_c q x_c + min * sum_c x_c.
+//    INT8: m16n8k32 s8 x s8. F16: m16n8k16 f16 x f16 -> f32.
+//  * x of the CTA's k-range is staged in shared memory; the prepared meta likewise.
+//  * Outliers (values that replace the dequantized weight, kernels.rs:211-219) are a per-row
+//    CSR of (col, v - dequant(q)); each row's entries are loaded before the main loop and
+//    applied with x from shared memory after it, reduced in a fixed order.
+//  * Warps reduce through shared memory in warp order; k-splits of one row tile form a thread
+//    block cluster and reduce through distributed shared memory in rank order. Results are
+//    deterministic; there is no global scratch and no atomic.
+//  * Programmatic dependent launch: the first weight loads are issued before
+//    griddepcontrol.wait, overlapping the x preparation kernel.
 #include <algorithm>
+#include <map>
+#include <mutex>
+#include <tuple>
 
 #include "common.cuh"
 #include "gemv.cuh"
 
 namespace pox {
 
-template <int KIND>
-struct KindTraits;
-template <>
-struct KindTraits<kKindI4> {
-    static constexpr int KB = 128;
-};
-template <>
-struct KindTraits<kKindI8> {
-    static constexpr int KB = 64;
-};
-template <>
-struct KindTraits<kKindF16> {
-    static constexpr int KB = 32;
-};
-
-constexpr int kConsumerWarps = 8;
-constexpr int kStreamThreads = (kConsumerWarps + 1) * 32;
-constexpr int kItemBytes = kChunkTiles * kTileBytesL;  // 8 KiB
-constexpr int kItemScaleBytes = kChunkTiles * 64;      // 512 B (INT4)
-constexpr long long kWaitCycles = 4000000000LL;        // ~2 s at 2 GHz
-
 // ---- PTX wrappers -------------------------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
+__device__ __forceinline__ uint4 lds128(uint32_t a) {
+    uint4 r;
+    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(a));
+    return r;
+}
+__device__ __forceinline__ uint2 ldg64_nc(const void* p) {
+    uint2 r;
+    asm volatile("ld.global.nc.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
+    return r;
+}
+__device__ __forceinline__ uint4 ldg128_nc(const void* p) {
+    uint4 r;
+    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
+    return r;
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+__device__ __forceinline__ void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ float ld_dsmem_f32(const void* local, uint32_t rank) {
+    uint32_t remote;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
+    return v;
+}
+
+// ------------------------------------------------------------------------------------------
+// x preparation
+// ------------------------------------------------------------------------------------------
+size_t xprep_bytes(int kind, int K) {
+    const size_t Kp = (size_t)((K + kXBlock - 1) / kXBlock) * kXBlock;
+    const size_t cols = 2 * (size_t)kMaxBatch * Kp * (kind == kKindF16 ? 2 : 1);
+    const size_t meta = (size_t)kMaxBatch * (((Kp / kXBlock) + 1) & ~(size_t)1) * sizeof(float2);
+    return ((cols + 255) & ~(size_t)255) + meta;
+}
+
+XPrep xprep_view(void* scratch, int kind, int K) {
+    XPrep v;
+    v.Kp = ((K + kXBlock - 1) / kXBlock) * kXBlock;
+    v.nxb = v.Kp / kXBlock;
+    v.nxbs = (v.nxb + 1) & ~1;
+    const size_t cols = 2 * (size_t)kMaxBatch * v.Kp * (kind == kKindF16 ? 2 : 1);
+    v.cols = scratch;
+    v.meta = reinterpret_cast<float2*>((char*)scratch + ((cols + 255) & ~(size_t)255));
+    return v;
+}
+
+constexpr int kXLimbMax = 16383;  // |X| bound of the 15-bit quantization
+
+// One warp per (batch row, 128-k block); lane l covers k = 4l .. 4l+3 of the block.
+__global__ void __launch_bounds__(256) xprep_int_kernel(const float* __restrict__ x, int B, int K, uint8_t* cols,
+                                                        float2* meta, int Kp, int nxb, int nxbs) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int wid = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (wid >= B * nxb) return;
+    const int b = wid / nxb, blk = wid % nxb;
+    const int k = blk * kXBlock + lane * 4;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (k < K) v = *reinterpret_cast<const float4*>(x + (size_t)b * K + k);  // K % 4 == 0 on this path
+    float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float inv = m > 0.f ? (float)kXLimbMax / m : 0.f;
+    int X[4] = {__float2int_rn(v.x * inv), __float2int_rn(v.y * inv), __float2int_rn(v.z * inv),
+                __float2int_rn(v.w * inv)};
+    uint32_t hi = 0, lo = 0;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int q = max(-kXLimbMax, min(kXLimbMax, X[i]));
+        hi |= ((uint32_t)(q >> 7) & 0xFFu) << (8 * i);
+        lo |= ((uint32_t)q & 0x7Fu) << (8 * i);
+    }
+    *reinterpret_cast<uint32_t*>(cols + (size_t)(2 * b) * Kp + k) = hi;
+    *reinterpret_cast<uint32_t*>(cols + (size_t)(2 * b + 1) * Kp + k) = lo;
+    const float s = warp_sum((v.x + v.y) + (v.z + v.w));
+    if (lane == 0) meta[(size_t)b * nxbs + blk] = make_float2(m > 0.f ? m / (float)kXLimbMax : 0.f, s);
+}
+
+// One thread per 2 elements: hi = f16(x), lo = f16(x - hi).
+__global__ void __launch_bounds__(256) xprep_f16_kernel(const float* __restrict__ x, int B, int K, __half* cols,
+                                                        int Kp) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int per = Kp / 2;
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= B * per) return;
+    const int b = i / per, k = (i % per) * 2;
+    float2 v = make_float2(0.f, 0.f);
+    if (k < K) v = *reinterpret_cast<const float2*>(x + (size_t)b * K + k);  // K % 32 == 0 on this path
+    const __half h0 = __float2half_rn(v.x), h1 = __float2half_rn(v.y);
+    const __half l0 = __float2half_rn(v.x - __half2float(h0)), l1 = __float2half_rn(v.y - __half2float(h1));
+    *reinterpret_cast<__half2*>(cols + (size_t)(2 * b) * Kp + k) = __halves2half2(h0, h1);
+    *reinterpret_cast<__half2*>(cols + (size_t)(2 * b + 1) * Kp + k) = __halves2half2(l0, l1);
+}
+
+cudaError_t launch_xprep(int kind, const float* x, int B, int K, const XPrep& xp, bool pdl, cudaStream_t st) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    if (kind == kKindF16) {
+        const int n = B * (xp.Kp / 2);
+        cfg.gridDim = dim3((n + 255) / 256, 1, 1);
+        return cudaLaunchKernelEx(&cfg, xprep_f16_kernel, x, B, K, (__half*)xp.cols, xp.Kp);
+    }
+    const int warps = B * xp.nxb;
+    cfg.gridDim = dim3((warps + 7) / 8, 1, 1);
+    return cudaLaunchKernelEx(&cfg, xprep_int_kernel, x, B, K, (uint8_t*)xp.cols, xp.meta, xp.Kp, xp.nxb, xp.nxbs);
+}
+
+// ------------------------------------------------------------------------------------------
+// Tensor-core GEMV
+// ------------------------------------------------------------------------------------------
+// Shared-memory plan of a CTA (bytes):
+//   [weight rings: W warps x kStages x (tile + INT4 scale words)] [ring mbarriers, x / entry mbarriers]
+//   [x columns] [x meta] [warp partials] [outlier sums] [cluster partials] [outlier entries + row bounds]
+//   [32 zero bytes]
+// Staged x columns are padded so that 128-bit reads of neighbouring columns fall in different banks.
+constexpr int kStages = 3;     // weight tiles in flight per warp (one 1 KiB tile per stage)
+constexpr int kEntCap = 1024;  // outlier entries of a row tile staged in shared memory
+
+struct SmemPlan {
+    int kbr;                   // max k-blocks per CTA
+    int cstride;               // bytes per staged x column
+    int nxr;                   // x meta blocks per batch row (stride, even)
+    int ring, bars, xs, xm, red, ocorr, part, ent, zero, total;  // byte offsets; total = size
+};
+__host__ __device__ inline SmemPlan smem_plan(int kind, int B, int W, int S, int nkb, bool outl) {
+    SmemPlan p;
+    const int KB = kind_kblock(kind), XB = kind == kKindF16 ? 2 : 1;
+    const int tb = kTileBytes + (kind == kKindI4 ? 64 : 0);
+    p.kbr = (nkb + S - 1) / S;
+    const int xr = p.kbr * KB * XB;
+    p.cstride = ((xr + 127) & ~127) + (kind == kKindI4 ? 16 : 64);
+    p.nxr = ((p.kbr * KB + kXBlock - 1) / kXBlock + 2 + 1) & ~1;
+    int o = 0;
+    p.ring = o; o += W * kStages * tb;
+    p.bars = o; o += W * kStages * 8 + 16;
+    p.xs = o;   o += (2 * B * p.cstride + 15) & ~15;
+    p.xm = o;   o += kind == kKindF16 ? 0 : B * p.nxr * 8;
+    p.red = o;  o += W * 128 * 4;
+    p.ocorr = o; o += 128 * 4;
+    p.part = o; o += 128 * 4;
+    p.ent = o;  o += outl ? kEntCap * 8 + 32 * 4 : 0;
+    p.zero = o; o += 32;
+    p.total = o;
+    return p;
+}
+
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
 }
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
                  : "memory");
 }
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-// Bounded wait on the phase of the given parity. false = the budget ran out.
+constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 2 GHz: a bounded wait, never a hang
+// Bounded wait on the phase of the given parity; false = the budget ran out.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    if (ok) return true;
     const long long t0 = clock64();
     for (;;) {
-        uint32_t ok;
         asm volatile(
             "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n"
             " selp.u32 %0, 1, 0, p;\n}"
@@ -82,473 +228,477 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
         if (clock64() - t0 > kWaitCycles) return false;
     }
 }
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar,
-                                         uint64_t policy) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::
-            "r"(dst),
-        "l"(src), "r"(bytes), "r"(bar), "l"(policy)
-        : "memory");
+// TMA bulk copy (no multicast) global -> shared, completion counted on an mbarrier.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+                 "l"(src), "r"(bytes), "r"(bar)
+                 : "memory");
 }
-__device__ __forceinline__ uint64_t policy_evict_first() {
-    uint64_t p;
-    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
-    return p;
-}
-__device__ __forceinline__ uint4 lds128(uint32_t a) {
-    uint4 r;
-    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(a));
-    return r;
-}
-__device__ __forceinline__ uint32_t lds32(uint32_t a) {
-    uint32_t r;
-    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(r) : "r"(a));
-    return r;
-}
-__device__ __forceinline__ uint2 lds64a(uint32_t a) {
+__device__ __forceinline__ uint2 lds64(uint32_t a) {
     uint2 r;
     asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "r"(a));
     return r;
 }
-__device__ __forceinline__ void consumer_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32)); }
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
 
-constexpr int kGroupItems = 4;           // items per bulk copy (one ring group)
-constexpr int kEntryCapG = 256;          // outlier entries staged per ring group (2 KiB)
-constexpr int kXBlock = 128;             // k per x quantization block (integer path)
-constexpr int kXLimbMax = 16383;         // |X| bound of the 15-bit x quantization
+enum { kErrWaitRing = 1, kErrWaitX = 2, kErrWaitEnt = 4 };
 
-// Shared-memory plan of the streaming kernel (bytes). ring groups x kGroupItems blobs.
-struct StreamSmem {
-    size_t ring, ering, bars, meta, xs, xb, red, total;
-    int xstride;  // bytes per staged x column
-};
-__host__ __device__ inline StreamSmem stream_smem(int kind, int B, int groups, int span) {
-    StreamSmem s;
-    const int ck = kChunkTiles * kind_kblock(kind);
-    const size_t stride = (kind == kKindI4 ? kChunkTiles * 64 : 0) + (size_t)kChunkTiles * kTileBytesL;
-    s.ring = (size_t)groups * kGroupItems * stride;
-    s.ering = kind == kKindI4 ? (size_t)groups * kEntryCapG * 8 : 0;
-    s.bars = (size_t)2 * groups * 8;
-    s.meta = (size_t)groups * (kGroupItems + 1) * 8;
-    if (kind == kKindF16) {
-        s.xstride = (span * ck + 16) * 2;        // f16 hi / lo columns
-        s.xs = (size_t)2 * B * s.xstride;
-        s.xb = 0;
-    } else {
-        s.xstride = span * ck + 32;              // int8 hi / lo limb columns (permuted per 32 k)
-        s.xs = ((size_t)2 * B * s.xstride + 15) & ~(size_t)15;
-        s.xb = (size_t)2 * B * ((span * ck + kXBlock - 1) / kXBlock) * 4;  // per-block scale, sum(x)
-    }
-    s.red = (size_t)kConsumerWarps * 16 * kMaxBatch * 4;
-    s.total = s.ring + s.ering + s.bars + s.meta + s.xs + s.xb + s.red;
-    return s;
-}
-
-// Byte position of window offset kk inside a limb column: per 32 k, lane t's four k of each
-// half (k 4t..4t+3 and 16+4t..16+4t+3) are adjacent, so one LDS.64 yields both B registers.
-__device__ __forceinline__ int limb_pos(int kk) {
-    const int r = kk & 31;
-    return (kk & ~31) + 8 * ((r & 15) >> 2) + 4 * (r >> 4) + (r & 3);
-}
-
-// Reduction of one row tile by the warp that delivered its last chunk: partial sums of all
-// chunks in chunk order (deterministic), written to y.
-template <int KIND>
-__device__ void reduce_row_tile(const StreamArgs& a, const TileLayout& L, int T) {
-    const int lane = threadIdx.x & 31;
-    const int B = a.B;
-    for (int i = lane; i < 16 * B; i += 32) {
-        const int ri = i / B, b = i % B;
-        const int row = T * 16 + ri;
-        const float* p = a.partial + ((size_t)T * L.nchunks * 16 + ri) * kMaxBatch + b;
-        float s = 0.f;
-#pragma unroll 8
-        for (int c = 0; c < L.nchunks; c++) s += __ldcg(p + (size_t)c * 16 * kMaxBatch);
-        if (row < a.N) a.y[(size_t)b * a.N + row] = KIND == kKindI8 ? s * a.i8_scale : s;
-    }
-    if (lane == 0) a.counters[T] = 0u;  // self-cleaning for the next launch
-}
-
-template <int KIND, int NB>
-__global__ void __launch_bounds__(kStreamThreads, 1) gemv_stream_kernel(StreamArgs a) {
-    constexpr int KB = KindTraits<KIND>::KB;
-    constexpr int CK = kChunkTiles * KB;  // k per chunk
-    constexpr int SB = KIND == kKindI4 ? kChunkTiles * 64 : 0;  // scale bytes leading a blob
-    constexpr uint32_t STRIDE = SB + kChunkTiles * kTileBytesL;
+// BT: exact batch 1..4, or 8 for a runtime batch of 5..8 (two MMA column blocks).
+template <int KIND, int BT>
+__global__ void __launch_bounds__(512, 2) gemv_tc_kernel(const GemvArgs a) {
+    constexpr int KB = KIND == kKindI4 ? 128 : (KIND == kKindI8 ? 64 : 32);
+    constexpr int XB = KIND == kKindF16 ? 2 : 1;
+    constexpr int NB = BT > 4 ? 2 : 1;
+    constexpr int G = (KIND == kKindI4 && BT <= 2) ? 2 : 1;  // tiles whose results share one MMA accumulator
+    constexpr int SB = KIND == kKindI4 ? 64 : 0;
+    constexpr int TB = kTileBytes + SB;  // staged bytes per tile
     extern __shared__ __align__(128) unsigned char smem[];
 
-    const TileLayout L(KIND, a.N, a.K);
-    const int NG = a.ring;  // ring groups
-    const int B = a.B;
-    const StreamSmem sp = stream_smem(KIND, B, NG, a.span);
-    unsigned char* ring = smem;
-    uint2* ering = reinterpret_cast<uint2*>(smem + sp.ring);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + sp.ring + sp.ering);
-    uint2* meta = reinterpret_cast<uint2*>(smem + sp.ring + sp.ering + sp.bars);  // [NG][kGroupItems+1]
-    unsigned char* xs = smem + sp.ring + sp.ering + sp.bars + sp.meta;
-    float* xblk = reinterpret_cast<float*>(smem + sp.ring + sp.ering + sp.bars + sp.meta + sp.xs);
-    float* redall = reinterpret_cast<float*>(smem + sp.ring + sp.ering + sp.bars + sp.meta + sp.xs + sp.xb);
+    const int B = BT > 4 ? a.B : BT;
+    const int W = blockDim.x >> 5;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, t = lane & 3;
+    const int S = a.S, s = blockIdx.x, T = blockIdx.y;
+    const int nkb = a.nkb;
+    const int kb0 = (int)((long long)s * nkb / S), kb1 = (int)((long long)(s + 1) * nkb / S);
+    const int k0 = kb0 * KB, k1 = kb1 * KB;
+    const bool has_out = KIND == kKindI4 && a.row_ptr != nullptr;
+    const SmemPlan P = smem_plan(KIND, B, W, S, nkb, has_out);
+    const uint32_t sbase = smem_u32(smem);
+    const uint32_t ring = sbase + P.ring + warp * kStages * TB;
+    const uint32_t wbar = sbase + P.bars + warp * kStages * 8;
+    const uint32_t xbar = sbase + P.bars + W * kStages * 8, ebar = xbar + 8;
+    const uint32_t xs = sbase + P.xs, zero = sbase + P.zero;
+    const int cs = P.cstride;
+    const int xb0 = k0 / kXBlock, xb0a = xb0 & ~1;  // meta copies start on an even block (16 bytes)
+    const float2* xms = reinterpret_cast<const float2*>(smem + P.xm);
+    float* red = reinterpret_cast<float*>(smem + P.red);
+    float* ocorr = reinterpret_cast<float*>(smem + P.ocorr);
+    float* part = reinterpret_cast<float*>(smem + P.part);
+    const uint2* ent_s = reinterpret_cast<const uint2*>(smem + P.ent);
+    uint32_t* rp_s = reinterpret_cast<uint32_t*>(smem + P.ent + kEntCap * 8);
 
-    const int items = L.items();
-    const int G = gridDim.x;
-    const int i0 = (int)((long long)blockIdx.x * items / G);
-    const int i1 = (int)((long long)(blockIdx.x + 1) * items / G);
-    const int n = i1 - i0;
-    const int ngroups = (n + kGroupItems - 1) / kGroupItems;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + NG);
-    const bool outl = KIND == kKindI4 && a.item_ptr != nullptr;
+    // this warp's tiles: kb = kb0 + warp + i * W, i < nt
+    const int nt = kb0 + warp < kb1 ? (kb1 - kb0 - warp + W - 1) / W : 0;
+    const uint8_t* wsrc = a.w + ((size_t)T * nkb + kb0 + warp) * kTileBytes;
+    const uint32_t* ssrc = KIND == kKindI4 ? a.sc + ((size_t)T * nkb + kb0 + warp) * 16 : nullptr;
+    const size_t wstep = (size_t)W * kTileBytes;
 
+    if (lane == 0)
+        for (int i = 0; i < kStages; i++) mbar_init(wbar + 8 * i, 1);
     if (tid == 0) {
-        for (int s = 0; s < NG; s++) {
-            mbar_init(full0 + 8 * s, 2);  // blob copy + outlier-entry copy
-            mbar_init(empty0 + 8 * s, kGroupItems);
-        }
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        mbar_init(xbar, 1);
+        mbar_init(ebar, 1);
     }
+    if (tid < 8) reinterpret_cast<uint32_t*>(smem + P.zero)[tid] = 0u;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     __syncthreads();
     pdl_launch_dependents();
-    if (n <= 0) return;
 
-    if (warp == kConsumerWarps) {
-        // ---------------- producer warp: lane 0 issues the copies ----------------
-        const uint64_t pol = policy_evict_first();
-        auto issue_blobs = [&](int g) {
-            const int gs = g % NG;
-            const int m = min(kGroupItems, n - g * kGroupItems);
-            const uint32_t bytes = (uint32_t)m * STRIDE;
-            mbar_arrive_expect_tx(full0 + 8 * gs, bytes);
-            bulk_g2s(smem_u32(ring + (size_t)gs * kGroupItems * STRIDE),
-                     a.blobs + (size_t)(i0 + g * kGroupItems) * STRIDE, bytes, full0 + 8 * gs, pol);
-        };
-        // outlier offsets of items [i0, i1]: one warp-wide load per 32 items
-        uint32_t ipv = 0;
-        int ip_base = -1;
-        auto ip_at = [&](int li) -> uint32_t {  // warp-collective, li in [0, n]
-            const int base = li & ~31;
-            if (base != ip_base) {
-                ip_base = base;
-                ipv = base + lane <= n ? __ldg(a.item_ptr + i0 + base + lane) : 0u;
-            }
-            return __shfl_sync(0xffffffffu, ipv, li & 31);
-        };
-        auto issue_entries = [&](int g) {  // warp-collective
-            const int gs = g % NG;
-            const int m = min(kGroupItems, n - g * kGroupItems);
-            uint32_t e[kGroupItems + 1];
-#pragma unroll
-            for (int j = 0; j <= kGroupItems; j++) {
-                const int li = g * kGroupItems + (j < m ? j : m);
-                e[j] = outl ? ip_at(li) : 0u;
-            }
-            // li is clamped to the group's end, so e[j] == e[m] for j >= m
-            if (lane == 0) {
-                uint32_t bytes = 0, estart = e[0] & ~1u;
-                if (outl && e[kGroupItems] > e[0]) {
-                    uint32_t cnt = e[kGroupItems] - estart;
-                    if (cnt > (uint32_t)kEntryCapG) cnt = kEntryCapG;
-                    cnt = (cnt + 1) & ~1u;
-                    bytes = cnt * 8;
-                }
-                uint2* mg = meta + gs * (kGroupItems + 1);
-#pragma unroll
-                for (int j = 0; j < kGroupItems; j++) mg[j] = make_uint2(e[j], e[j + 1]);
-                mg[kGroupItems] = make_uint2(estart, estart + bytes / 8);
-                if (bytes) {
-                    mbar_arrive_expect_tx(full0 + 8 * gs, bytes);
-                    bulk_g2s(smem_u32(ering + (size_t)gs * kEntryCapG), a.entries + estart, bytes, full0 + 8 * gs,
-                             pol);
-                } else {
-                    mbar_arrive(full0 + 8 * gs);
-                }
-            }
-        };
-        int issued = 0;
-        bool abort = false;
-        const int first = min(NG, ngroups);
-        if (lane == 0)
-            for (int g = 0; g < first; g++) issue_blobs(g);  // weights first: no dependency
-        for (int g = 0; g < first; g++) issue_entries(g);
-        issued = first;
-        for (int g = first; g < ngroups && !abort; g++) {
-            int ok = 1;
-            if (lane == 0) {
-                if (!mbar_wait(empty0 + 8 * (g % NG), ((g / NG) - 1) & 1)) {
-                    atomicOr(a.err, kErrTimeoutEmpty);
-                    ok = 0;
-                } else {
-                    issue_blobs(g);
-                }
-            }
-            ok = __shfl_sync(0xffffffffu, ok, 0);
-            if (!ok) {
-                abort = true;
-                // the blob copy was not issued: complete the phase's entry arrival anyway so the
-                // bounded drain below never waits on a half-armed barrier
-                break;
-            }
-            issue_entries(g);
-            issued = g + 1;
+    // ---- weight ring: the first kStages tiles of this warp (immutable data: no dependency) ----
+    auto issue = [&](int i) {  // lane 0 only
+        const uint32_t st = ring + (i % kStages) * TB, bar = wbar + 8 * (i % kStages);
+        mbar_expect_tx(bar, TB);
+        bulk_g2s(st, wsrc + (size_t)i * wstep, kTileBytes, bar);
+        if (KIND == kKindI4) bulk_g2s(st + kTileBytes, ssrc + (size_t)i * W * 16, 64, bar);
+    };
+    if (lane == 0)
+        for (int i = 0; i < kStages && i < nt; i++) issue(i);
+
+    // ---- outlier CSR bounds of the row tile (rows 16T..16T+15 are one contiguous entry range) ----
+    uint32_t e_lo = 0, e_hi = 0, rpv = 0;
+    if (has_out) {
+        const int r0 = T * 16, r1 = min(T * 16 + 16, a.N);
+        if (tid == 0) {
+            e_lo = __ldg(a.row_ptr + r0);
+            e_hi = __ldg(a.row_ptr + r1);
         }
-        if (lane == 0) {
-            // never leave with copies in flight: wait (bounded) for the last use of every group
-            for (int g = issued - 1; g >= 0 && g >= issued - NG; g--) mbar_wait(full0 + 8 * (g % NG), (g / NG) & 1);
-        }
-        return;
+        if (tid <= 16) rpv = __ldg(a.row_ptr + min(r0 + tid, r1));
     }
 
-    // ---------------- consumers ----------------
-    const int g = lane >> 2, t = lane & 3;
-    const int c_first = i0 / L.nT, c_last = (i1 - 1) / L.nT;
-    const int kw0 = c_first * CK;
-    const int kw1 = min(a.K, (c_last + 1) * CK);
-    const int kw = kw1 - kw0;
-    pdl_wait();  // x (and the scratch of a previous launch) are visible from here on
-    const int nxb = (kw + kXBlock - 1) / kXBlock;           // x blocks in the window
-    const int xbs = (a.span * CK + kXBlock - 1) / kXBlock;  // x-block stride per limb column
-    if (KIND == kKindF16) {
-        for (int b = 0; b < B; b++) {
-            const float* xb = a.x + (size_t)b * a.K + kw0;
-            __half* hi = reinterpret_cast<__half*>(xs + (size_t)(2 * b) * sp.xstride);
-            __half* lo = reinterpret_cast<__half*>(xs + (size_t)(2 * b + 1) * sp.xstride);
-            for (int k = tid * 2; k < kw; k += kConsumerWarps * 64) {
-                const float2 v = *reinterpret_cast<const float2*>(xb + k);
-                const __half h0 = __float2half_rn(v.x), h1 = __float2half_rn(v.y);
-                const __half l0 = __float2half_rn(v.x - __half2float(h0));
-                const __half l1 = __float2half_rn(v.y - __half2float(h1));
-                *reinterpret_cast<__half2*>(hi + k) = __halves2half2(h0, h1);
-                *reinterpret_cast<__half2*>(lo + k) = __halves2half2(l0, l1);
-            }
-        }
-    } else {
-        // 15-bit quantization of x per 128-k block: X = rint(x * 16383 / max|x|) split into two
-        // exact int8 limbs (X = 128 hi + lo); the integer MMAs then compute sum q*X exactly.
-        for (int i = warp; i < B * nxb; i += kConsumerWarps) {
-            const int b = i / nxb, bl = i % nxb;
-            const int kk = bl * kXBlock + lane * 4;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (kk < kw) v = *reinterpret_cast<const float4*>(a.x + (size_t)b * a.K + kw0 + kk);
-            float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-            const float inv = m > 0.f ? (float)kXLimbMax / m : 0.f;
-            const float sc = m > 0.f ? m / (float)kXLimbMax : 0.f;
-            const int X0 = __float2int_rn(v.x * inv), X1 = __float2int_rn(v.y * inv);
-            const int X2 = __float2int_rn(v.z * inv), X3 = __float2int_rn(v.w * inv);
-            const uint32_t hi = ((uint32_t)(X0 >> 7) & 0xFFu) | (((uint32_t)(X1 >> 7) & 0xFFu) << 8) |
-                                (((uint32_t)(X2 >> 7) & 0xFFu) << 16) | (((uint32_t)(X3 >> 7) & 0xFFu) << 24);
-            const uint32_t lo = ((uint32_t)X0 & 0x7Fu) | (((uint32_t)X1 & 0x7Fu) << 8) | (((uint32_t)X2 & 0x7Fu) << 16) |
-                                (((uint32_t)X3 & 0x7Fu) << 24);
-            if (kk < kw) {
-                const int pos = limb_pos(kk);
-                *reinterpret_cast<uint32_t*>(xs + (size_t)(2 * b) * sp.xstride + pos) = hi;
-                *reinterpret_cast<uint32_t*>(xs + (size_t)(2 * b + 1) * sp.xstride + pos) = lo;
-            }
-            float sum = (v.x + v.y) + (v.z + v.w);
-            sum = warp_sum(sum);
-            if (lane == 0) {
-                xblk[(2 * b) * xbs + bl] = sc;
-                xblk[(2 * b + 1) * xbs + bl] = sum;
-            }
+    // ---- x of this CTA's k-range, its meta and the outlier entries: bulk copies ----
+    pdl_wait();
+    if (tid == 0) {
+        const unsigned char* xq = reinterpret_cast<const unsigned char*>(a.xq);
+        const uint32_t xbytes = (uint32_t)((k1 - k0) * XB);
+        const int nmeta = KIND == kKindF16 ? 0 : (((k1 + kXBlock - 1) / kXBlock - xb0a + 1) & ~1);
+        mbar_expect_tx(xbar, 2 * B * xbytes + (uint32_t)(B * nmeta * 8));
+        for (int c = 0; c < 2 * B; c++) bulk_g2s(xs + c * cs, xq + ((size_t)c * a.Kp + k0) * XB, xbytes, xbar);
+        for (int b = 0; b < B && nmeta > 0; b++)
+            bulk_g2s(sbase + P.xm + b * P.nxr * 8, a.xm + (size_t)b * a.nxbs + xb0a, nmeta * 8, xbar);
+        if (has_out) {
+            const uint32_t lo = e_lo & ~1u;
+            const uint32_t n = min((e_hi - lo + 1) & ~1u, (uint32_t)kEntCap);  // entries buffer has 2 pad slots
+            mbar_expect_tx(ebar, n * 8);
+            if (n) bulk_g2s(sbase + P.ent, a.ent + lo, n * 8, ebar);
         }
     }
-    consumer_bar();
+    bool ok = mbar_wait(xbar, 0);
+    ok = __all_sync(0xffffffffu, ok);
+    if (!ok && lane == 0) atomicOr(a.err, kErrWaitX);
 
-    float* red = redall + warp * 16 * kMaxBatch;
-    const uint32_t xs_base = smem_u32(xs);
-    const int ncols = 2 * B;
-    int done_items = 0;
-    for (int i = warp; i < n; i += kConsumerWarps) {
-        const int gi = i / kGroupItems, gs = gi % NG, j4 = i % kGroupItems;
-        if (!mbar_wait(full0 + 8 * gs, (gi / NG) & 1)) {
-            atomicOr(a.err, kErrTimeoutFull);
+    // ---- main loop: tiles from the ring, A fragments straight from the staged bytes ----
+    float acc[NB][2];
+    float fd[NB][4];
+#pragma unroll
+    for (int nb = 0; nb < NB; nb++) {
+        acc[nb][0] = acc[nb][1] = 0.f;
+        fd[nb][0] = fd[nb][1] = fd[nb][2] = fd[nb][3] = 0.f;
+    }
+    // column packing (INT4, batch 1-2): column 2*slot + limb, slot = u * BT + b for tile u of a group
+    const int slot_g = g >> 1, u_g = slot_g / (BT > 4 ? 4 : BT), b_g = slot_g % (BT > 4 ? 4 : BT);
+    const bool xg_valid = G == 2 ? (u_g < G) : (g < 2 * B);
+    const int col_g = G == 2 ? 2 * b_g + (g & 1) : g;
+    const int u_t = t / (BT > 4 ? 4 : BT), b_t = t % (BT > 4 ? 4 : BT);
+
+    int i = 0, fail_at = 0;
+    while (ok && i < nt) {
+        uint4 wa[G], wb[G];
+        uint2 scw = make_uint2(0u, 0u);
+        int kbu[G];
+#pragma unroll
+        for (int u = 0; u < G; u++) {
+            kbu[u] = kb0 + warp + (i + u) * W;
+            wa[u] = wb[u] = make_uint4(0u, 0u, 0u, 0u);
+            if (i + u < nt) {
+                const int st = (i + u) % kStages;
+                const bool w_ok = mbar_wait(wbar + 8 * st, ((i + u) / kStages) & 1);
+                if (!__all_sync(0xffffffffu, w_ok)) {
+                    ok = false;
+                    fail_at = i + u;
+                    break;
+                }
+                const uint32_t sa = ring + st * TB + lane * 16;
+                wa[u] = lds128(sa);
+                wb[u] = lds128(sa + 512);
+                if (KIND == kKindI4 && (G == 1 || u == u_t)) scw = lds64(ring + st * TB + kTileBytes + 8 * g);
+                __syncwarp();
+                if (lane == 0 && i + u + kStages < nt) {
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // reads done before the refill
+                    issue(i + u + kStages);
+                }
+            }
+        }
+        if (!ok) {
+            if (lane == 0) atomicOr(a.err, kErrWaitRing);
             break;
         }
-        const int item = i0 + i;
-        const int c = item / L.nT, T = item - c * L.nT;
-        const int kc = L.kch(c);
-        const uint32_t st = smem_u32(ring + ((size_t)gs * kGroupItems + j4) * STRIDE);
-        uint4 ta[kChunkTiles], tb[kChunkTiles];
-        uint32_t sg[kChunkTiles], sg8[kChunkTiles];
+        if (KIND == kKindI4) {
+            int dl[NB][4], dh[NB][4];
 #pragma unroll
-        for (int j = 0; j < kChunkTiles; j++) {
-            if (j < kc) {
-                ta[j] = lds128(st + SB + j * kTileBytesL + lane * 16);
-                tb[j] = lds128(st + SB + j * kTileBytesL + 512 + lane * 16);
-                if (KIND == kKindI4) {
-                    sg[j] = lds32(st + j * 64 + g * 4);
-                    sg8[j] = lds32(st + j * 64 + (g + 8) * 4);
+            for (int nb = 0; nb < NB; nb++)
+#pragma unroll
+                for (int q = 0; q < 4; q++) dl[nb][q] = dh[nb][q] = 0;
+#pragma unroll
+            for (int u = 0; u < G; u++) {
+                uint32_t X[NB][8];
+#pragma unroll
+                for (int nb = 0; nb < NB; nb++) {
+                    const bool v = G == 2 ? (xg_valid && u == u_g && i + u < nt) : (col_g + 8 * nb < 2 * B);
+                    const uint32_t xa = v ? xs + (col_g + 8 * nb) * cs + (uint32_t)(kbu[u] - kb0) * 128u + 32u * t
+                                          : zero;
+                    const uint4 v0 = lds128(xa), v1 = lds128(v ? xa + 16 : zero + 16);
+                    X[nb][0] = v0.x, X[nb][1] = v0.y, X[nb][2] = v0.z, X[nb][3] = v0.w;
+                    X[nb][4] = v1.x, X[nb][5] = v1.y, X[nb][6] = v1.z, X[nb][7] = v1.w;
                 }
-            }
-        }
-        // outlier entries of this item: staged in the group's entry buffer up to its end
-        uint32_t e0 = 0, e1 = 0, es = 0, ee = 0;
-        uint2 oen[2] = {make_uint2(0u, 0u), make_uint2(0u, 0u)};
-        if (outl) {
-            const uint2 mi = meta[gs * (kGroupItems + 1) + j4];
-            const uint2 mg = meta[gs * (kGroupItems + 1) + kGroupItems];
-            e0 = mi.x, e1 = mi.y, es = mg.x, ee = mg.y;
+                const uint32_t ra[4] = {wa[u].x, wa[u].y, wa[u].z, wa[u].w};
+                const uint32_t rb[4] = {wb[u].x, wb[u].y, wb[u].z, wb[u].w};
 #pragma unroll
-            for (int q = 0; q < 2; q++) {
-                const uint32_t e = e0 + lane + 32u * q;
-                if (e < e1 && e < ee) oen[q] = lds64a(smem_u32(ering + (size_t)gs * kEntryCapG + (e - es)));
-            }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(empty0 + 8 * gs);  // the group refills once its items are read
-
-        float acc[NB][2];
-#pragma unroll
-        for (int nb = 0; nb < NB; nb++) acc[nb][0] = acc[nb][1] = 0.f;
-        float dacc[NB][4];
-#pragma unroll
-        for (int nb = 0; nb < NB; nb++) dacc[nb][0] = dacc[nb][1] = dacc[nb][2] = dacc[nb][3] = 0.f;
-#pragma unroll
-        for (int j = 0; j < kChunkTiles; j++) {
-            if (j < kc) {
-                const int kb = c * kChunkTiles + j;
-                const int kk0 = kb * KB - kw0;  // window offset of this tile
-                const uint32_t ra[4] = {ta[j].x, ta[j].y, ta[j].z, ta[j].w};
-                const uint32_t rb[4] = {tb[j].x, tb[j].y, tb[j].z, tb[j].w};
-                if (KIND == kKindF16) {
-                    const uint32_t xk = xs_base + 2u * (uint32_t)(kk0 + 4 * t);
-#pragma unroll
-                    for (int jj = 0; jj < 2; jj++) {
-#pragma unroll
-                        for (int nb = 0; nb < NB; nb++) {
-                            const int col = g + 8 * nb;
-                            uint2 b0 = make_uint2(0u, 0u);
-                            if (col < ncols) b0 = lds64a(xk + (uint32_t)(col * sp.xstride) + 2u * 16u * jj);
-                            mma_16816(dacc[nb], ra[2 * jj], rb[2 * jj], ra[2 * jj + 1], rb[2 * jj + 1], b0.x, b0.y);
-                        }
-                    }
-                } else {
-                    int d[NB][4];
-#pragma unroll
-                    for (int nb = 0; nb < NB; nb++) d[nb][0] = d[nb][1] = d[nb][2] = d[nb][3] = 0;
-                    constexpr int MM = KIND == kKindI4 ? 4 : 2;  // k32 MMAs per tile
-#pragma unroll
-                    for (int m = 0; m < MM; m++) {
-                        uint32_t a0, a1, a2, a3;
-                        if (KIND == kKindI4) {
-                            a0 = ra[m] & 0x0F0F0F0Fu;
-                            a1 = rb[m] & 0x0F0F0F0Fu;
-                            a2 = (ra[m] >> 4) & 0x0F0F0F0Fu;
-                            a3 = (rb[m] >> 4) & 0x0F0F0F0Fu;
-                        } else {
-                            a0 = ra[2 * m];
-                            a1 = rb[2 * m];
-                            a2 = ra[2 * m + 1];
-                            a3 = rb[2 * m + 1];
-                        }
-                        const uint32_t xk = xs_base + (uint32_t)(kk0 + 32 * m + 8 * t);
-#pragma unroll
-                        for (int nb = 0; nb < NB; nb++) {
-                            const int col = g + 8 * nb;
-                            uint2 b0 = make_uint2(0u, 0u);
-                            if (col < ncols) b0 = lds64a(xk + (uint32_t)(col * sp.xstride));
-                            if (KIND == kKindI4) imma_16832_u8s8(d[nb], a0, a1, a2, a3, b0.x, b0.y);
-                            else imma_16832_s8s8(d[nb], a0, a1, a2, a3, b0.x, b0.y);
-                        }
-                    }
-                    const int bl = kk0 / kXBlock;
-                    float fg = 1.f, fm = 0.f, fg8 = 1.f, fm8 = 0.f;
-                    if (KIND == kKindI4) {
-                        const float2 s0 = __half22float2(*reinterpret_cast<const __half2*>(&sg[j]));
-                        const float2 s1 = __half22float2(*reinterpret_cast<const __half2*>(&sg8[j]));
-                        fg = s0.x, fm = s0.y, fg8 = s1.x, fm8 = s1.y;
-                    }
+                for (int j = 0; j < 2; j++) {
+                    const uint32_t a0 = ra[2 * j] & 0x0F0F0F0Fu, a1 = rb[2 * j] & 0x0F0F0F0Fu;
+                    const uint32_t a2 = ra[2 * j + 1] & 0x0F0F0F0Fu, a3 = rb[2 * j + 1] & 0x0F0F0F0Fu;
+                    const uint32_t h0 = ra[2 * j] & 0xF0F0F0F0u, h1 = rb[2 * j] & 0xF0F0F0F0u;
+                    const uint32_t h2 = ra[2 * j + 1] & 0xF0F0F0F0u, h3 = rb[2 * j + 1] & 0xF0F0F0F0u;
 #pragma unroll
                     for (int nb = 0; nb < NB; nb++) {
-                        const int b = t + 4 * nb;
-                        if (b < B) {
-                            const float sx = xblk[(2 * b) * xbs + bl];
-                            const float S0 = (float)(d[nb][0] * 128 + d[nb][1]) * sx;
-                            const float S1 = (float)(d[nb][2] * 128 + d[nb][3]) * sx;
-                            if (KIND == kKindI4) {
-                                const float sum = xblk[(2 * b + 1) * xbs + bl];
-                                acc[nb][0] = fmaf(fg, S0, fmaf(fm, sum, acc[nb][0]));
-                                acc[nb][1] = fmaf(fg8, S1, fmaf(fm8, sum, acc[nb][1]));
-                            } else {
-                                acc[nb][0] += S0;
-                                acc[nb][1] += S1;
-                            }
-                        }
+                        imma_16832_u8s8(dl[nb], a0, a1, a2, a3, X[nb][4 * j], X[nb][4 * j + 2]);
+                        imma_16832_u8s8(dh[nb], h0, h1, h2, h3, X[nb][4 * j + 1], X[nb][4 * j + 3]);
                     }
                 }
             }
-        }
-        if (KIND == kKindF16) {
+            // epilogue: lane t owns slot t (G == 2) or batch t (+4): tile u_t, batch b_t
+            const bool ev = G == 2 ? (u_t < G && i + u_t < nt) : true;
+            const int kbe = G == 2 ? (u_t == 0 ? kbu[0] : kbu[G - 1]) : kbu[0];
+            const float2 s0 = __half22float2(*reinterpret_cast<const __half2*>(&scw.x));
+            const float2 s1 = __half22float2(*reinterpret_cast<const __half2*>(&scw.y));
 #pragma unroll
             for (int nb = 0; nb < NB; nb++) {
-                acc[nb][0] = dacc[nb][0] + dacc[nb][1];
-                acc[nb][1] = dacc[nb][2] + dacc[nb][3];
-            }
-        }
-        // outlier correction of this item: sum (v - dequant(q)) * x[c], x from the limbs
-        if (outl && e1 > e0) {
-            for (int q = lane; q < 16 * kMaxBatch; q += 32) red[q] = 0.f;
-            __syncwarp();
-            for (uint32_t e = e0 + lane; e < e1; e += 32) {
-                const uint32_t r = e - e0;
-                uint2 en = r < 32u ? oen[0] : oen[1];
-                if (r >= 64u || e >= ee) en = __ldg(a.entries + e);
-                const int ri = (int)(en.x & 15u);
-                const int kx = (int)(en.x >> 4) - kw0;
-                const float corr = __uint_as_float(en.y);
-                const int pos = limb_pos(kx);
-                for (int b = 0; b < B; b++) {
-                    const int X = (int)(int8_t)xs[(size_t)(2 * b) * sp.xstride + pos] * 128 +
-                                  (int)(int8_t)xs[(size_t)(2 * b + 1) * sp.xstride + pos];
-                    const float xv = (float)X * xblk[(2 * b) * xbs + kx / kXBlock];
-                    atomicAdd(red + ri * kMaxBatch + b, corr * xv);
+                const int b = G == 2 ? b_t : t + 4 * nb;
+                if (ev && b < B) {
+                    const float2 m = xms[b * P.nxr + (kbe - xb0a)];
+                    const float sx = m.x * 0.0625f;  // S below is 16 * sum q X
+                    const int S0 = (dl[nb][0] * 16 + dh[nb][0]) * 128 + (dl[nb][1] * 16 + dh[nb][1]);
+                    const int S1 = (dl[nb][2] * 16 + dh[nb][2]) * 128 + (dl[nb][3] * 16 + dh[nb][3]);
+                    acc[nb][0] = fmaf(s0.x, (float)S0 * sx, fmaf(s0.y, m.y, acc[nb][0]));
+                    acc[nb][1] = fmaf(s1.x, (float)S1 * sx, fmaf(s1.y, m.y, acc[nb][1]));
                 }
             }
-            __syncwarp();
+        } else if (KIND == kKindI8) {
+            uint32_t X[NB][4];
+#pragma unroll
+            for (int nb = 0; nb < NB; nb++) {
+                const bool v = g + 8 * nb < 2 * B;
+                const uint4 v0 = lds128(v ? xs + (g + 8 * nb) * cs + (uint32_t)(kbu[0] - kb0) * 64u + 16u * t : zero);
+                X[nb][0] = v0.x, X[nb][1] = v0.y, X[nb][2] = v0.z, X[nb][3] = v0.w;
+            }
+            int d[NB][4];
+#pragma unroll
+            for (int nb = 0; nb < NB; nb++) d[nb][0] = d[nb][1] = d[nb][2] = d[nb][3] = 0;
+            const uint32_t ra[4] = {wa[0].x, wa[0].y, wa[0].z, wa[0].w};
+            const uint32_t rb[4] = {wb[0].x, wb[0].y, wb[0].z, wb[0].w};
+#pragma unroll
+            for (int m = 0; m < 2; m++)
+#pragma unroll
+                for (int nb = 0; nb < NB; nb++)
+                    imma_16832_s8s8(d[nb], ra[2 * m], rb[2 * m], ra[2 * m + 1], rb[2 * m + 1], X[nb][2 * m],
+                                    X[nb][2 * m + 1]);
+            const int xbl = (kbu[0] * 64) / kXBlock - xb0a;
 #pragma unroll
             for (int nb = 0; nb < NB; nb++) {
                 const int b = t + 4 * nb;
                 if (b < B) {
-                    acc[nb][0] += red[g * kMaxBatch + b];
-                    acc[nb][1] += red[(g + 8) * kMaxBatch + b];
+                    const float sx = xms[b * P.nxr + xbl].x;
+                    acc[nb][0] = fmaf((float)(d[nb][0] * 128 + d[nb][1]), sx, acc[nb][0]);
+                    acc[nb][1] = fmaf((float)(d[nb][2] * 128 + d[nb][3]), sx, acc[nb][1]);
                 }
             }
-            __syncwarp();
-        }
-        // partial sums of this (row tile, chunk): fire-and-forget stores
-        float* P = a.partial + ((size_t)T * L.nchunks + c) * 16 * kMaxBatch;
+        } else {
 #pragma unroll
-        for (int nb = 0; nb < NB; nb++) {
-            const int b = t + 4 * nb;
-            if (b < B) {
-                __stcg(P + g * kMaxBatch + b, acc[nb][0]);
-                __stcg(P + (g + 8) * kMaxBatch + b, acc[nb][1]);
+            for (int nb = 0; nb < NB; nb++) {
+                const bool v = g + 8 * nb < 2 * B;
+                const uint4 v0 =
+                    lds128(v ? xs + (g + 8 * nb) * cs + ((uint32_t)(kbu[0] - kb0) * 32u + 8u * t) * 2u : zero);
+                mma_16816(fd[nb], wa[0].x, wb[0].x, wa[0].y, wb[0].y, v0.x, v0.y);
+                mma_16816(fd[nb], wa[0].z, wb[0].z, wa[0].w, wb[0].w, v0.z, v0.w);
             }
         }
-        done_items++;
+        i += G;
+    }
+    if (!ok && lane == 0) {
+        // never leave with copies in flight into this warp's ring: bounded waits on what was issued
+        const int issued = min(nt, fail_at + kStages);
+        for (int j = fail_at; j < issued; j++) mbar_wait(wbar + 8 * (j % kStages), (j / kStages) & 1);
+    }
+    if (KIND == kKindF16) {
+#pragma unroll
+        for (int nb = 0; nb < NB; nb++) {
+            acc[nb][0] = fd[nb][0] + fd[nb][1];  // hi + lo column of batch row t + 4 nb
+            acc[nb][1] = fd[nb][2] + fd[nb][3];
+        }
+    }
+    if (G == 2) {
+        // BT == 1: lanes t = 0, 1 hold tiles 0, 1 of batch 0; BT == 2: lanes t, t ^ 2 hold batch t & 1
+        const int off = BT == 1 ? 1 : 2;
+        acc[0][0] += __shfl_xor_sync(0xffffffffu, acc[0][0], off);
+        acc[0][1] += __shfl_xor_sync(0xffffffffu, acc[0][1], off);
     }
 
-    // ---- publish this warp's partials; the last contributor of a row tile reduces it ----
-    __threadfence();
-    __syncwarp();
-    for (int j0 = 0; j0 < done_items; j0 += 32) {
-        const int j = j0 + lane;
-        bool last = false;
-        int T = 0;
-        if (j < done_items) {
-            const int item = i0 + warp + kConsumerWarps * j;
-            T = item % L.nT;
-            last = atomicAdd(a.counters + T, 1u) == (unsigned)L.nchunks - 1;
+    // ---- warp partials -> shared memory ----
+    float* rw = red + warp * 128;
+#pragma unroll
+    for (int nb = 0; nb < NB; nb++) {
+        const int b = G == 2 ? b_t : t + 4 * nb;
+        const bool own = G == 2 ? (t < BT) : true;
+        if (own && b < B) {
+            rw[g * 8 + b] = acc[nb][0];
+            rw[(g + 8) * 8 + b] = acc[nb][1];
         }
-        unsigned m = __ballot_sync(0xffffffffu, last);
-        if (m) __threadfence();
-        while (m) {
-            const int src = __ffs(m) - 1;
-            m &= m - 1;
-            reduce_row_tile<KIND>(a, L, __shfl_sync(0xffffffffu, T, src));
+    }
+    if (has_out && tid <= 16) rp_s[tid] = rpv;
+    __syncthreads();
+
+    // ---- outlier correction: sum over the row's entries of (v - dequant(q)) * x[col] ----
+    if (has_out) {
+        const bool eok = __all_sync(0xffffffffu, mbar_wait(ebar, 0));  // always: no copy left in flight
+        if (!eok && lane == 0) atomicOr(a.err, kErrWaitEnt);
+        const int tpr = 2 * W;  // threads per row: aligned lane groups of 8, 16 or 32
+        const int ri = tid / tpr, sub = tid % tpr;
+        const uint32_t lo = rp_s[0] & ~1u;  // the entry copy starts on an even index (16 bytes)
+        const uint32_t rb = rp_s[ri] - lo, re = rp_s[ri + 1] - lo;
+        float o[NB * 4];
+#pragma unroll
+        for (int b = 0; b < NB * 4; b++) o[b] = 0.f;
+        if (ok && eok) {
+            for (uint32_t e = rb + sub; e < re; e += tpr) {
+                const uint2 en = e < (uint32_t)kEntCap ? ent_s[e] : __ldg(a.ent + lo + e);
+                const int col = (int)en.x;
+                if (col >= k0 && col < k1) {
+                    const int kk = col - k0;
+                    const int xbl = col / kXBlock - xb0a;
+                    const float corr = __uint_as_float(en.y);
+#pragma unroll
+                    for (int b = 0; b < NB * 4; b++) {
+                        if (b < B) {
+                            const int X = (int)(int8_t)smem[P.xs + (2 * b) * cs + kk] * 128 +
+                                          (int)(int8_t)smem[P.xs + (2 * b + 1) * cs + kk];
+                            o[b] = fmaf(corr, (float)X * xms[b * P.nxr + xbl].x, o[b]);
+                        }
+                    }
+                }
+            }
         }
+#pragma unroll
+        for (int b = 0; b < NB * 4; b++) {
+            if (b < B) {
+                for (int off = tpr >> 1; off > 0; off >>= 1) o[b] += __shfl_xor_sync(0xffffffffu, o[b], off);
+                if (sub == 0) ocorr[ri * 8 + b] = o[b];
+            }
+        }
+        __syncthreads();
+    }
+
+    // ---- reduction: warps in order, then k-splits (cluster ranks) in order ----
+    const int rr = tid >> 3, bb = tid & 7;
+    float p = 0.f;
+    if (tid < 128 && bb < B) {
+        for (int w = 0; w < W; w++) p += red[w * 128 + tid];
+        if (has_out) p += ocorr[tid];
+    }
+    const float oscale = KIND == kKindI8 ? a.i8_scale : 1.f;
+    const int row = T * 16 + rr;
+    if (S == 1) {
+        if (tid < 128 && bb < B && row < a.N) a.y[(size_t)bb * a.N + row] = p * oscale;
+    } else {
+        if (tid < 128) part[tid] = p;
+        cluster_sync_all();
+        if (s == 0 && tid < 128 && bb < B) {
+            for (int r = 1; r < S; r++) p += ld_dsmem_f32(part + tid, (uint32_t)r);
+            if (row < a.N) a.y[(size_t)bb * a.N + row] = p * oscale;
+        }
+        cluster_sync_all();  // remote shared memory stays valid until rank 0 has read it
+    }
+}
+
+// ---- host-side planning ----
+static int num_sms() {
+    int dev = 0, n = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n > 0 ? n : 148;
+}
+
+template <int KIND, int BT>
+static cudaError_t prepare_kernel(int dev) {
+    static std::mutex mu;
+    static unsigned done_mask = 0;  // devices whose attribute is set (device ids < 32)
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev < 32 && ((done_mask >> dev) & 1u)) return cudaSuccess;
+    cudaError_t e = cudaFuncSetAttribute(gemv_tc_kernel<KIND, BT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         227 * 1024);
+    if (e == cudaSuccess && dev < 32) done_mask |= 1u << dev;
+    return e;
+}
+
+template <int KIND, int BT>
+static int occupancy(int W, int smem) {
+    static std::mutex mu;
+    static std::map<std::tuple<int, int, int>, int> cache;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(mu);
+    auto key = std::make_tuple(dev, W, smem);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, gemv_tc_kernel<KIND, BT>, W * 32, smem) != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+    }
+    cache[key] = n;
+    return n;
+}
+
+struct GemvPlan {
+    int W = 0, S = 0, smem = 0;
+};
+
+// Chooses warps per CTA (W) and k-splits per row tile (S, a thread block cluster): all CTAs
+// resident in one wave if possible, enough warps in flight, few splits, several tiles per warp.
+template <int KIND, int BT>
+static GemvPlan plan_gemv(int nT, int nkb, int B, bool outl) {
+    const int sms = num_sms();
+    GemvPlan best;
+    double best_score = -1.0;
+    for (int S : {1, 2, 4, 8}) {
+        if (S > nkb) break;
+        const int kbr = (nkb + S - 1) / S;
+        for (int W : {16, 8, 4}) {
+            if (W > kbr && W != 4) continue;  // keep every warp busy (the smallest CTA excepted)
+            const SmemPlan sp = smem_plan(KIND, B, W, S, nkb, outl);
+            if (sp.total > 227 * 1024) continue;
+            const int occ = occupancy<KIND, BT>(W, sp.total);
+            if (occ <= 0) continue;
+            const long long ctas = (long long)nT * S, slots = (long long)occ * sms;
+            const long long waves = (ctas + slots - 1) / slots;
+            const double eff_w = waves == 1 ? 1.0 : (double)ctas / (double)(waves * slots);
+            const double active = (double)std::min(ctas, slots) * W;
+            const double eff_p = std::min(1.0, active / 2500.0);
+            const double tpw = (double)kbr / W;
+            const double eff_o = tpw / (tpw + 1.0);
+            double pen = 1.0;
+            for (int q = S; q > 1; q >>= 1) pen *= 0.97;
+            const double score = eff_w * eff_p * eff_o * pen;
+            if (score > best_score) {
+                best_score = score;
+                best.W = W;
+                best.S = S;
+                best.smem = sp.total;
+            }
+        }
+    }
+    return best;
+}
+
+template <int KIND, int BT>
+static cudaError_t launch_tc_t(const GemvArgs& in, bool pdl, cudaStream_t st) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaError_t e = prepare_kernel<KIND, BT>(dev);
+    if (e != cudaSuccess) return e;
+    if (in.nT > 65535) return cudaErrorInvalidConfiguration;
+    const GemvPlan pl = plan_gemv<KIND, BT>(in.nT, in.nkb, in.B, KIND == kKindI4 && in.row_ptr != nullptr);
+    if (pl.W == 0) return cudaErrorInvalidConfiguration;
+    GemvArgs a = in;
+    a.S = pl.S;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(pl.S, in.nT, 1);
+    cfg.blockDim = dim3(pl.W * 32, 1, 1);
+    cfg.dynamicSmemBytes = pl.smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    if (pdl) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        na++;
+    }
+    if (pl.S > 1) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = pl.S;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = 1;
+        na++;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = na;
+    return cudaLaunchKernelEx(&cfg, gemv_tc_kernel<KIND, BT>, a);
+}
+
+template <int KIND>
+static cudaError_t launch_tc_kind(const GemvArgs& a, bool pdl, cudaStream_t st) {
+    switch (a.B) {
+        case 1: return launch_tc_t<KIND, 1>(a, pdl, st);
+        case 2: return launch_tc_t<KIND, 2>(a, pdl, st);
+        case 3: return launch_tc_t<KIND, 3>(a, pdl, st);
+        case 4: return launch_tc_t<KIND, 4>(a, pdl, st);
+        default: return launch_tc_t<KIND, 8>(a, pdl, st);
+    }
+}
+
+cudaError_t launch_gemv_tc(int kind, const GemvArgs& a, bool pdl, cudaStream_t st) {
+    if (a.B < 1 || a.B > kMaxBatch) return cudaErrorInvalidValue;
+    switch (kind) {
+        case kKindI4: return launch_tc_kind<kKindI4>(a, pdl, st);
+        case kKindI8: return launch_tc_kind<kKindI8>(a, pdl, st);
+        default: return launch_tc_kind<kKindF16>(a, pdl, st);
     }
 }
 
@@ -618,86 +768,84 @@ __global__ void gemv_f16_generic_kernel(GemvGenericArgs a) {
     }
 }
 
+cudaError_t launch_gemv_generic(int kind, const GemvGenericArgs& a, cudaStream_t st) {
+    const int warps = 8;
+    dim3 grid((a.N + warps - 1) / warps);
+    if (kind == kKindI4) gemv_i4_generic_kernel<<<grid, warps * 32, 0, st>>>(a);
+    else if (kind == kKindI8) gemv_i8_generic_kernel<<<grid, warps * 32, 0, st>>>(a);
+    else gemv_f16_generic_kernel<<<grid, warps * 32, 0, st>>>(a);
+    return cudaGetLastError();
+}
+
 // ------------------------------------------------------------------------------------------
-// Upload-time re-tiling into item blobs (one thread per output 32-bit word). Word o of the
-// (T, kb)-ordered tile sequence: o = ((T * nkb + kb) * 2 + s) * 128 + lane * 4 + w
-// (s = row half g / g+8, w = word of the lane's 16 bytes).
+// Upload-time re-tiling. Output word o of the tile sequence decomposes as
+// o = ((T * nkb + kb) * 2 + s) * 128 + lane * 4 + w, i.e. the byte layout of TileLayout.
 // ------------------------------------------------------------------------------------------
 template <int KIND>
-__global__ void repack_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ blobs, TileLayout L,
+__global__ void repack_kernel(const uint8_t* __restrict__ src, uint32_t* __restrict__ out, TileLayout L,
                               size_t total) {
     for (size_t o = blockIdx.x * (size_t)blockDim.x + threadIdx.x; o < total; o += (size_t)gridDim.x * blockDim.x) {
         const int w = (int)(o & 3), lane = (int)((o >> 2) & 31), s = (int)((o >> 7) & 1);
-        const size_t tl = o >> 8;
-        const int T = (int)(tl / L.nkb), kb = (int)(tl % L.nkb);
+        const size_t tile = o >> 8;
+        const int T = (int)(tile / L.nkb), kb = (int)(tile % L.nkb);
         const int g = lane >> 2, t = lane & 3;
         const size_t row = (size_t)T * 16 + g + 8 * s;
         uint32_t word = 0;
         if (row < (size_t)L.N) {
             if (KIND == kKindI4) {
-                const size_t row_bytes = (size_t)(L.K + 1) / 2;
+                // 8 nibbles k0..k0+7 (k0 = 128 kb + 32 t + 8 w): .pox byte j holds k 2j (low), 2j+1
+                // (high); the tile byte i holds k0+i (low) and k0+4+i (high)
+                const uint32_t v =
+                    *reinterpret_cast<const uint32_t*>(src + row * (size_t)(L.K / 2) + (size_t)kb * 64 + 16 * t + 4 * w);
 #pragma unroll
-                for (int p = 0; p < 8; p++) {
-                    // word w feeds the k32 MMA w: even nibbles are k 4t..4t+3 (A registers 0/1),
-                    // odd nibbles k 16+4t..16+4t+3 (A registers 2/3); (v & 0x0F0F0F0F) and
-                    // (v >> 4 & 0x0F0F0F0F) are then the u8 fragments
-                    const int k = kb * 128 + 32 * w + ((p & 1) ? 16 : 0) + 4 * t + (p >> 1);
-                    const uint8_t byte = src[row * row_bytes + (k >> 1)];
-                    const uint32_t nib = (k & 1) ? (byte >> 4) : (byte & 15u);
-                    word |= nib << (4 * p);
-                }
+                for (int i = 0; i < 4; i++)
+                    word |= (((v >> (4 * i)) & 15u) | (((v >> (4 * (i + 4))) & 15u) << 4)) << (8 * i);
             } else if (KIND == kKindI8) {
-                // word 2m: k 32m+4t..+3, word 2m+1: k 32m+16+4t..+3 (s8 fragments of the k32 MMA m)
-                const int k = kb * 64 + 16 * w + 4 * t;
-                word = *reinterpret_cast<const uint32_t*>(src + row * L.K + k);
+                word = *reinterpret_cast<const uint32_t*>(src + row * (size_t)L.K + (size_t)kb * 64 + 16 * t + 4 * w);
             } else {
-                const int k = kb * 32 + 16 * (w >> 1) + 4 * t + 2 * (w & 1);
-                word = *reinterpret_cast<const uint32_t*>(src + (row * L.K + k) * 2);
+                word = *reinterpret_cast<const uint32_t*>(src + (row * (size_t)L.K + (size_t)kb * 32 + 8 * t + 2 * w) * 2);
             }
         }
-        *reinterpret_cast<uint32_t*>(blobs + L.tile_off(T, kb) + s * 512 + lane * 16 + w * 4) = word;
+        out[o] = word;
     }
 }
 
-// INT4 scales into the blobs: per tile 16 rows of (f16 scale | f16 min << 16); a group spanning
-// several 128-k blocks is repeated in each.
-__global__ void repack_i4_scales_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ blobs, TileLayout L,
+// INT4 scale words: [(T * nkb + kb) * 16 + 2 g + s] = (f16 scale | f16 min << 16) of row
+// 16 T + g + 8 s and the group holding k-block kb.
+__global__ void repack_i4_scales_kernel(const uint8_t* __restrict__ src, uint32_t* __restrict__ sc, TileLayout L,
                                         int groups, int gs, size_t total) {
     for (size_t o = blockIdx.x * (size_t)blockDim.x + threadIdx.x; o < total; o += (size_t)gridDim.x * blockDim.x) {
-        const int ri = (int)(o & 15);
-        const size_t tl = o >> 4;
-        const int T = (int)(tl / L.nkb), kb = (int)(tl % L.nkb);
-        const size_t row = (size_t)T * 16 + ri;
+        const int j = (int)(o & 15);
+        const size_t tile = o >> 4;
+        const int T = (int)(tile / L.nkb), kb = (int)(tile % L.nkb);
+        const size_t row = (size_t)T * 16 + (j >> 1) + 8 * (j & 1);
         uint32_t v = 0;
         if (row < (size_t)L.N) {
             const int grp = kb * 128 / gs;
-            const uint8_t* p = src + (row * groups + grp) * 4;
-            v = (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+            v = *reinterpret_cast<const uint32_t*>(src + (row * groups + grp) * 4);
         }
-        *reinterpret_cast<uint32_t*>(blobs + L.scale_off(T, kb) + ri * 4) = v;
+        sc[o] = v;
     }
 }
 
 // ------------------------------------------------------------------------------------------
-// Dequantization (verification path): bit-exact with the reference.
+// Dequantization (verification path): bit-exact with the reference (mul, then add).
 // ------------------------------------------------------------------------------------------
-__global__ void dequant_i4_tiled_kernel(const uint8_t* __restrict__ blobs, float* __restrict__ out, TileLayout L) {
+__global__ void dequant_i4_tiled_kernel(const uint8_t* __restrict__ tiles, const uint32_t* __restrict__ sc,
+                                        float* __restrict__ out, TileLayout L) {
     const size_t total = (size_t)L.N * L.K;
     for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total;
          idx += (size_t)gridDim.x * blockDim.x) {
         const size_t row = idx / L.K;
         const int k = (int)(idx % L.K);
-        const int T = (int)(row / 16);
-        const int ri = (int)(row % 16), g = ri & 7, s = ri >> 3;
-        const int kb = k / 128, kin = k % 128;
-        const int w = kin / 32, r = kin % 32, half = r >> 4, t = (r & 15) >> 2, i = r & 3;
-        const int lane = g * 4 + t;
-        const int p = 2 * i + half;
-        const uint32_t word = *reinterpret_cast<const uint32_t*>(blobs + L.tile_off(T, kb) + s * 512 + lane * 16 + w * 4);
-        const uint32_t q = (word >> (4 * p)) & 15u;
-        const uint32_t sm = *reinterpret_cast<const uint32_t*>(blobs + L.scale_off(T, kb) + ri * 4);
-        const float sc = half_bits_to_float(sm), mn = half_bits_to_float(sm >> 16);
-        out[idx] = __fadd_rn(mn, __fmul_rn((float)q, sc));
+        const int T = (int)(row / 16), ri = (int)(row % 16), g = ri & 7, s = ri >> 3;
+        const int kb = k / 128, kin = k % 128, t = kin / 32, rem = kin % 32, w = rem / 8, p = rem % 8;
+        const size_t tile = (size_t)T * L.nkb + kb;
+        const uint8_t byte = tiles[tile * kTileBytes + s * 512 + (4 * g + t) * 16 + 4 * w + (p & 3)];
+        const uint32_t q = (p < 4) ? (byte & 15u) : (byte >> 4);
+        const uint32_t sm = sc[tile * 16 + 2 * g + s];
+        const float scl = half_bits_to_float(sm), mn = half_bits_to_float(sm >> 16);
+        out[idx] = __fadd_rn(mn, __fmul_rn((float)q, scl));
     }
 }
 
@@ -719,20 +867,17 @@ __global__ void dequant_i4_raw_kernel(const uint8_t* __restrict__ raw, const uin
     }
 }
 
-__global__ void dequant_i8_tiled_kernel(const uint8_t* __restrict__ blobs, float scale, float* __restrict__ out,
+__global__ void dequant_i8_tiled_kernel(const uint8_t* __restrict__ tiles, float scale, float* __restrict__ out,
                                         TileLayout L) {
     const size_t total = (size_t)L.N * L.K;
     for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total;
          idx += (size_t)gridDim.x * blockDim.x) {
         const size_t row = idx / L.K;
         const int k = (int)(idx % L.K);
-        const int T = (int)(row / 16);
-        const int ri = (int)(row % 16), g = ri & 7, s = ri >> 3;
-        const int kb = k / 64, kin = k % 64;
-        const int w = kin / 16, rem = kin % 16, t = rem / 4, kk = rem % 4;
-        const int lane = g * 4 + t;
-        const uint32_t word = *reinterpret_cast<const uint32_t*>(blobs + L.tile_off(T, kb) + s * 512 + lane * 16 + w * 4);
-        const int8_t q = (int8_t)((word >> (8 * kk)) & 0xFFu);
+        const int T = (int)(row / 16), ri = (int)(row % 16), g = ri & 7, s = ri >> 3;
+        const int kb = k / 64, kin = k % 64, t = kin / 16, j = kin % 16;
+        const size_t tile = (size_t)T * L.nkb + kb;
+        const int8_t q = (int8_t)tiles[tile * kTileBytes + s * 512 + (4 * g + t) * 16 + j];
         out[idx] = __fmul_rn((float)q, scale);
     }
 }
@@ -752,101 +897,9 @@ __global__ void apply_outliers_kernel(const uint32_t* __restrict__ row_ptr, cons
     }
 }
 
-__global__ void apply_outliers_items_kernel(const uint32_t* __restrict__ item_ptr, const uint2* __restrict__ entries,
-                                            const uint16_t* __restrict__ vals, float* __restrict__ out, int nT,
-                                            int items, int K) {
-    for (int item = blockIdx.x * blockDim.y + threadIdx.y; item < items; item += gridDim.x * blockDim.y) {
-        const int T = item % nT;
-        for (uint32_t e = item_ptr[item] + threadIdx.x; e < item_ptr[item + 1]; e += blockDim.x) {
-            const uint2 en = entries[e];
-            const size_t row = (size_t)T * 16 + (en.x & 15u);
-            out[row * K + (en.x >> 4)] = half_bits_to_float(vals[e]);
-        }
-    }
-}
-
 // ------------------------------------------------------------------------------------------
 // Host-side launchers
 // ------------------------------------------------------------------------------------------
-static int num_sms() {
-    int dev = 0, n = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    return n > 0 ? n : 148;
-}
-
-size_t stream_scratch_bytes(int kind, int N, int K) {
-    const TileLayout L(kind, N, K);
-    return (size_t)L.nT * L.nchunks * 16 * kMaxBatch * 4 + (size_t)L.nT * 4;
-}
-
-template <int KIND, int NB>
-static cudaError_t launch_stream_t(const StreamArgs& a, int grid, size_t smem, bool pdl, cudaStream_t st) {
-    auto kern = gemv_stream_kernel<KIND, NB>;
-    static int attr_dev = -1;  // the attribute is per device: set once per device in use
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (attr_dev != dev) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-        if (e != cudaSuccess) return e;
-        attr_dev = dev;
-    }
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid, 1, 1);
-    cfg.blockDim = dim3(kStreamThreads, 1, 1);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, kern, a);
-}
-
-cudaError_t launch_gemv_stream(int kind, const StreamArgs& in, bool pdl, cudaStream_t st) {
-    StreamArgs a = in;
-    if (a.B < 1 || a.B > kMaxBatch) return cudaErrorInvalidValue;
-    const TileLayout L(kind, a.N, a.K);
-    const int items = L.items();
-    const int grid = items < num_sms() ? items : num_sms();
-    // widest x window any CTA stages (chunks)
-    int span = 1;
-    for (int c = 0; c < grid; c++) {
-        const int i0 = (int)((long long)c * items / grid), i1 = (int)((long long)(c + 1) * items / grid);
-        if (i1 > i0) span = std::max(span, (i1 - 1) / L.nT - i0 / L.nT + 1);
-    }
-    a.span = span;
-    a.ring = 4;  // ring groups of kGroupItems items
-    StreamSmem sp = stream_smem(kind, a.B, a.ring, span);
-    while (sp.total > 227 * 1024 && a.ring > 2) {
-        a.ring -= 1;
-        sp = stream_smem(kind, a.B, a.ring, span);
-    }
-    if (sp.total > 227 * 1024) return cudaErrorInvalidConfiguration;
-    const bool two = a.B > 4;
-    switch (kind) {
-        case kKindI4:
-            return two ? launch_stream_t<kKindI4, 2>(a, grid, sp.total, pdl, st)
-                       : launch_stream_t<kKindI4, 1>(a, grid, sp.total, pdl, st);
-        case kKindI8:
-            return two ? launch_stream_t<kKindI8, 2>(a, grid, sp.total, pdl, st)
-                       : launch_stream_t<kKindI8, 1>(a, grid, sp.total, pdl, st);
-        default:
-            return two ? launch_stream_t<kKindF16, 2>(a, grid, sp.total, pdl, st)
-                       : launch_stream_t<kKindF16, 1>(a, grid, sp.total, pdl, st);
-    }
-}
-
-cudaError_t launch_gemv_generic(int kind, const GemvGenericArgs& a, cudaStream_t st) {
-    const int warps = 8;
-    dim3 grid((a.N + warps - 1) / warps);
-    if (kind == kKindI4) gemv_i4_generic_kernel<<<grid, warps * 32, 0, st>>>(a);
-    else if (kind == kKindI8) gemv_i8_generic_kernel<<<grid, warps * 32, 0, st>>>(a);
-    else gemv_f16_generic_kernel<<<grid, warps * 32, 0, st>>>(a);
-    return cudaGetLastError();
-}
-
 static dim3 grid_for(size_t total) {
     size_t blocks = (total + 255) / 256;
     const size_t cap = (size_t)num_sms() * 32;
@@ -855,31 +908,33 @@ static dim3 grid_for(size_t total) {
     return dim3((unsigned)blocks);
 }
 
-cudaError_t launch_repack(int kind, const uint8_t* src, uint8_t* blobs, int N, int K, cudaStream_t st) {
+cudaError_t launch_repack(int kind, const uint8_t* src, uint8_t* tiles, int N, int K, cudaStream_t st) {
     const TileLayout L(kind, N, K);
-    const size_t total = (size_t)L.nT * L.nkb * 256;
-    if (kind == kKindI4) repack_kernel<kKindI4><<<grid_for(total), 256, 0, st>>>(src, blobs, L, total);
-    else if (kind == kKindI8) repack_kernel<kKindI8><<<grid_for(total), 256, 0, st>>>(src, blobs, L, total);
-    else repack_kernel<kKindF16><<<grid_for(total), 256, 0, st>>>(src, blobs, L, total);
+    const size_t total = L.tiles() * 256;
+    uint32_t* out = reinterpret_cast<uint32_t*>(tiles);
+    if (kind == kKindI4) repack_kernel<kKindI4><<<grid_for(total), 256, 0, st>>>(src, out, L, total);
+    else if (kind == kKindI8) repack_kernel<kKindI8><<<grid_for(total), 256, 0, st>>>(src, out, L, total);
+    else repack_kernel<kKindF16><<<grid_for(total), 256, 0, st>>>(src, out, L, total);
     return cudaGetLastError();
 }
 
-cudaError_t launch_repack_i4_scales(const uint8_t* src, uint8_t* blobs, int N, int K, int gs, cudaStream_t st) {
+cudaError_t launch_repack_i4_scales(const uint8_t* src, uint32_t* sc, int N, int K, int gs, cudaStream_t st) {
     const TileLayout L(kKindI4, N, K);
-    const size_t total = (size_t)L.nT * L.nkb * 16;
+    const size_t total = L.scale_words();
     const int groups = (K + gs - 1) / gs;
-    repack_i4_scales_kernel<<<grid_for(total), 256, 0, st>>>(src, blobs, L, groups, gs, total);
+    repack_i4_scales_kernel<<<grid_for(total), 256, 0, st>>>(src, sc, L, groups, gs, total);
     return cudaGetLastError();
 }
 
-cudaError_t launch_dequant_i4(bool tiled, const void* w, const void* raw_scales, float* out, int N, int K,
-                              int groups, int gs, cudaStream_t st) {
+cudaError_t launch_dequant_i4(bool tiled, const void* w, const void* scales, float* out, int N, int K, int groups,
+                              int gs, cudaStream_t st) {
     const size_t total = (size_t)N * K;
     if (tiled)
-        dequant_i4_tiled_kernel<<<grid_for(total), 256, 0, st>>>((const uint8_t*)w, out, TileLayout(kKindI4, N, K));
+        dequant_i4_tiled_kernel<<<grid_for(total), 256, 0, st>>>((const uint8_t*)w, (const uint32_t*)scales, out,
+                                                                 TileLayout(kKindI4, N, K));
     else
-        dequant_i4_raw_kernel<<<grid_for(total), 256, 0, st>>>((const uint8_t*)w, (const uint8_t*)raw_scales, out, N,
-                                                               K, groups, gs);
+        dequant_i4_raw_kernel<<<grid_for(total), 256, 0, st>>>((const uint8_t*)w, (const uint8_t*)scales, out, N, K,
+                                                               groups, gs);
     return cudaGetLastError();
 }
 
@@ -898,16 +953,6 @@ cudaError_t launch_apply_outliers(const uint32_t* row_ptr, const uint2* entries,
     dim3 block(32, 8);
     dim3 grid((N + 7) / 8 < 4096 ? (N + 7) / 8 : 4096);
     apply_outliers_kernel<<<grid, block, 0, st>>>(row_ptr, entries, vals, out, N, K);
-    return cudaGetLastError();
-}
-
-cudaError_t launch_apply_outliers_items(const uint32_t* item_ptr, const uint2* entries, const uint16_t* vals,
-                                        float* out, int N, int K, cudaStream_t st) {
-    const TileLayout L(kKindI4, N, K);
-    dim3 block(32, 8);
-    const int items = L.items();
-    dim3 grid((items + 7) / 8 < 4096 ? (items + 7) / 8 : 4096);
-    apply_outliers_items_kernel<<<grid, block, 0, st>>>(item_ptr, entries, vals, out, L.nT, items, K);
     return cudaGetLastError();
 }
 

@@ -1,5 +1,5 @@
-// gemv.cuh -- launch interface and device-layout definitions of the GEMV / re-tiling /
-// dequantization kernels (gemv.cu).
+// gemv.cuh -- launch interface and device layout of the weight-only quantized GEMV, the x
+// preparation, re-tiling and dequantization kernels (gemv.cu).
 #pragma once
 
 #include <cuda_runtime.h>
@@ -9,63 +9,71 @@ namespace pox {
 
 enum { kKindI4 = 0, kKindI8 = 1, kKindF16 = 2 };
 
-constexpr int kTileBytesL = 1024;  // one tile: 16 rows x one k-block
-constexpr int kChunkTiles = 8;     // k-blocks per chunk (one streamed item = one row tile x one chunk)
-constexpr int kMaxBatch = 8;       // batch rows per launch of the streaming kernel
+constexpr int kTileBytes = 1024;  // one tile: 16 rows x one k-block
+constexpr int kMaxBatch = 8;      // batch rows per launch of the tensor-core GEMV
+constexpr int kXBlock = 128;      // k per x quantization block
 
 __host__ __device__ inline int kind_kblock(int kind) { return kind == kKindI4 ? 128 : (kind == kKindI8 ? 64 : 32); }
 
-// Device layout of a re-tiled weight matrix. The matrix is cut into items: one row tile (16
-// rows) x one chunk of kChunkTiles k-blocks. Items are ordered chunk-major (item = c * nT + T)
-// and stored as uniform blobs, so a CTA streaming a contiguous item range reads one contiguous
-// byte range and touches at most a couple of chunks of x:
-//   INT4 blob = [scales: 8 k-blocks x 16 rows x (f16 scale | f16 min << 16), 512 B][8 tiles]
-//   INT8/F16 blob = [8 tiles]
-// A tile (16 rows x one k-block) is 1 KiB: bytes [s*512 + lane*16, +16) hold lane's 16 bytes of
-// row g + 8s (g = lane/4) in MMA fragment order. The last chunk of a row may hold fewer than
-// kChunkTiles k-blocks; its blobs keep the full stride.
+// Device layout of a re-tiled weight matrix [N][K].
+// Tiles are 16 rows x one k-block (INT4 128 k, INT8 64 k, F16 32 k) = 1 KiB, stored row-tile
+// major: tile (T, kb) at byte (T * nkb + kb) * 1024, so the k-blocks of one row tile are one
+// contiguous stream. Inside a tile, lane l = 4g + t of a warp owns the 16 bytes at
+// s * 512 + l * 16 (s = 0, 1): row 16T + g + 8s, k sub-range t of the block:
+//   INT4: word w (4 bytes) of the 16: byte i = q[k0 + 8w + i] | q[k0 + 8w + 4 + i] << 4,
+//         k0 = 128 kb + 32 t (low nibbles and high nibbles each cover 4 consecutive k)
+//   INT8: byte j = q[64 kb + 16 t + j]
+//   F16 : half j = w[32 kb + 8 t + j]
+// so that a tile is read with two fully coalesced 512-byte warp loads and every lane's bytes
+// are directly the A fragments of m16n8k32 (u8/s8) or m16n8k16 (f16) MMAs.
+// INT4 scales: u32 (f16 scale | f16 min << 16) at [(T * nkb + kb) * 16 + 2g + s].
 struct TileLayout {
-    int N, K, KB, nT, nkb, nchunks, scale_bytes;
-    size_t stride;
+    int N, K, KB, nT, nkb;
     __host__ __device__ TileLayout(int kind, int N_, int K_) : N(N_), K(K_) {
         KB = kind_kblock(kind);
         nT = (N + 15) / 16;
         nkb = K / KB;
-        nchunks = (nkb + kChunkTiles - 1) / kChunkTiles;
-        scale_bytes = kind == kKindI4 ? kChunkTiles * 64 : 0;
-        stride = (size_t)scale_bytes + (size_t)kChunkTiles * kTileBytesL;
     }
-    __host__ __device__ int kch(int c) const {
-        const int r = nkb - c * kChunkTiles;
-        return r < kChunkTiles ? r : kChunkTiles;
-    }
-    __host__ __device__ int items() const { return nT * nchunks; }
-    __host__ __device__ size_t bytes() const { return (size_t)items() * stride; }
-    // byte offset of tile (row tile T, k-block kb) and of its 16 scale words (INT4)
-    __host__ __device__ size_t tile_off(int T, int kb) const {
-        const size_t item = (size_t)(kb / kChunkTiles) * nT + T;
-        return item * stride + scale_bytes + (size_t)(kb % kChunkTiles) * kTileBytesL;
-    }
-    __host__ __device__ size_t scale_off(int T, int kb) const {
-        const size_t item = (size_t)(kb / kChunkTiles) * nT + T;
-        return item * stride + (size_t)(kb % kChunkTiles) * 64;
-    }
+    __host__ __device__ size_t tiles() const { return (size_t)nT * nkb; }
+    __host__ __device__ size_t bytes() const { return tiles() * kTileBytes; }
+    __host__ __device__ size_t scale_words() const { return tiles() * 16; }
 };
 
-struct StreamArgs {
-    const unsigned char* blobs;  // re-tiled weights (item blobs, see TileLayout)
-    float i8_scale;              // INT8 per-tensor scale
-    const uint32_t* item_ptr;    // outlier CSR by item [items+1] (nullptr if none)
-    const uint2* entries;        // (col << 4 | row % 16, f32 bits of v - dequant(q))
-    const float* x;              // [B][K] device, 16-byte aligned
-    float* y;                    // [B][N] device
-    float* partial;              // scratch [nT][nchunks][16][kMaxBatch]
-    unsigned* counters;          // scratch [nT], zero between launches
-    int* err;                    // error flag (host-mapped)
-    int N, K, B;
-    int ring;                    // smem ring stages
-    int span;                    // max chunks of x a CTA stages
+// Prepared activations ("x prep"): x [B][K] f32 becomes, per batch row b, two columns
+// 2b (hi) and 2b+1 (lo) of Kp = ceil(K / 128) * 128 elements each:
+//   INT4 / INT8 weights: per 128-k block, X = rint(x * 16383 / max|x|) split into exact int8
+//     limbs X = 128 * hi + lo (hi in [-128, 127], lo in [0, 127]); meta[b][blk] = (max|x| /
+//     16383, sum of x over the block)
+//   F16 weights: hi = f16(x), lo = f16(x - hi) (22 significant bits of x)
+struct XPrep {
+    void* cols;      // [2B][Kp] bytes (INT) or halves (F16)
+    float2* meta;    // [B][nxbs]: nxbs = Kp / 128 rounded up to even (16-byte aligned rows)
+    int Kp, nxb, nxbs;
 };
+
+struct GemvArgs {
+    const uint8_t* w;        // tiles
+    const uint32_t* sc;      // INT4 scale words (nullptr otherwise)
+    float i8_scale;          // INT8 per-tensor scale
+    const uint32_t* row_ptr; // outlier CSR by row [N+1] (nullptr if none)
+    const uint2* ent;        // (col, f32 bits of v - dequant(q))
+    const void* xq;          // prepared x columns
+    const float2* xm;        // prepared x meta
+    const float* x;          // original x [B][K] f32 (outlier correction)
+    float* y;                // [B][N]
+    int* err;                // kernel error flag (a bounded wait expired)
+    int N, K, Kp, B, nxb, nxbs;
+    int nT, nkb, S;          // row tiles, k-blocks, k-splits (cluster size)
+};
+
+// Scratch bytes of the prepared x for a tensor of `K` columns at up to kMaxBatch rows.
+size_t xprep_bytes(int kind, int K);
+XPrep xprep_view(void* scratch, int kind, int K);
+
+cudaError_t launch_xprep(int kind, const float* x, int B, int K, const XPrep& xp, bool pdl, cudaStream_t st);
+// Plans and launches the tensor-core GEMV (B <= kMaxBatch). pdl lets the weight stream start
+// before the previous kernel in the stream (the x preparation) has finished.
+cudaError_t launch_gemv_tc(int kind, const GemvArgs& a, bool pdl, cudaStream_t st);
 
 // Row-per-warp GEMV over the raw .pox layout (any even group size, any cols).
 struct GemvGenericArgs {
@@ -78,24 +86,14 @@ struct GemvGenericArgs {
     float* y;
     int N, K, B, gs, groups;
 };
-
-enum { kErrTimeoutFull = 1, kErrTimeoutEmpty = 2 };
-
-// Scratch bytes the streaming kernel needs for a tensor (partials + counters).
-size_t stream_scratch_bytes(int kind, int N, int K);
-// Plans and launches the streaming GEMV (B <= kMaxBatch). Returns cudaErrorInvalidConfiguration
-// when the shape does not fit the kernel's shared-memory plan. pdl enables programmatic
-// dependent launch (the weight stream may start before the previous kernel in the stream ends).
-cudaError_t launch_gemv_stream(int kind, const StreamArgs& a, bool pdl, cudaStream_t st);
 cudaError_t launch_gemv_generic(int kind, const GemvGenericArgs& a, cudaStream_t st);
-cudaError_t launch_repack(int kind, const uint8_t* src, uint8_t* blobs, int N, int K, cudaStream_t st);
-cudaError_t launch_repack_i4_scales(const uint8_t* src, uint8_t* blobs, int N, int K, int gs, cudaStream_t st);
-cudaError_t launch_dequant_i4(bool tiled, const void* w, const void* raw_scales, float* out, int N, int K,
-                              int groups, int gs, cudaStream_t st);
+
+cudaError_t launch_repack(int kind, const uint8_t* src, uint8_t* tiles, int N, int K, cudaStream_t st);
+cudaError_t launch_repack_i4_scales(const uint8_t* src, uint32_t* sc, int N, int K, int gs, cudaStream_t st);
+cudaError_t launch_dequant_i4(bool tiled, const void* w, const void* scales, float* out, int N, int K, int groups,
+                              int gs, cudaStream_t st);
 cudaError_t launch_dequant_i8(bool tiled, const void* w, float scale, float* out, int N, int K, cudaStream_t st);
 cudaError_t launch_apply_outliers(const uint32_t* row_ptr, const uint2* entries, const uint16_t* vals, float* out,
                                   int N, int K, cudaStream_t st);
-cudaError_t launch_apply_outliers_items(const uint32_t* item_ptr, const uint2* entries, const uint16_t* vals,
-                                        float* out, int N, int K, cudaStream_t st);
 
 }  // namespace pox

@@ -104,14 +104,12 @@ static void free_tensor_mem(pox_tensor* t) {
     cudaFree(t->w);
     cudaFree(t->scales_dev);
     cudaFree(t->row_ptr);
-    cudaFree(t->item_ptr);
     cudaFree(t->entries);
     cudaFree(t->vals);
     cudaFree(t->scratch);
     t->scratch = nullptr;
     t->w = t->scales_dev = nullptr;
     t->row_ptr = nullptr;
-    t->item_ptr = nullptr;
     t->entries = nullptr;
     t->vals = nullptr;
 }
@@ -324,14 +322,15 @@ int pox::upload_tensor_locked(pox_cuda_ctx* ctx, const pox_tensor_desc* d, pox_t
         CKF(cudaMemcpyAsync(tmp, d->data, raw_bytes, cudaMemcpyHostToDevice, st), "cudaMemcpy(raw)");
         if (t->tiled) {
             const TileLayout TL(kKindI4, N, K);
-            CKF(cudaMalloc(&t->w, TL.bytes()), "cudaMalloc(blobs)");
-            CKF(cudaMemsetAsync(t->w, 0, TL.bytes(), st), "cudaMemset(blobs)");
+            CKF(cudaMalloc(&t->w, TL.bytes()), "cudaMalloc(tiles)");
             CKF(launch_repack(kKindI4, (const uint8_t*)tmp, (uint8_t*)t->w, N, K, st), "repack_i4");
             CKF(cudaMalloc(&tmp_s, sbytes), "cudaMalloc(raw scales)");
             CKF(cudaMemcpyAsync(tmp_s, d->scales, sbytes, cudaMemcpyHostToDevice, st), "cudaMemcpy(scales)");
-            CKF(launch_repack_i4_scales((const uint8_t*)tmp_s, (uint8_t*)t->w, N, K, (int)d->group_size, st),
+            CKF(cudaMalloc(&t->scales_dev, TL.scale_words() * 4), "cudaMalloc(scale words)");
+            CKF(launch_repack_i4_scales((const uint8_t*)tmp_s, (uint32_t*)t->scales_dev, N, K, (int)d->group_size,
+                                        st),
                 "repack_i4_scales");
-            t->bytes += TL.bytes();
+            t->bytes += TL.bytes() + TL.scale_words() * 4;
         } else {
             t->w = tmp;
             tmp = nullptr;
@@ -345,51 +344,18 @@ int pox::upload_tensor_locked(pox_cuda_ctx* ctx, const pox_tensor_desc* d, pox_t
         std::vector<uint16_t> vals;
         rc = build_outlier_csr(d, rp, cols, corr, vals);
         if (rc) return fail(rc);
-        std::vector<uint32_t> ip;
-        std::vector<uint2> ent(cols.size());
-        std::vector<uint16_t> ivals;
-        if (!cols.empty() && t->tiled) {
-            // re-key by streamed item (row tile x k-chunk): the GEMV consumer that owns an item
-            // applies that item's outliers with x from its shared-memory window
-            const TileLayout TL(kKindI4, N, K);
-            std::vector<uint32_t> rows(cols.size());
-            for (size_t r = 0; r < d->rows; r++)
-                for (uint32_t e = rp[r]; e < rp[r + 1]; e++) rows[e] = (uint32_t)r;
-            auto item_of = [&](size_t e) {
-                return (uint32_t)((cols[e] / 128 / kChunkTiles) * TL.nT + rows[e] / 16);
-            };
-            std::vector<uint32_t> order(cols.size());
-            for (size_t e = 0; e < order.size(); e++) order[e] = (uint32_t)e;
-            std::stable_sort(order.begin(), order.end(),
-                             [&](uint32_t a, uint32_t b) { return item_of(a) < item_of(b); });
-            ip.assign((size_t)TL.items() + 1, 0);
-            ivals.resize(cols.size());
-            for (size_t i = 0; i < order.size(); i++) {
-                const uint32_t e = order[i];
-                uint32_t cb;
-                std::memcpy(&cb, &corr[e], 4);
-                ent[i] = make_uint2((cols[e] << 4) | (rows[e] & 15u), cb);
-                ivals[i] = vals[e];
-                ip[item_of(e) + 1]++;
-            }
-            for (size_t i = 0; i + 1 < ip.size(); i++) ip[i + 1] += ip[i];
-        } else {
+        if (!cols.empty()) {
+            std::vector<uint2> ent(cols.size());
             for (size_t i = 0; i < cols.size(); i++) {
                 uint32_t cb;
                 std::memcpy(&cb, &corr[i], 4);
                 ent[i] = make_uint2(cols[i], cb);
             }
-        }
-        if (!cols.empty()) {
             t->nnz = cols.size();
-            if (t->tiled) {
-                if ((rc = upload_vec(ip, (void**)&t->item_ptr, &t->bytes, st))) return fail(rc);
-                if ((rc = upload_vec(ivals, (void**)&t->vals, &t->bytes, st))) return fail(rc);
-            } else {
-                if ((rc = upload_vec(rp, (void**)&t->row_ptr, &t->bytes, st))) return fail(rc);
-                if ((rc = upload_vec(vals, (void**)&t->vals, &t->bytes, st))) return fail(rc);
-            }
-            ent.push_back(make_uint2(0u, 0u));  // pad: entry copies are rounded up to 16-byte pairs
+            if ((rc = upload_vec(rp, (void**)&t->row_ptr, &t->bytes, st))) return fail(rc);
+            if ((rc = upload_vec(vals, (void**)&t->vals, &t->bytes, st))) return fail(rc);
+            ent.push_back(make_uint2(0u, 0u));  // padding: the GEMV copies entries in 16-byte pairs
+            ent.push_back(make_uint2(0u, 0u));
             if ((rc = upload_vec(ent, (void**)&t->entries, &t->bytes, st))) return fail(rc);
             // the host vectors must outlive the async copies
             CKF(cudaStreamSynchronize(st), "cudaStreamSynchronize(upload)");
@@ -402,8 +368,7 @@ int pox::upload_tensor_locked(pox_cuda_ctx* ctx, const pox_tensor_desc* d, pox_t
         CKF(cudaMemcpyAsync(tmp, d->data, raw_bytes, cudaMemcpyHostToDevice, st), "cudaMemcpy(raw)");
         if (t->tiled) {
             const size_t tiles_bytes = TileLayout(kKindI8, N, K).bytes();
-            CKF(cudaMalloc(&t->w, tiles_bytes), "cudaMalloc(blobs)");
-            CKF(cudaMemsetAsync(t->w, 0, tiles_bytes, st), "cudaMemset(blobs)");
+            CKF(cudaMalloc(&t->w, tiles_bytes), "cudaMalloc(tiles)");
             CKF(launch_repack(kKindI8, (const uint8_t*)tmp, (uint8_t*)t->w, N, K, st), "repack_i8");
             t->bytes += tiles_bytes;
         } else {
@@ -418,8 +383,7 @@ int pox::upload_tensor_locked(pox_cuda_ctx* ctx, const pox_tensor_desc* d, pox_t
         CKF(cudaMemcpyAsync(tmp, d->data, raw_bytes, cudaMemcpyHostToDevice, st), "cudaMemcpy(raw)");
         if (t->tiled) {
             const size_t tiles_bytes = TileLayout(kKindF16, N, K).bytes();
-            CKF(cudaMalloc(&t->w, tiles_bytes), "cudaMalloc(blobs)");
-            CKF(cudaMemsetAsync(t->w, 0, tiles_bytes, st), "cudaMemset(blobs)");
+            CKF(cudaMalloc(&t->w, tiles_bytes), "cudaMalloc(tiles)");
             CKF(launch_repack(kKindF16, (const uint8_t*)tmp, (uint8_t*)t->w, N, K, st), "repack_f16");
             t->bytes += tiles_bytes;
         } else {
@@ -430,9 +394,8 @@ int pox::upload_tensor_locked(pox_cuda_ctx* ctx, const pox_tensor_desc* d, pox_t
     }
     if (t->tiled) {
         const int kind = d->dtype == POX_I4 ? kKindI4 : (d->dtype == POX_I8 ? kKindI8 : kKindF16);
-        const size_t sb = stream_scratch_bytes(kind, N, K);
-        CKF(cudaMalloc(&t->scratch, sb), "cudaMalloc(gemv scratch)");
-        CKF(cudaMemsetAsync(t->scratch, 0, sb, st), "cudaMemset(gemv scratch)");
+        const size_t sb = xprep_bytes(kind, K);
+        CKF(cudaMalloc(&t->scratch, sb), "cudaMalloc(prepared x)");
         t->scratch_bytes = sb;
         t->bytes += sb;
     }
@@ -494,20 +457,30 @@ int pox::gemv_launch(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x, siz
         cudaError_t e;
         if (t->tiled) {
             const TileLayout TL(kind, N, K);
-            StreamArgs a = {};
-            a.blobs = (const unsigned char*)t->w;
+            const XPrep xp = xprep_view(t->scratch, kind, K);
+            e = launch_xprep(kind, xb, (int)b, K, xp, true, st);
+            if (e != cudaSuccess) return cuda_error(e, "x preparation launch");
+            GemvArgs a = {};
+            a.w = (const uint8_t*)t->w;
+            a.sc = kind == kKindI4 ? (const uint32_t*)t->scales_dev : nullptr;
             a.i8_scale = t->i8_scale;
-            a.item_ptr = t->item_ptr;
-            a.entries = t->entries;
+            a.row_ptr = kind == kKindI4 ? t->row_ptr : nullptr;
+            a.ent = t->entries;
+            a.xq = xp.cols;
+            a.xm = xp.meta;
             a.x = xb;
             a.y = yb;
-            a.partial = (float*)t->scratch;
-            a.counters = (unsigned*)((char*)t->scratch + (size_t)TL.nT * TL.nchunks * 16 * kMaxBatch * 4);
-            a.err = ctx->err_dev;
             a.N = N;
             a.K = K;
+            a.Kp = xp.Kp;
             a.B = (int)b;
-            e = launch_gemv_stream(kind, a, true, st);
+            a.nxb = xp.nxb;
+            a.nxbs = xp.nxbs;
+            a.err = ctx->err_dev;
+            a.nT = TL.nT;
+            a.nkb = TL.nkb;
+            a.S = 1;
+            e = launch_gemv_tc(kind, a, true, st);
         } else {
             GemvGenericArgs a;
             a.raw = (const uint8_t*)t->w;
@@ -656,8 +629,7 @@ static int dequant_launch(const pox_tensor* t, float* out, cudaStream_t st) {
     if (t->dtype == POX_I4) {
         e = launch_dequant_i4(t->tiled, t->w, t->scales_dev, out, N, K, t->groups, (int)t->gs, st);
         if (e == cudaSuccess && t->nnz)
-            e = t->tiled ? launch_apply_outliers_items(t->item_ptr, t->entries, t->vals, out, N, K, st)
-                         : launch_apply_outliers(t->row_ptr, t->entries, t->vals, out, N, K, st);
+            e = launch_apply_outliers(t->row_ptr, t->entries, t->vals, out, N, K, st);
     } else if (t->dtype == POX_I8) {
         e = launch_dequant_i8(t->tiled, t->w, t->i8_scale, out, N, K, st);
     } else {

@@ -138,6 +138,17 @@ int pox_cuda_tensor_gemv(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x_
 /* Same with host x/y: copies x in and y out, synchronous. */
 int pox_cuda_tensor_gemv_host(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x, size_t batch,
                               float* y);
+/* Same GEMV as pox_cuda_tensor_gemv, for callers that cannot allocate device memory once they
+ * are running (an engine that reserved its HBM at start-up, a host runtime that only hands over
+ * buffers it owns). No counterpart in the reference: it exists only because this backend's
+ * GEMV needs scratch for the prepared x. That scratch is a fixed 1 MiB + 16 KiB array in device
+ * memory, shared by every call on a device and held until the process exits; the call allocates
+ * and frees nothing. Limit: cols <= 32768 (larger -> POX_ERR_UNSUPPORTED). Calls whose kernels
+ * overlap on the same device (other streams or contexts) race on the shared array: serialize
+ * them. The first call on a device looks up the array's device address, so make that first call
+ * before any stream capture. */
+int pox_cuda_tensor_gemv_noalloc(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x_dev, size_t batch,
+                                 float* y_dev, void* stream);
 /* Dequantizes a resident tensor into out_dev ([rows][cols] f32, device), bit-exact with
  * dequantize_int4_group / dequantize_int8_symmetric (kernels.rs:85-128,157-173) followed by
  * SparseOutlierTable::apply_to (outlier.rs:88-95). Asynchronous on `stream`. */

@@ -72,6 +72,7 @@ def _declare(L):
         "pox_cuda_tensor_info": (i32, [vp, C.POINTER(sz), C.POINTER(sz), C.POINTER(sz), C.POINTER(sz)]),
         "pox_cuda_tensor_gemv": (i32, [vp, vp, vp, sz, vp, vp]),
         "pox_cuda_tensor_gemv_host": (i32, [vp, vp, vp, sz, vp]),
+        "pox_cuda_tensor_gemv_noalloc": (i32, [vp, vp, vp, sz, vp, vp]),
         "pox_cuda_tensor_dequant": (i32, [vp, vp, vp, vp]),
         "pox_cuda_tensor_dequant_host": (i32, [vp, vp, vp]),
     }

@@ -340,11 +340,13 @@ def run_ours(args):
                 "pct_of_peak": round(100.0 * achieved / peak, 2),
                 "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                              "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                             "kernel": "gemv_tc_kernel<INT4,1> with its x preparation (one step = both launches, "
+                                       "PDL-overlapped, timed together with CUDA events)",
                              "traffic": traffic},
                 "e2e": {"value": round(e2e_gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": COLS * 4,
                         "d2h_bytes_per_step": ROWS * 4, "steps": e2e_steps,
                         "us_per_call": e2e_s / e2e_steps * 1e6},
-                "gpu_launches": args.steps, "clocks": clocks, "check_max_rel": rel,
+                "gpu_launches": 2 * args.steps, "clocks": clocks, "check_max_rel": rel,
                 "cpu_baseline": cpu}
         print(json.dumps(line), flush=True)
     for tt in tensors:

@@ -37,38 +37,6 @@
 
 namespace pox {
 
-// ---- PTX wrappers -------------------------------------------------------------------------
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ uint4 lds128(uint32_t a) {
-    uint4 r;
-    asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(a));
-    return r;
-}
-__device__ __forceinline__ uint2 ldg64_nc(const void* p) {
-    uint2 r;
-    asm volatile("ld.global.nc.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "l"(p));
-    return r;
-}
-__device__ __forceinline__ uint4 ldg128_nc(const void* p) {
-    uint4 r;
-    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "l"(p));
-    return r;
-}
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
-__device__ __forceinline__ void cluster_sync_all() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-__device__ __forceinline__ float ld_dsmem_f32(const void* local, uint32_t rank) {
-    uint32_t remote;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(remote) : "memory");
-    return v;
-}
-
 // ------------------------------------------------------------------------------------------
 // x preparation
 // ------------------------------------------------------------------------------------------
@@ -90,7 +58,6 @@ XPrep xprep_view(void* scratch, int kind, int K) {
     return v;
 }
 
-constexpr int kXLimbMax = 16383;  // |X| bound of the 15-bit quantization
 
 // One warp per (batch row, 128-k block); lane l covers k = 4l .. 4l+3 of the block.
 __global__ void __launch_bounds__(256) xprep_int_kernel(const float* __restrict__ x, int B, int K, uint8_t* cols,
@@ -179,7 +146,7 @@ struct SmemPlan {
 __host__ __device__ inline SmemPlan smem_plan(int kind, int B, int W, int S, int nkb, bool outl) {
     SmemPlan p;
     const int KB = kind_kblock(kind), XB = kind == kKindF16 ? 2 : 1;
-    const int tb = kTileBytes + (kind == kKindI4 ? 64 : 0);
+    const int tb = kind_tile_bytes(kind);
     p.kbr = (nkb + S - 1) / S;
     const int xr = p.kbr * KB * XB;
     p.cstride = ((xr + 127) & ~127) + (kind == kKindI4 ? 16 : 64);
@@ -198,49 +165,6 @@ __host__ __device__ inline SmemPlan smem_plan(int kind, int B, int W, int S, int
     return p;
 }
 
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
-                 : "memory");
-}
-constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 2 GHz: a bounded wait, never a hang
-// Bounded wait on the phase of the given parity; false = the budget ran out.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n"
-        " selp.u32 %0, 1, 0, p;\n}"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    if (ok) return true;
-    const long long t0 = clock64();
-    for (;;) {
-        asm volatile(
-            "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n"
-            " selp.u32 %0, 1, 0, p;\n}"
-            : "=r"(ok)
-            : "r"(bar), "r"(parity)
-            : "memory");
-        if (ok) return true;
-        if (clock64() - t0 > kWaitCycles) return false;
-    }
-}
-// TMA bulk copy (no multicast) global -> shared, completion counted on an mbarrier.
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-    asm volatile("cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
-                 "l"(src), "r"(bytes), "r"(bar)
-                 : "memory");
-}
-__device__ __forceinline__ uint2 lds64(uint32_t a) {
-    uint2 r;
-    asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(r.x), "=r"(r.y) : "r"(a));
-    return r;
-}
-
-enum { kErrWaitRing = 1, kErrWaitX = 2, kErrWaitEnt = 4 };
 
 // BT: exact batch 1..4, or 8 for a runtime batch of 5..8 (two MMA column blocks).
 template <int KIND, int BT>
@@ -278,9 +202,8 @@ __global__ void __launch_bounds__(512, 2) gemv_tc_kernel(const GemvArgs a) {
 
     // this warp's tiles: kb = kb0 + warp + i * W, i < nt
     const int nt = kb0 + warp < kb1 ? (kb1 - kb0 - warp + W - 1) / W : 0;
-    const uint8_t* wsrc = a.w + ((size_t)T * nkb + kb0 + warp) * kTileBytes;
-    const uint32_t* ssrc = KIND == kKindI4 ? a.sc + ((size_t)T * nkb + kb0 + warp) * 16 : nullptr;
-    const size_t wstep = (size_t)W * kTileBytes;
+    const uint8_t* wsrc = a.w + ((size_t)T * nkb + kb0 + warp) * TB;
+    const size_t wstep = (size_t)W * TB;
 
     if (lane == 0)
         for (int i = 0; i < kStages; i++) mbar_init(wbar + 8 * i, 1);
@@ -297,8 +220,7 @@ __global__ void __launch_bounds__(512, 2) gemv_tc_kernel(const GemvArgs a) {
     auto issue = [&](int i) {  // lane 0 only
         const uint32_t st = ring + (i % kStages) * TB, bar = wbar + 8 * (i % kStages);
         mbar_expect_tx(bar, TB);
-        bulk_g2s(st, wsrc + (size_t)i * wstep, kTileBytes, bar);
-        if (KIND == kKindI4) bulk_g2s(st + kTileBytes, ssrc + (size_t)i * W * 16, 64, bar);
+        bulk_g2s(st, wsrc + (size_t)i * wstep, TB, bar);  // INT4: nibbles and scale words in one copy
     };
     if (lane == 0)
         for (int i = 0; i < kStages && i < nt; i++) issue(i);
@@ -782,7 +704,7 @@ cudaError_t launch_gemv_generic(int kind, const GemvGenericArgs& a, cudaStream_t
 // o = ((T * nkb + kb) * 2 + s) * 128 + lane * 4 + w, i.e. the byte layout of TileLayout.
 // ------------------------------------------------------------------------------------------
 template <int KIND>
-__global__ void repack_kernel(const uint8_t* __restrict__ src, uint32_t* __restrict__ out, TileLayout L,
+__global__ void repack_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ out, TileLayout L,
                               size_t total) {
     for (size_t o = blockIdx.x * (size_t)blockDim.x + threadIdx.x; o < total; o += (size_t)gridDim.x * blockDim.x) {
         const int w = (int)(o & 3), lane = (int)((o >> 2) & 31), s = (int)((o >> 7) & 1);
@@ -806,13 +728,13 @@ __global__ void repack_kernel(const uint8_t* __restrict__ src, uint32_t* __restr
                 word = *reinterpret_cast<const uint32_t*>(src + (row * (size_t)L.K + (size_t)kb * 32 + 8 * t + 2 * w) * 2);
             }
         }
-        out[o] = word;
+        *reinterpret_cast<uint32_t*>(out + tile * L.tb + (o & 255) * 4) = word;
     }
 }
 
-// INT4 scale words: [(T * nkb + kb) * 16 + 2 g + s] = (f16 scale | f16 min << 16) of row
-// 16 T + g + 8 s and the group holding k-block kb.
-__global__ void repack_i4_scales_kernel(const uint8_t* __restrict__ src, uint32_t* __restrict__ sc, TileLayout L,
+// INT4 scale words: word 2 g + s after the nibbles of tile (T, kb) = (f16 scale | f16 min << 16) of
+// row 16 T + g + 8 s and the group holding k-block kb.
+__global__ void repack_i4_scales_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ tiles, TileLayout L,
                                         int groups, int gs, size_t total) {
     for (size_t o = blockIdx.x * (size_t)blockDim.x + threadIdx.x; o < total; o += (size_t)gridDim.x * blockDim.x) {
         const int j = (int)(o & 15);
@@ -824,15 +746,14 @@ __global__ void repack_i4_scales_kernel(const uint8_t* __restrict__ src, uint32_
             const int grp = kb * 128 / gs;
             v = *reinterpret_cast<const uint32_t*>(src + (row * groups + grp) * 4);
         }
-        sc[o] = v;
+        *reinterpret_cast<uint32_t*>(tiles + tile * L.tb + kTileBytes + j * 4) = v;
     }
 }
 
 // ------------------------------------------------------------------------------------------
 // Dequantization (verification path): bit-exact with the reference (mul, then add).
 // ------------------------------------------------------------------------------------------
-__global__ void dequant_i4_tiled_kernel(const uint8_t* __restrict__ tiles, const uint32_t* __restrict__ sc,
-                                        float* __restrict__ out, TileLayout L) {
+__global__ void dequant_i4_tiled_kernel(const uint8_t* __restrict__ tiles, float* __restrict__ out, TileLayout L) {
     const size_t total = (size_t)L.N * L.K;
     for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total;
          idx += (size_t)gridDim.x * blockDim.x) {
@@ -841,9 +762,9 @@ __global__ void dequant_i4_tiled_kernel(const uint8_t* __restrict__ tiles, const
         const int T = (int)(row / 16), ri = (int)(row % 16), g = ri & 7, s = ri >> 3;
         const int kb = k / 128, kin = k % 128, t = kin / 32, rem = kin % 32, w = rem / 8, p = rem % 8;
         const size_t tile = (size_t)T * L.nkb + kb;
-        const uint8_t byte = tiles[tile * kTileBytes + s * 512 + (4 * g + t) * 16 + 4 * w + (p & 3)];
+        const uint8_t byte = tiles[tile * L.tb + s * 512 + (4 * g + t) * 16 + 4 * w + (p & 3)];
         const uint32_t q = (p < 4) ? (byte & 15u) : (byte >> 4);
-        const uint32_t sm = sc[tile * 16 + 2 * g + s];
+        const uint32_t sm = *reinterpret_cast<const uint32_t*>(tiles + tile * L.tb + kTileBytes + (2 * g + s) * 4);
         const float scl = half_bits_to_float(sm), mn = half_bits_to_float(sm >> 16);
         out[idx] = __fadd_rn(mn, __fmul_rn((float)q, scl));
     }
@@ -877,7 +798,7 @@ __global__ void dequant_i8_tiled_kernel(const uint8_t* __restrict__ tiles, float
         const int T = (int)(row / 16), ri = (int)(row % 16), g = ri & 7, s = ri >> 3;
         const int kb = k / 64, kin = k % 64, t = kin / 16, j = kin % 16;
         const size_t tile = (size_t)T * L.nkb + kb;
-        const int8_t q = (int8_t)tiles[tile * kTileBytes + s * 512 + (4 * g + t) * 16 + j];
+        const int8_t q = (int8_t)tiles[tile * L.tb + s * 512 + (4 * g + t) * 16 + j];
         out[idx] = __fmul_rn((float)q, scale);
     }
 }
@@ -911,18 +832,17 @@ static dim3 grid_for(size_t total) {
 cudaError_t launch_repack(int kind, const uint8_t* src, uint8_t* tiles, int N, int K, cudaStream_t st) {
     const TileLayout L(kind, N, K);
     const size_t total = L.tiles() * 256;
-    uint32_t* out = reinterpret_cast<uint32_t*>(tiles);
-    if (kind == kKindI4) repack_kernel<kKindI4><<<grid_for(total), 256, 0, st>>>(src, out, L, total);
-    else if (kind == kKindI8) repack_kernel<kKindI8><<<grid_for(total), 256, 0, st>>>(src, out, L, total);
-    else repack_kernel<kKindF16><<<grid_for(total), 256, 0, st>>>(src, out, L, total);
+    if (kind == kKindI4) repack_kernel<kKindI4><<<grid_for(total), 256, 0, st>>>(src, tiles, L, total);
+    else if (kind == kKindI8) repack_kernel<kKindI8><<<grid_for(total), 256, 0, st>>>(src, tiles, L, total);
+    else repack_kernel<kKindF16><<<grid_for(total), 256, 0, st>>>(src, tiles, L, total);
     return cudaGetLastError();
 }
 
-cudaError_t launch_repack_i4_scales(const uint8_t* src, uint32_t* sc, int N, int K, int gs, cudaStream_t st) {
+cudaError_t launch_repack_i4_scales(const uint8_t* src, uint8_t* tiles, int N, int K, int gs, cudaStream_t st) {
     const TileLayout L(kKindI4, N, K);
-    const size_t total = L.scale_words();
+    const size_t total = L.tiles() * 16;
     const int groups = (K + gs - 1) / gs;
-    repack_i4_scales_kernel<<<grid_for(total), 256, 0, st>>>(src, sc, L, groups, gs, total);
+    repack_i4_scales_kernel<<<grid_for(total), 256, 0, st>>>(src, tiles, L, groups, gs, total);
     return cudaGetLastError();
 }
 
@@ -930,8 +850,7 @@ cudaError_t launch_dequant_i4(bool tiled, const void* w, const void* scales, flo
                               int gs, cudaStream_t st) {
     const size_t total = (size_t)N * K;
     if (tiled)
-        dequant_i4_tiled_kernel<<<grid_for(total), 256, 0, st>>>((const uint8_t*)w, (const uint32_t*)scales, out,
-                                                                 TileLayout(kKindI4, N, K));
+        dequant_i4_tiled_kernel<<<grid_for(total), 256, 0, st>>>((const uint8_t*)w, out, TileLayout(kKindI4, N, K));
     else
         dequant_i4_raw_kernel<<<grid_for(total), 256, 0, st>>>((const uint8_t*)w, (const uint8_t*)scales, out, N, K,
                                                                groups, gs);

@@ -12,6 +12,9 @@ enum { kKindI4 = 0, kKindI8 = 1, kKindF16 = 2 };
 constexpr int kTileBytes = 1024;  // one tile: 16 rows x one k-block
 constexpr int kMaxBatch = 8;      // batch rows per launch of the tensor-core GEMV
 constexpr int kXBlock = 128;      // k per x quantization block
+constexpr int kXLimbMax = 16383;  // |X| bound of the 15-bit x quantization
+
+enum { kErrWaitRing = 1, kErrWaitX = 2, kErrWaitEnt = 4 };  // bits of the kernel error flag
 
 __host__ __device__ inline int kind_kblock(int kind) { return kind == kKindI4 ? 128 : (kind == kKindI8 ? 64 : 32); }
 
@@ -26,17 +29,20 @@ __host__ __device__ inline int kind_kblock(int kind) { return kind == kKindI4 ? 
 //   F16 : half j = w[32 kb + 8 t + j]
 // so that a tile is read with two fully coalesced 512-byte warp loads and every lane's bytes
 // are directly the A fragments of m16n8k32 (u8/s8) or m16n8k16 (f16) MMAs.
-// INT4 scales: u32 (f16 scale | f16 min << 16) at [(T * nkb + kb) * 16 + 2g + s].
+// INT4 tiles carry their scales: the 1 KiB of nibbles is followed by 16 u32 words
+// (f16 scale | f16 min << 16), word 2g + s for row 16T + g + 8s, so one blob is 1088 bytes and a
+// run of consecutive tiles is one contiguous copy.
+__host__ __device__ inline int kind_tile_bytes(int kind) { return kTileBytes + (kind == kKindI4 ? 64 : 0); }
 struct TileLayout {
-    int N, K, KB, nT, nkb;
+    int N, K, KB, nT, nkb, tb;
     __host__ __device__ TileLayout(int kind, int N_, int K_) : N(N_), K(K_) {
         KB = kind_kblock(kind);
         nT = (N + 15) / 16;
         nkb = K / KB;
+        tb = kind_tile_bytes(kind);
     }
     __host__ __device__ size_t tiles() const { return (size_t)nT * nkb; }
-    __host__ __device__ size_t bytes() const { return tiles() * kTileBytes; }
-    __host__ __device__ size_t scale_words() const { return tiles() * 16; }
+    __host__ __device__ size_t bytes() const { return tiles() * tb; }
 };
 
 // Prepared activations ("x prep"): x [B][K] f32 becomes, per batch row b, two columns
@@ -52,8 +58,7 @@ struct XPrep {
 };
 
 struct GemvArgs {
-    const uint8_t* w;        // tiles
-    const uint32_t* sc;      // INT4 scale words (nullptr otherwise)
+    const uint8_t* w;        // tile blobs (TileLayout)
     float i8_scale;          // INT8 per-tensor scale
     const uint32_t* row_ptr; // outlier CSR by row [N+1] (nullptr if none)
     const uint2* ent;        // (col, f32 bits of v - dequant(q))
@@ -89,7 +94,7 @@ struct GemvGenericArgs {
 cudaError_t launch_gemv_generic(int kind, const GemvGenericArgs& a, cudaStream_t st);
 
 cudaError_t launch_repack(int kind, const uint8_t* src, uint8_t* tiles, int N, int K, cudaStream_t st);
-cudaError_t launch_repack_i4_scales(const uint8_t* src, uint32_t* sc, int N, int K, int gs, cudaStream_t st);
+cudaError_t launch_repack_i4_scales(const uint8_t* src, uint8_t* tiles, int N, int K, int gs, cudaStream_t st);
 cudaError_t launch_dequant_i4(bool tiled, const void* w, const void* scales, float* out, int N, int K, int groups,
                               int gs, cudaStream_t st);
 cudaError_t launch_dequant_i8(bool tiled, const void* w, float scale, float* out, int N, int K, cudaStream_t st);

@@ -85,7 +85,6 @@ extern "C" int pox_cuda_tensor_gemv_noalloc(pox_cuda_ctx* ctx, const pox_tensor*
             if (e != cudaSuccess) return cuda_error(e, "x preparation launch");
             GemvArgs a = {};
             a.w = (const uint8_t*)t->w;
-            a.sc = kind == kKindI4 ? (const uint32_t*)t->scales_dev : nullptr;
             a.i8_scale = t->i8_scale;
             a.row_ptr = kind == kKindI4 ? t->row_ptr : nullptr;
             a.ent = t->entries;

@@ -326,11 +326,9 @@ int pox::upload_tensor_locked(pox_cuda_ctx* ctx, const pox_tensor_desc* d, pox_t
             CKF(launch_repack(kKindI4, (const uint8_t*)tmp, (uint8_t*)t->w, N, K, st), "repack_i4");
             CKF(cudaMalloc(&tmp_s, sbytes), "cudaMalloc(raw scales)");
             CKF(cudaMemcpyAsync(tmp_s, d->scales, sbytes, cudaMemcpyHostToDevice, st), "cudaMemcpy(scales)");
-            CKF(cudaMalloc(&t->scales_dev, TL.scale_words() * 4), "cudaMalloc(scale words)");
-            CKF(launch_repack_i4_scales((const uint8_t*)tmp_s, (uint32_t*)t->scales_dev, N, K, (int)d->group_size,
-                                        st),
+            CKF(launch_repack_i4_scales((const uint8_t*)tmp_s, (uint8_t*)t->w, N, K, (int)d->group_size, st),
                 "repack_i4_scales");
-            t->bytes += TL.bytes() + TL.scale_words() * 4;
+            t->bytes += TL.bytes();
         } else {
             t->w = tmp;
             tmp = nullptr;
@@ -462,7 +460,6 @@ int pox::gemv_launch(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x, siz
             if (e != cudaSuccess) return cuda_error(e, "x preparation launch");
             GemvArgs a = {};
             a.w = (const uint8_t*)t->w;
-            a.sc = kind == kKindI4 ? (const uint32_t*)t->scales_dev : nullptr;
             a.i8_scale = t->i8_scale;
             a.row_ptr = kind == kKindI4 ? t->row_ptr : nullptr;
             a.ent = t->entries;

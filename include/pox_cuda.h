@@ -149,12 +149,78 @@ int pox_cuda_tensor_gemv_host(pox_cuda_ctx* ctx, const pox_tensor* t, const floa
  * before any stream capture. */
 int pox_cuda_tensor_gemv_noalloc(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x_dev, size_t batch,
                                  float* y_dev, void* stream);
+/* Operation fused into a GEMV's input (the decode step's RMSNorm before q/k/v and gate/up,
+ * engine.rs:294-350, and SwiGLU before down, engine.rs:671-677). Row b of the GEMV input is
+ *   POX_OP_NONE:   x[b * ld_x + k]
+ *   POX_OP_RMSNORM: x[b * ld_x + k] * (1 / sqrt(sum_k x^2 / cols + eps)) * f16 norm_w[k] (norm_w may be NULL)
+ *   POX_OP_SWIGLU:  g / (1 + exp(-g)) * up[b * ld_up + k] with g = x[b * ld_x + k]
+ * ld_x / ld_up of 0 mean cols. norm_w and up are device pointers. */
+typedef enum { POX_OP_NONE = 0, POX_OP_RMSNORM = 1, POX_OP_SWIGLU = 2 } pox_gemv_op_mode;
+typedef struct {
+    int mode;
+    const uint16_t* norm_w;
+    float eps;
+    const float* up;
+    uint32_t ld_x, ld_up;
+} pox_gemv_op;
+/* y = op(x) W^T (+ resid when resid_dev is non-NULL; resid may alias y), on device pointers,
+ * asynchronous on `stream`. Tensors in the tiled layout only (INT4 with cols and group size
+ * multiples of 128, INT8 with cols % 64 == 0, F16 with cols % 32 == 0); otherwise
+ * POX_ERR_UNSUPPORTED. */
+int pox_cuda_tensor_gemv_ex(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x_dev, size_t batch, float* y_dev,
+                            const pox_gemv_op* op, const float* resid_dev, void* stream);
 /* Dequantizes a resident tensor into out_dev ([rows][cols] f32, device), bit-exact with
  * dequantize_int4_group / dequantize_int8_symmetric (kernels.rs:85-128,157-173) followed by
  * SparseOutlierTable::apply_to (outlier.rs:88-95). Asynchronous on `stream`. */
 int pox_cuda_tensor_dequant(pox_cuda_ctx* ctx, const pox_tensor* t, float* out_dev, void* stream);
 /* Host-output variant of pox_cuda_tensor_dequant, synchronous; out holds rows*cols floats. */
 int pox_cuda_tensor_dequant_host(pox_cuda_ctx* ctx, const pox_tensor* t, float* out);
+
+/* ---- decode step of a Llama-architecture model ------------------------------------------- */
+
+/* ModelConfig fields the decode path uses (crates/paraoxidizer-core/src/arch.rs:96-112;
+ * head_dim = hidden / heads, arch.rs:135-137). */
+typedef struct {
+    uint32_t hidden, intermediate, layers, heads, kv_heads, vocab;
+    float rms_eps, rope_theta;
+} pox_llama_config;
+
+typedef struct pox_model pox_model;
+
+/* A model on the context's device with a paged fp16 KV cache of kv_blocks pages of 16 tokens
+ * (the page size of crates/paraoxidizer-runtime/src/paged_cache.rs:4) for up to max_batch
+ * sequences of up to max_blocks_per_seq pages each. Replaces the engine state of PoxEngine
+ * (engine.rs:86-104) plus its contiguous f32 KvCache (engine.rs:10-84). */
+int pox_cuda_model_create(pox_cuda_ctx* ctx, const pox_llama_config* cfg, uint32_t max_batch, uint32_t kv_blocks,
+                          uint32_t max_blocks_per_seq, pox_model** out);
+void pox_cuda_model_destroy(pox_model* m);
+/* model.embed_tokens.weight, model.norm.weight, lm_head.weight as f16 (.pox F16 payloads):
+ * [vocab][hidden], [hidden], [vocab][hidden]. */
+int pox_cuda_model_set_embeddings(pox_model* m, const uint16_t* embed, const uint16_t* final_norm,
+                                  const uint16_t* lm_head);
+/* Layer `layer`: proj[7] = q, k, v, o, gate, up, down projections (INT4 .pox tensors, optional
+ * outlier tables), input_layernorm and post_attention_layernorm weights as f16 [hidden]. q/k/v and
+ * gate/up are concatenated into one resident tensor each. */
+int pox_cuda_model_set_layer(pox_model* m, uint32_t layer, const pox_tensor_desc* proj, const uint16_t* attn_norm,
+                             const uint16_t* mlp_norm);
+/* One decode step for `batch` sequences (engine.rs:411-716 forward_token, batched): row b feeds
+ * tokens[b] at positions[b], its KV pages listed in block_tables[b * max_blocks_per_seq + j]
+ * (page j holds positions 16 j .. 16 j + 15; paged_cache.rs:149-162). logits [batch][vocab]
+ * (non-finite -> 0, engine.rs:709-713) and the greedy next tokens (sampler.rs:55-65) are written
+ * to host memory when non-NULL. Synchronous. */
+int pox_cuda_model_decode(pox_model* m, uint32_t batch, const uint32_t* tokens, const uint32_t* positions,
+                          const int32_t* block_tables, float* logits, uint32_t* next_tokens);
+/* Device-pointer variant, asynchronous on `stream` (NULL: the context's stream). NULL inputs keep
+ * the model's current device buffers (pox_cuda_model_buffers); advance != 0 then feeds the greedy
+ * tokens back and increments the positions on the device, so consecutive calls decode greedily. */
+int pox_cuda_model_decode_device(pox_model* m, uint32_t batch, const uint32_t* tokens_dev,
+                                 const uint32_t* positions_dev, const int32_t* block_tables_dev, float* logits_dev,
+                                 uint32_t* next_dev, int advance, void* stream);
+/* The model's device buffers (any out pointer may be NULL): tokens [max_batch], positions
+ * [max_batch], block tables [max_batch][max_blocks_per_seq], logits [max_batch][vocab], next
+ * tokens [max_batch]. */
+int pox_cuda_model_buffers(pox_model* m, uint32_t** tokens_dev, uint32_t** positions_dev, int32_t** block_tables_dev,
+                           float** logits_dev, uint32_t** next_dev);
 
 #ifdef __cplusplus
 }

@@ -43,6 +43,24 @@ class TensorDesc(C.Structure):
                 ("outliers", C.c_void_p), ("outlier_len", C.c_size_t)]
 
 
+class GemvOp(C.Structure):
+    """pox_gemv_op (include/pox_cuda.h): RMSNorm / SwiGLU fused into a GEMV's input."""
+
+    _fields_ = [("mode", C.c_int), ("norm_w", C.c_void_p), ("eps", C.c_float), ("up", C.c_void_p),
+                ("ld_x", C.c_uint32), ("ld_up", C.c_uint32)]
+
+
+POX_OP_NONE, POX_OP_RMSNORM, POX_OP_SWIGLU = 0, 1, 2
+
+
+class LlamaConfig(C.Structure):
+    """pox_llama_config (include/pox_cuda.h): ModelConfig fields of the decode path
+    (crates/paraoxidizer-core/src/arch.rs:96-112)."""
+
+    _fields_ = [("hidden", C.c_uint32), ("intermediate", C.c_uint32), ("layers", C.c_uint32), ("heads", C.c_uint32),
+                ("kv_heads", C.c_uint32), ("vocab", C.c_uint32), ("rms_eps", C.c_float), ("rope_theta", C.c_float)]
+
+
 _lib = None
 
 
@@ -55,7 +73,7 @@ def declared_symbols() -> list[str]:
 
 
 def _declare(L):
-    vp, sz, i32 = C.c_void_p, C.c_size_t, C.c_int
+    vp, sz, i32, u32 = C.c_void_p, C.c_size_t, C.c_int, C.c_uint32
     sig = {
         "pox_cuda_last_error": (C.c_char_p, []),
         "pox_cuda_version": (C.c_char_p, []),
@@ -73,6 +91,15 @@ def _declare(L):
         "pox_cuda_tensor_gemv": (i32, [vp, vp, vp, sz, vp, vp]),
         "pox_cuda_tensor_gemv_host": (i32, [vp, vp, vp, sz, vp]),
         "pox_cuda_tensor_gemv_noalloc": (i32, [vp, vp, vp, sz, vp, vp]),
+        "pox_cuda_tensor_gemv_ex": (i32, [vp, vp, vp, sz, vp, C.POINTER(GemvOp), vp, vp]),
+        "pox_cuda_model_create": (i32, [vp, C.POINTER(LlamaConfig), u32, u32, u32, C.POINTER(vp)]),
+        "pox_cuda_model_destroy": (None, [vp]),
+        "pox_cuda_model_set_embeddings": (i32, [vp, vp, vp, vp]),
+        "pox_cuda_model_set_layer": (i32, [vp, u32, C.POINTER(TensorDesc), vp, vp]),
+        "pox_cuda_model_decode": (i32, [vp, u32, vp, vp, vp, vp, vp]),
+        "pox_cuda_model_decode_device": (i32, [vp, u32, vp, vp, vp, vp, vp, i32, vp]),
+        "pox_cuda_model_buffers": (i32, [vp, C.POINTER(vp), C.POINTER(vp), C.POINTER(vp), C.POINTER(vp),
+                                         C.POINTER(vp)]),
         "pox_cuda_tensor_dequant": (i32, [vp, vp, vp, vp]),
         "pox_cuda_tensor_dequant_host": (i32, [vp, vp, vp]),
     }

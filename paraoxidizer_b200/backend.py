@@ -87,6 +87,7 @@ class CudaBackend:
     def __init__(self, ctx: int, device: int):
         self.ctx = ctx
         self.device = device
+        self._children = []  # weak references to CudaModel objects (destroyed with the context)
 
     @staticmethod
     def new(device: int = 0) -> Optional["CudaBackend"]:
@@ -106,6 +107,11 @@ class CudaBackend:
 
     def close(self) -> None:
         if self.ctx:
+            for ref in self._children:  # pox_cuda_destroy frees the models still on the context
+                child = ref()
+                if child is not None:
+                    child.handle = None
+            self._children.clear()
             L.lib().pox_cuda_destroy(self.ctx)
             self.ctx = None
 

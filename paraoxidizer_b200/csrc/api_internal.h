@@ -45,7 +45,7 @@ struct pox_cuda_ctx {
     size_t scratch_y_bytes = 0;
     int* err_host = nullptr;  // kernel error flag (host-mapped); nonzero = a bounded wait expired
     int* err_dev = nullptr;
-    void* extras = nullptr;  // owned by other translation units (decode engine state)
+    std::vector<pox_model*> models;  // decode models created on this context (destroyed with it)
 };
 
 namespace pox {
@@ -53,7 +53,11 @@ int set_error(int code, const char* fmt, ...);
 int cuda_error(cudaError_t e, const char* what);
 int ensure_scratch(pox_cuda_ctx* ctx, size_t xbytes, size_t ybytes);
 int upload_tensor_locked(pox_cuda_ctx* ctx, const pox_tensor_desc* d, pox_tensor** out, bool keep);
-int gemv_launch(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x, size_t batch, float* y, cudaStream_t st);
+struct PrepOp;
+// GEMV of a resident tensor on device pointers; op fuses RMSNorm / SwiGLU into the x preparation
+// and resid (same shape as y, may alias it) is added to the result (tiled tensors only).
+int gemv_launch(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x, size_t batch, float* y, cudaStream_t st,
+                const PrepOp* op = nullptr, const float* resid = nullptr);
 void destroy_ctx_extras(pox_cuda_ctx* ctx);
 // After a synchronize: turns a raised kernel error flag into POX_ERR_TIMEOUT (and clears it).
 int take_kernel_error(pox_cuda_ctx* ctx);

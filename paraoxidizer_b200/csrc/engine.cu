@@ -1,6 +1,732 @@
-// engine.cu -- decode-step state owned by a context (paged KV cache, model, tensor parallel).
+// engine.cu -- one decode step of a Llama-architecture model on B200 (sm_100a): the CUDA
+// counterpart of PoxEngine::forward_token (crates/paraoxidizer-runtime/src/engine.rs:411-716) for a
+// batch of sequences, with the KV cache in fp16 pages of 16 tokens addressed through per-sequence
+// block tables (the block-table semantics of crates/paraoxidizer-runtime/src/paged_cache.rs:149-162).
+//
+// Per layer: 4 GEMV launches on resident re-tiled weights (QKV and gate/up are concatenated at
+// load, so every projection row is computed exactly as in the separate tensors):
+//   qkv  = W_qkv  rmsnorm(x, attn_norm)            (norm fused into the GEMV's x preparation)
+//   rope(q, k); k, v -> KV pages at pos             (rope_append_kernel)
+//   att  = paged GQA attention over 0..=pos          (attn_split_kernel + attn_combine_kernel)
+//   x   += W_o att                                   (residual fused into the GEMV epilogue)
+//   gu   = W_gu   rmsnorm(x, mlp_norm)
+//   x   += W_down silu(g) * u                        (SwiGLU fused into the x preparation)
+// then logits = W_head rmsnorm(x, final_norm) (F16 GEMV), non-finite logits -> 0, greedy argmax.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstring>
+#include <vector>
+
+#include "../../include/pox_cuda.h"
 #include "api_internal.h"
+#include "common.cuh"
+#include "gemv.cuh"
 
 namespace pox {
-void destroy_ctx_extras(pox_cuda_ctx* ctx) { (void)ctx; }
+
+constexpr int kPage = 16;       // tokens per KV page (paged_cache.rs DEFAULT_BLOCK_SIZE)
+constexpr int kSplitTok = 128;  // context tokens per attention CTA
+
+struct LayerW {
+    pox_tensor* qkv = nullptr;
+    pox_tensor* o = nullptr;
+    pox_tensor* gu = nullptr;
+    pox_tensor* down = nullptr;
+    uint16_t* attn_norm = nullptr;
+    uint16_t* mlp_norm = nullptr;
+};
+
 }  // namespace pox
+
+struct pox_model {
+    pox_cuda_ctx* ctx = nullptr;
+    pox_llama_config cfg{};
+    int H = 0, I = 0, V = 0, L = 0, nq = 0, nkv = 0, hd = 0, G = 0, qkv_rows = 0;
+    uint32_t max_batch = 0, kv_blocks = 0, max_blocks_per_seq = 0;
+    uint16_t* embed = nullptr;
+    uint16_t* final_norm = nullptr;
+    pox_tensor* lm_head = nullptr;
+    std::vector<pox::LayerW> layers;
+    __half* kc = nullptr;  // [kv_blocks][L][nkv][16][hd]
+    __half* vc = nullptr;
+    float* x = nullptr;       // [B][H] residual stream
+    float* qkv = nullptr;     // [B][qkv_rows]
+    float* att = nullptr;     // [B][nq * hd]
+    float* gu = nullptr;      // [B][2 I]
+    float* logits = nullptr;  // [B][V]
+    float* apart = nullptr;   // [B][nkv][max_splits][G][hd + 2]
+    uint32_t* tok = nullptr;  // [B]
+    uint32_t* pos = nullptr;  // [B]
+    uint32_t* next = nullptr; // [B]
+    int32_t* btab = nullptr;  // [B][max_blocks_per_seq]
+    int max_splits = 0;
+};
+
+namespace pox {
+
+// ---- embedding (engine.rs:420-524): f16 row of token % vocab; a row with no |x| > 1e-6 becomes
+// sin(tok * 0.17) * 0.1 everywhere ----
+__global__ void embed_kernel(const uint32_t* __restrict__ tokens, const uint16_t* __restrict__ embed, int V, int H,
+                             float* __restrict__ x) {
+    const int b = blockIdx.x;
+    const uint32_t tok = tokens[b] % (uint32_t)V;
+    const uint16_t* row = embed + (size_t)tok * H;
+    float* xr = x + (size_t)b * H;
+    int sig = 0;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) {
+        const float v = half_bits_to_float(row[i]);
+        xr[i] = v;
+        sig |= fabsf(v) > 1e-6f;
+    }
+    if (!__syncthreads_or(sig)) {
+        const float val = __fmul_rn(sinf(__fmul_rn((float)tok, 0.17f)), 0.1f);
+        for (int i = threadIdx.x; i < H; i += blockDim.x) xr[i] = val;
+    }
+}
+
+// ---- RoPE (engine.rs:353-408, interleaved pairs) on q and k in place, then k and v into the KV
+// page of position pos (block_table[pos / 16], slot pos % 16) ----
+__global__ void rope_append_kernel(float* __restrict__ qkv, int qkv_rows, const uint32_t* __restrict__ pos,
+                                   const int32_t* __restrict__ btab, int mbps, __half* __restrict__ kc,
+                                   __half* __restrict__ vc, int layer, int L, int nq, int nkv, int hd, float theta) {
+    const int b = blockIdx.y, h = blockIdx.x;  // h < nq: q head; nq <= h < nq + nkv: kv head
+    const int i = threadIdx.x;                 // pair index < hd / 2
+    const uint32_t p = pos[b];
+    float* row = qkv + (size_t)b * qkv_rows;
+    const float th = fmaxf(theta, 1.0f);
+    const float exponent = __fdiv_rn((float)(2 * i), (float)hd);
+    const float freq = __fdiv_rn(1.0f, powf(th, exponent));
+    const float angle = __fmul_rn((float)p, freq);
+    float c = 1.0f, s = 0.0f;
+    if (isfinite(angle)) {
+        c = cosf(angle);
+        s = sinf(angle);
+    }
+    float* v = row + (size_t)h * hd;  // q heads, then k heads (k follows q in the fused projection)
+    const float a0 = v[2 * i], a1 = v[2 * i + 1];
+    const float r0 = __fsub_rn(__fmul_rn(a0, c), __fmul_rn(a1, s));
+    const float r1 = __fadd_rn(__fmul_rn(a0, s), __fmul_rn(a1, c));
+    v[2 * i] = r0;
+    v[2 * i + 1] = r1;
+    if (h >= nq) {
+        const int hk = h - nq;
+        const int blk = btab[(size_t)b * mbps + p / kPage];
+        const size_t off = ((((size_t)blk * L + layer) * nkv + hk) * kPage + p % kPage) * hd;
+        kc[off + 2 * i] = __float2half_rn(r0);
+        kc[off + 2 * i + 1] = __float2half_rn(r1);
+        const float* vv = row + (size_t)(nq + nkv + hk) * hd;
+        vc[off + 2 * i] = __float2half_rn(vv[2 * i]);
+        vc[off + 2 * i + 1] = __float2half_rn(vv[2 * i + 1]);
+    }
+}
+
+// ---- paged GQA decode attention (engine.rs:580-641), split over the context ----
+// CTA (split, kv head, batch row): tokens [split * 128, min(ctx, +128)) for the G query heads of
+// this kv head. Scores: one token per lane (its K row read from the page), dot products against
+// q in shared memory; softmax partial over the split; V accumulation: one token at a time, dims
+// spread over lanes. Writes (max, sum, acc[hd]) per query head for the combine kernel.
+template <int HD>
+__global__ void __launch_bounds__(128) attn_split_kernel(const float* __restrict__ qkv, int qkv_rows,
+                                                         const uint32_t* __restrict__ pos,
+                                                         const int32_t* __restrict__ btab, int mbps,
+                                                         const __half* __restrict__ kc, const __half* __restrict__ vc,
+                                                         int layer, int L, int nq, int nkv, int G, int max_splits,
+                                                         float* __restrict__ apart) {
+    constexpr int DPL = HD / 32;  // dims per lane
+    const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const int ctx = (int)pos[b] + 1;
+    const int t0 = split * kSplitTok;
+    if (t0 >= ctx) return;  // the combine kernel reads only ceil(ctx / 128) splits
+    const int t1 = min(ctx, t0 + kSplitTok);
+    const int nt = t1 - t0;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    __shared__ float qs[8][HD];
+    __shared__ float ps[8][kSplitTok];
+    __shared__ float red[4][8];
+    __shared__ float acc_s[4][8][HD];
+    const float scale = 1.0f / sqrtf(fmaxf((float)HD, 1.0f));
+    const float* qrow = qkv + (size_t)b * qkv_rows + (size_t)h * G * HD;
+    for (int i = tid; i < G * HD; i += 128) qs[i / HD][i % HD] = qrow[i];
+    __syncthreads();
+
+    // scores: token t0 + tid (128 threads = 128 tokens)
+    float sc[8];
+#pragma unroll
+    for (int g = 0; g < 8; g++) sc[g] = -INFINITY;
+    if (tid < nt) {
+        const int t = t0 + tid;
+        const int blk = btab[(size_t)b * mbps + t / kPage];
+        const __half* kr = kc + ((((size_t)blk * L + layer) * nkv + h) * kPage + t % kPage) * HD;
+        float dot[8];
+#pragma unroll
+        for (int g = 0; g < 8; g++) dot[g] = 0.f;
+#pragma unroll 4
+        for (int d0 = 0; d0 < HD; d0 += 8) {
+            const uint4 raw = *reinterpret_cast<const uint4*>(kr + d0);
+            const __half2* hp = reinterpret_cast<const __half2*>(&raw);
+            float kf[8];
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const float2 f = __half22float2(hp[j]);
+                kf[2 * j] = f.x;
+                kf[2 * j + 1] = f.y;
+            }
+#pragma unroll
+            for (int g = 0; g < 8; g++) {
+                if (g < G) {
+#pragma unroll
+                    for (int j = 0; j < 8; j++) dot[g] = fmaf(qs[g][d0 + j], kf[j], dot[g]);
+                }
+            }
+        }
+#pragma unroll
+        for (int g = 0; g < 8; g++) sc[g] = dot[g] * scale;
+    }
+    // softmax partial: max and exp over the split
+    float mx[8];
+#pragma unroll
+    for (int g = 0; g < 8; g++) {
+        float m = sc[g];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (lane == 0) red[warp][g] = m;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int g = 0; g < 8; g++) {
+        mx[g] = fmaxf(fmaxf(red[0][g], red[1][g]), fmaxf(red[2][g], red[3][g]));
+        if (!isfinite(mx[g])) mx[g] = 0.f;
+    }
+    __syncthreads();
+    float l[8];
+#pragma unroll
+    for (int g = 0; g < 8; g++) {
+        float p = 0.f;
+        if (tid < nt && g < G) {
+            p = expf(sc[g] - mx[g]);
+            if (!isfinite(p)) p = 0.f;
+            ps[g][tid] = p;
+        }
+        l[g] = warp_sum(p);
+        if (lane == 0) red[warp][g] = l[g];
+    }
+    __syncthreads();
+    // V accumulation: warp w takes tokens w, w + 4, ...; lane holds dims DPL * lane .. + DPL
+    float acc[8][DPL];
+#pragma unroll
+    for (int g = 0; g < 8; g++)
+#pragma unroll
+        for (int j = 0; j < DPL; j++) acc[g][j] = 0.f;
+    for (int j = warp; j < nt; j += 4) {
+        const int t = t0 + j;
+        const int blk = btab[(size_t)b * mbps + t / kPage];
+        const __half* vr = vc + ((((size_t)blk * L + layer) * nkv + h) * kPage + t % kPage) * HD + DPL * lane;
+        float vf[DPL];
+        if constexpr (DPL == 4) {
+            const uint2 raw = *reinterpret_cast<const uint2*>(vr);
+            const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+            const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+            vf[0] = f0.x;
+            vf[1] = f0.y;
+            vf[2] = f1.x;
+            vf[3] = f1.y;
+        } else if constexpr (DPL == 2) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(vr));
+            vf[0] = f.x;
+            vf[1] = f.y;
+        } else {
+            vf[0] = __half2float(vr[0]);
+        }
+#pragma unroll
+        for (int g = 0; g < 8; g++) {
+            if (g < G) {
+                const float p = ps[g][j];
+#pragma unroll
+                for (int q = 0; q < DPL; q++) acc[g][q] = fmaf(p, vf[q], acc[g][q]);
+            }
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < 8; g++)
+        if (g < G)
+#pragma unroll
+            for (int q = 0; q < DPL; q++) acc_s[warp][g][DPL * lane + q] = acc[g][q];
+    __syncthreads();
+    float* out = apart + ((((size_t)b * nkv + h) * max_splits + split) * G) * (HD + 2);
+    for (int i = tid; i < G * HD; i += 128) {
+        const int g = i / HD, d = i % HD;
+        out[(size_t)g * (HD + 2) + 2 + d] = (acc_s[0][g][d] + acc_s[1][g][d]) + (acc_s[2][g][d] + acc_s[3][g][d]);
+    }
+    if (tid < G) {
+        out[(size_t)tid * (HD + 2)] = mx[tid];
+        out[(size_t)tid * (HD + 2) + 1] = (red[0][tid] + red[1][tid]) + (red[2][tid] + red[3][tid]);
+    }
+}
+
+// Combines the splits of one (batch row, query head): out = sum_s e^(m_s - M) acc_s / sum_s e^(m_s - M) l_s
+// (the reference's 1 / sum_exp, 0 when the sum is <= 1e-9).
+__global__ void attn_combine_kernel(const uint32_t* __restrict__ pos, int nq, int nkv, int G, int hd, int max_splits,
+                                    const float* __restrict__ apart, float* __restrict__ att) {
+    const int hq = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+    const int ns = ((int)pos[b] + 1 + kSplitTok - 1) / kSplitTok;
+    const int h = hq / G, g = hq % G;
+    const float* base = apart + (((size_t)b * nkv + h) * max_splits * G + g) * (hd + 2);
+    const size_t sstride = (size_t)G * (hd + 2);
+    float M = -INFINITY;
+    for (int s = 0; s < ns; s++) M = fmaxf(M, base[s * sstride]);
+    float num = 0.f, den = 0.f;
+    for (int s = 0; s < ns; s++) {
+        const float* ps = base + s * sstride;
+        const float w = expf(ps[0] - M);
+        den = fmaf(w, ps[1], den);
+        if (d < hd) num = fmaf(w, ps[2 + d], num);
+    }
+    const float inv = den > 1e-9f ? 1.0f / den : 0.f;
+    if (d < hd) att[((size_t)b * nq + hq) * hd + d] = num * inv;
+}
+
+// Non-finite logits -> 0 (engine.rs:709-713), then greedy argmax: the first index of the maximum
+// (sampler.rs:55-65, strict >).
+__global__ void __launch_bounds__(1024) argmax_kernel(float* __restrict__ logits, int V, uint32_t* __restrict__ next) {
+    const int b = blockIdx.x;
+    float* lr = logits + (size_t)b * V;
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+        float v = lr[i];
+        if (!isfinite(v)) {
+            v = 0.f;
+            lr[i] = 0.f;
+        }
+        if (v > bv) {
+            bv = v;
+            bi = i;
+        }
+    }
+    __shared__ float sv[32];
+    __shared__ int si[32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) {
+            bv = ov;
+            bi = oi;
+        }
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) {
+        sv[warp] = bv;
+        si[warp] = bi;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        const int nw = blockDim.x >> 5;
+        bv = lane < nw ? sv[lane] : -INFINITY;
+        bi = lane < nw ? si[lane] : 0x7fffffff;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if (lane == 0) next[b] = bi == 0x7fffffff ? 0u : (uint32_t)bi;
+    }
+}
+
+// Feeds the greedy tokens back and advances the positions (a self-contained multi-step loop).
+__global__ void advance_kernel(uint32_t* tok, uint32_t* pos, const uint32_t* next, int B) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b < B) {
+        tok[b] = next[b];
+        pos[b] += 1;
+    }
+}
+
+static void destroy_model(pox_model* m);
+
+// Destroys the models still registered on a context that is being destroyed.
+void destroy_ctx_extras(pox_cuda_ctx* ctx) {
+    std::vector<pox_model*> ms;
+    {
+        std::lock_guard<std::mutex> lk(ctx->mu);
+        ms.swap(ctx->models);
+    }
+    for (pox_model* m : ms) destroy_model(m);
+}
+
+static int check_launch(const char* what) {
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? POX_OK : cuda_error(e, what);
+}
+
+// Concatenates INT4 projections with equal cols / group size row-wise (.pox payloads are row
+// major, so the bytes concatenate; outlier flat indices shift by the rows before them).
+static int concat_i4(const pox_tensor_desc* parts, int n, std::vector<uint8_t>& data, std::vector<uint8_t>& scales,
+                     std::vector<uint8_t>& outl, pox_tensor_desc* out) {
+    size_t rows = 0;
+    std::vector<uint32_t> idx;
+    std::vector<uint16_t> val;
+    data.clear();
+    scales.clear();
+    for (int i = 0; i < n; i++) {
+        const pox_tensor_desc& d = parts[i];
+        if (d.dtype != POX_I4 || d.cols != parts[0].cols || d.group_size != parts[0].group_size)
+            return set_error(POX_ERR_UNSUPPORTED, "model projections must be INT4 with one cols / group size");
+        const size_t rb = (d.cols + 1) / 2, sb = (d.cols + d.group_size - 1) / d.group_size * 4;
+        if (!d.data || d.data_len < d.rows * rb || !d.scales || d.scale_len < d.rows * sb)
+            return set_error(POX_ERR_LAYOUT, "projection %d: buffer layout incompatible with 2D GEMV", i);
+        data.insert(data.end(), d.data, d.data + d.rows * rb);
+        scales.insert(scales.end(), d.scales, d.scales + d.rows * sb);
+        if (d.outliers && d.outlier_len >= 4) {
+            uint32_t cnt;
+            std::memcpy(&cnt, d.outliers, 4);
+            if (4 + 6 * (size_t)cnt > d.outlier_len) return set_error(POX_ERR_LAYOUT, "outlier table truncated");
+            for (uint32_t e = 0; e < cnt; e++) {
+                uint32_t fi;
+                uint16_t fv;
+                std::memcpy(&fi, d.outliers + 4 + 4 * (size_t)e, 4);
+                std::memcpy(&fv, d.outliers + 4 + 4 * (size_t)cnt + 2 * (size_t)e, 2);
+                if ((uint64_t)fi >= (uint64_t)d.rows * d.cols) continue;  // never matches a row
+                idx.push_back((uint32_t)(fi + rows * d.cols));
+                val.push_back(fv);
+            }
+        }
+        rows += d.rows;
+    }
+    outl.clear();
+    if (!idx.empty()) {
+        const uint32_t cnt = (uint32_t)idx.size();
+        outl.resize(4 + 6 * (size_t)cnt);
+        std::memcpy(outl.data(), &cnt, 4);
+        std::memcpy(outl.data() + 4, idx.data(), 4 * (size_t)cnt);
+        std::memcpy(outl.data() + 4 + 4 * (size_t)cnt, val.data(), 2 * (size_t)cnt);
+    }
+    *out = pox_tensor_desc{};
+    out->dtype = POX_I4;
+    out->rows = rows;
+    out->cols = parts[0].cols;
+    out->group_size = parts[0].group_size;
+    out->data = data.data();
+    out->data_len = data.size();
+    out->scales = scales.data();
+    out->scale_len = scales.size();
+    out->outliers = outl.empty() ? nullptr : outl.data();
+    out->outlier_len = outl.size();
+    return POX_OK;
+}
+
+static int upload_f16(const uint16_t* h, size_t n, uint16_t** d, cudaStream_t st) {
+    if (!h) return set_error(POX_ERR_INVALID, "f16 buffer is NULL");
+    cudaError_t e = cudaMalloc(d, n * 2);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(*d, h, n * 2, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    return e == cudaSuccess ? POX_OK : cuda_error(e, "f16 upload");
+}
+
+static void free_tensor(pox_cuda_ctx* ctx, pox_tensor*& t) {
+    if (t) pox_cuda_tensor_free(ctx, t);
+    t = nullptr;
+}
+
+// The decode step on device buffers already filled (m->tok, m->pos, m->btab).
+static int decode_step(pox_model* m, int B, cudaStream_t st) {
+    pox_cuda_ctx* ctx = m->ctx;
+    int rc;
+    embed_kernel<<<B, 256, 0, st>>>(m->tok, m->embed, m->V, m->H, m->x);
+    if ((rc = check_launch("embed"))) return rc;
+    PrepOp norm;
+    norm.mode = kPrepNorm;
+    norm.eps = m->cfg.rms_eps;
+    for (int l = 0; l < m->L; l++) {
+        const LayerW& w = m->layers[l];
+        if (!w.qkv) return set_error(POX_ERR_INVALID, "layer %d has no weights", l);
+        norm.norm_w = w.attn_norm;
+        if ((rc = gemv_launch(ctx, w.qkv, m->x, B, m->qkv, st, &norm))) return rc;
+        rope_append_kernel<<<dim3(m->nq + m->nkv, B), m->hd / 2, 0, st>>>(
+            m->qkv, m->qkv_rows, m->pos, m->btab, (int)m->max_blocks_per_seq, m->kc, m->vc, l, m->L, m->nq, m->nkv,
+            m->hd, m->cfg.rope_theta);
+        if ((rc = check_launch("rope_append"))) return rc;
+        const dim3 ag(m->max_splits, m->nkv, B);
+        if (m->hd == 128)
+            attn_split_kernel<128><<<ag, 128, 0, st>>>(m->qkv, m->qkv_rows, m->pos, m->btab, (int)m->max_blocks_per_seq,
+                                                      m->kc, m->vc, l, m->L, m->nq, m->nkv, m->G, m->max_splits,
+                                                      m->apart);
+        else if (m->hd == 64)
+            attn_split_kernel<64><<<ag, 128, 0, st>>>(m->qkv, m->qkv_rows, m->pos, m->btab, (int)m->max_blocks_per_seq,
+                                                     m->kc, m->vc, l, m->L, m->nq, m->nkv, m->G, m->max_splits,
+                                                     m->apart);
+        else
+            attn_split_kernel<32><<<ag, 128, 0, st>>>(m->qkv, m->qkv_rows, m->pos, m->btab, (int)m->max_blocks_per_seq,
+                                                     m->kc, m->vc, l, m->L, m->nq, m->nkv, m->G, m->max_splits,
+                                                     m->apart);
+        if ((rc = check_launch("attn_split"))) return rc;
+        attn_combine_kernel<<<dim3(m->nq, B), std::max(32, m->hd), 0, st>>>(m->pos, m->nq, m->nkv, m->G, m->hd,
+                                                                           m->max_splits, m->apart, m->att);
+        if ((rc = check_launch("attn_combine"))) return rc;
+        if ((rc = gemv_launch(ctx, w.o, m->att, B, m->x, st, nullptr, m->x))) return rc;
+        norm.norm_w = w.mlp_norm;
+        if ((rc = gemv_launch(ctx, w.gu, m->x, B, m->gu, st, &norm))) return rc;
+        PrepOp sw;
+        sw.mode = kPrepSwiGLU;
+        sw.up = m->gu + m->I;
+        sw.ld_x = 2 * m->I;
+        sw.ld_up = 2 * m->I;
+        if ((rc = gemv_launch(ctx, w.down, m->gu, B, m->x, st, &sw, m->x))) return rc;
+    }
+    norm.norm_w = m->final_norm;
+    if ((rc = gemv_launch(ctx, m->lm_head, m->x, B, m->logits, st, &norm))) return rc;
+    argmax_kernel<<<B, 1024, 0, st>>>(m->logits, m->V, m->next);
+    return check_launch("argmax");
+}
+
+}  // namespace pox
+
+using namespace pox;
+
+extern "C" int pox_cuda_model_create(pox_cuda_ctx* ctx, const pox_llama_config* cfg, uint32_t max_batch,
+                                     uint32_t kv_blocks, uint32_t max_blocks_per_seq, pox_model** out) {
+    if (!ctx || !cfg || !out) return set_error(POX_ERR_INVALID, "NULL argument");
+    *out = nullptr;
+    if (!cfg->hidden || !cfg->heads || !cfg->kv_heads || !cfg->layers || !cfg->vocab || !cfg->intermediate ||
+        !max_batch || !kv_blocks || !max_blocks_per_seq)
+        return set_error(POX_ERR_INVALID, "zero dimension in the model configuration");
+    if (cfg->hidden % cfg->heads || cfg->heads % cfg->kv_heads)
+        return set_error(POX_ERR_UNSUPPORTED, "hidden %% heads or heads %% kv_heads is not 0");
+    const uint32_t hd = cfg->hidden / cfg->heads, G = cfg->heads / cfg->kv_heads;
+    if ((hd != 32 && hd != 64 && hd != 128) || G > 8)
+        return set_error(POX_ERR_UNSUPPORTED, "head_dim %u / %u query heads per kv head not supported", hd, G);
+    if (cfg->hidden % 128 || cfg->intermediate % 128)
+        return set_error(POX_ERR_UNSUPPORTED, "hidden and intermediate must be multiples of 128");
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    cudaError_t e = cudaSetDevice(ctx->device);
+    if (e != cudaSuccess) return cuda_error(e, "cudaSetDevice");
+    auto* m = new pox_model();
+    m->ctx = ctx;
+    m->cfg = *cfg;
+    m->H = (int)cfg->hidden;
+    m->I = (int)cfg->intermediate;
+    m->V = (int)cfg->vocab;
+    m->L = (int)cfg->layers;
+    m->nq = (int)cfg->heads;
+    m->nkv = (int)cfg->kv_heads;
+    m->hd = (int)hd;
+    m->G = (int)G;
+    m->qkv_rows = (m->nq + 2 * m->nkv) * m->hd;
+    m->max_batch = max_batch;
+    m->kv_blocks = kv_blocks;
+    m->max_blocks_per_seq = max_blocks_per_seq;
+    m->max_splits = (int)((max_blocks_per_seq * kPage + kSplitTok - 1) / kSplitTok);
+    m->layers.resize(m->L);
+    const size_t B = max_batch;
+    const size_t kv_elems = (size_t)kv_blocks * m->L * m->nkv * kPage * m->hd;
+    struct A { void** p; size_t bytes; } allocs[] = {
+        {(void**)&m->kc, kv_elems * 2},
+        {(void**)&m->vc, kv_elems * 2},
+        {(void**)&m->x, B * m->H * 4},
+        {(void**)&m->qkv, B * m->qkv_rows * 4},
+        {(void**)&m->att, B * m->nq * m->hd * 4},
+        {(void**)&m->gu, B * 2 * m->I * 4},
+        {(void**)&m->logits, B * m->V * 4},
+        {(void**)&m->apart, B * m->nkv * m->max_splits * m->G * (m->hd + 2) * 4},
+        {(void**)&m->tok, B * 4},
+        {(void**)&m->pos, B * 4},
+        {(void**)&m->next, B * 4},
+        {(void**)&m->btab, B * max_blocks_per_seq * 4},
+    };
+    for (auto& a : allocs) {
+        e = cudaMalloc(a.p, a.bytes);
+        if (e != cudaSuccess) {
+            for (auto& f : allocs) cudaFree(*f.p);
+            delete m;
+            return cuda_error(e, "cudaMalloc(model buffers)");
+        }
+    }
+    cudaMemsetAsync(m->kc, 0, kv_elems * 2, ctx->stream);
+    cudaMemsetAsync(m->vc, 0, kv_elems * 2, ctx->stream);
+    e = cudaStreamSynchronize(ctx->stream);
+    if (e != cudaSuccess) return cuda_error(e, "cudaMemset(KV pages)");
+    ctx->models.push_back(m);
+    *out = m;
+    return POX_OK;
+}
+
+extern "C" void pox_cuda_model_destroy(pox_model* m) {
+    if (!m) return;
+    pox_cuda_ctx* ctx = m->ctx;
+    {
+        std::lock_guard<std::mutex> lk(ctx->mu);
+        auto it = std::find(ctx->models.begin(), ctx->models.end(), m);
+        if (it == ctx->models.end()) return;  // already destroyed with its context
+        ctx->models.erase(it);
+    }
+    pox::destroy_model(m);
+}
+
+namespace pox {
+static void destroy_model(pox_model* m) {
+    pox_cuda_ctx* ctx = m->ctx;
+    cudaSetDevice(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    for (auto& w : m->layers) {
+        free_tensor(ctx, w.qkv);
+        free_tensor(ctx, w.o);
+        free_tensor(ctx, w.gu);
+        free_tensor(ctx, w.down);
+        cudaFree(w.attn_norm);
+        cudaFree(w.mlp_norm);
+    }
+    free_tensor(ctx, m->lm_head);
+    void* bufs[] = {m->embed, m->final_norm, m->kc, m->vc, m->x, m->qkv, m->att, m->gu, m->logits, m->apart,
+                    m->tok, m->pos, m->next, m->btab};
+    for (void* p : bufs) cudaFree(p);
+    delete m;
+}
+}  // namespace pox
+
+extern "C" int pox_cuda_model_set_embeddings(pox_model* m, const uint16_t* embed, const uint16_t* final_norm,
+                                             const uint16_t* lm_head) {
+    if (!m) return set_error(POX_ERR_INVALID, "model is NULL");
+    pox_cuda_ctx* ctx = m->ctx;
+    cudaStream_t st = ctx->stream;
+    {
+        std::lock_guard<std::mutex> lk(ctx->mu);
+        cudaSetDevice(ctx->device);
+        cudaFree(m->embed);
+        cudaFree(m->final_norm);
+        m->embed = m->final_norm = nullptr;
+        int rc = upload_f16(embed, (size_t)m->V * m->H, &m->embed, st);
+        if (!rc) rc = upload_f16(final_norm, (size_t)m->H, &m->final_norm, st);
+        if (rc) return rc;
+    }
+    free_tensor(ctx, m->lm_head);
+    pox_tensor_desc d = {};
+    d.dtype = POX_F16;
+    d.rows = (size_t)m->V;
+    d.cols = (size_t)m->H;
+    d.data = reinterpret_cast<const uint8_t*>(lm_head);
+    d.data_len = (size_t)m->V * m->H * 2;
+    return pox_cuda_tensor_upload(ctx, &d, &m->lm_head);
+}
+
+extern "C" int pox_cuda_model_set_layer(pox_model* m, uint32_t layer, const pox_tensor_desc* proj,
+                                        const uint16_t* attn_norm, const uint16_t* mlp_norm) {
+    if (!m || !proj) return set_error(POX_ERR_INVALID, "NULL argument");
+    if (layer >= (uint32_t)m->L) return set_error(POX_ERR_INVALID, "layer %u out of range", layer);
+    const size_t H = m->H, I = m->I, qd = (size_t)m->nq * m->hd, kvd = (size_t)m->nkv * m->hd;
+    const size_t want[7][2] = {{qd, H}, {kvd, H}, {kvd, H}, {H, qd}, {I, H}, {I, H}, {H, I}};
+    for (int i = 0; i < 7; i++)
+        if (proj[i].rows != want[i][0] || proj[i].cols != want[i][1])
+            return set_error(POX_ERR_LAYOUT, "projection %d is %zux%zu, expected %zux%zu", i, proj[i].rows,
+                             proj[i].cols, want[i][0], want[i][1]);
+    pox_cuda_ctx* ctx = m->ctx;
+    LayerW& w = m->layers[layer];
+    free_tensor(ctx, w.qkv);
+    free_tensor(ctx, w.o);
+    free_tensor(ctx, w.gu);
+    free_tensor(ctx, w.down);
+    std::vector<uint8_t> d0, s0, o0;
+    pox_tensor_desc cat;
+    int rc = concat_i4(proj, 3, d0, s0, o0, &cat);
+    if (!rc) rc = pox_cuda_tensor_upload(ctx, &cat, &w.qkv);
+    if (!rc) rc = concat_i4(proj + 3, 1, d0, s0, o0, &cat);
+    if (!rc) rc = pox_cuda_tensor_upload(ctx, &cat, &w.o);
+    if (!rc) rc = concat_i4(proj + 4, 2, d0, s0, o0, &cat);
+    if (!rc) rc = pox_cuda_tensor_upload(ctx, &cat, &w.gu);
+    if (!rc) rc = concat_i4(proj + 6, 1, d0, s0, o0, &cat);
+    if (!rc) rc = pox_cuda_tensor_upload(ctx, &cat, &w.down);
+    if (rc) return rc;
+    for (pox_tensor* t : {w.qkv, w.o, w.gu, w.down})
+        if (!t->tiled) return set_error(POX_ERR_UNSUPPORTED, "projections need cols %% 128 == 0 and group size %% 128 == 0");
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    cudaSetDevice(ctx->device);
+    cudaFree(w.attn_norm);
+    cudaFree(w.mlp_norm);
+    w.attn_norm = w.mlp_norm = nullptr;
+    rc = upload_f16(attn_norm, H, &w.attn_norm, ctx->stream);
+    if (!rc) rc = upload_f16(mlp_norm, H, &w.mlp_norm, ctx->stream);
+    return rc;
+}
+
+extern "C" int pox_cuda_model_decode_device(pox_model* m, uint32_t batch, const uint32_t* tokens_dev,
+                                            const uint32_t* positions_dev, const int32_t* block_tables_dev,
+                                            float* logits_dev, uint32_t* next_dev, int advance, void* stream) {
+    if (!m) return set_error(POX_ERR_INVALID, "model is NULL");
+    if (batch == 0) return POX_OK;
+    if (batch > m->max_batch) return set_error(POX_ERR_INVALID, "batch %u > max_batch %u", batch, m->max_batch);
+    if (!m->embed || !m->lm_head) return set_error(POX_ERR_INVALID, "embeddings not set");
+    pox_cuda_ctx* ctx = m->ctx;
+    cudaError_t e = cudaSetDevice(ctx->device);
+    if (e != cudaSuccess) return cuda_error(e, "cudaSetDevice");
+    cudaStream_t st = stream ? (cudaStream_t)stream : ctx->stream;
+    const size_t B = batch;
+    if (tokens_dev && tokens_dev != m->tok)
+        cudaMemcpyAsync(m->tok, tokens_dev, B * 4, cudaMemcpyDeviceToDevice, st);
+    if (positions_dev && positions_dev != m->pos)
+        cudaMemcpyAsync(m->pos, positions_dev, B * 4, cudaMemcpyDeviceToDevice, st);
+    if (block_tables_dev && block_tables_dev != m->btab)
+        cudaMemcpyAsync(m->btab, block_tables_dev, B * m->max_blocks_per_seq * 4, cudaMemcpyDeviceToDevice, st);
+    int rc = decode_step(m, (int)batch, st);
+    if (rc) return rc;
+    if (logits_dev) cudaMemcpyAsync(logits_dev, m->logits, B * m->V * 4, cudaMemcpyDeviceToDevice, st);
+    if (next_dev) cudaMemcpyAsync(next_dev, m->next, B * 4, cudaMemcpyDeviceToDevice, st);
+    if (advance) {
+        advance_kernel<<<(batch + 127) / 128, 128, 0, st>>>(m->tok, m->pos, m->next, (int)batch);
+        if ((rc = check_launch("advance"))) return rc;
+    }
+    e = cudaGetLastError();
+    return e == cudaSuccess ? POX_OK : cuda_error(e, "decode step");
+}
+
+extern "C" int pox_cuda_model_decode(pox_model* m, uint32_t batch, const uint32_t* tokens, const uint32_t* positions,
+                                     const int32_t* block_tables, float* logits, uint32_t* next_tokens) {
+    if (!m) return set_error(POX_ERR_INVALID, "model is NULL");
+    if (batch == 0) return POX_OK;
+    if (!tokens || !positions || !block_tables) return set_error(POX_ERR_INVALID, "NULL input");
+    if (batch > m->max_batch) return set_error(POX_ERR_INVALID, "batch %u > max_batch %u", batch, m->max_batch);
+    for (uint32_t b = 0; b < batch; b++) {
+        const uint32_t nb = positions[b] / kPage + 1;
+        if (nb > m->max_blocks_per_seq)
+            return set_error(POX_ERR_OOM, "position %u needs %u KV blocks, max_blocks_per_seq is %u", positions[b], nb,
+                             m->max_blocks_per_seq);
+        for (uint32_t j = 0; j < nb; j++) {
+            const int32_t blk = block_tables[(size_t)b * m->max_blocks_per_seq + j];
+            if (blk < 0 || (uint32_t)blk >= m->kv_blocks)
+                return set_error(POX_ERR_INVALID, "block table entry %d of row %u out of range", blk, b);
+        }
+    }
+    pox_cuda_ctx* ctx = m->ctx;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    cudaError_t e = cudaSetDevice(ctx->device);
+    if (e != cudaSuccess) return cuda_error(e, "cudaSetDevice");
+    cudaStream_t st = ctx->stream;
+    const size_t B = batch;
+    e = cudaMemcpyAsync(m->tok, tokens, B * 4, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(m->pos, positions, B * 4, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(m->btab, block_tables, B * m->max_blocks_per_seq * 4, cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) return cuda_error(e, "cudaMemcpy(decode inputs)");
+    int rc = decode_step(m, (int)batch, st);
+    if (rc) return rc;
+    if (logits) e = cudaMemcpyAsync(logits, m->logits, B * m->V * 4, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess && next_tokens) e = cudaMemcpyAsync(next_tokens, m->next, B * 4, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return cuda_error(e, "decode step");
+    return take_kernel_error(ctx);
+}
+
+extern "C" int pox_cuda_model_buffers(pox_model* m, uint32_t** tokens_dev, uint32_t** positions_dev,
+                                      int32_t** block_tables_dev, float** logits_dev, uint32_t** next_dev) {
+    if (!m) return set_error(POX_ERR_INVALID, "model is NULL");
+    if (tokens_dev) *tokens_dev = m->tok;
+    if (positions_dev) *positions_dev = m->pos;
+    if (block_tables_dev) *block_tables_dev = m->btab;
+    if (logits_dev) *logits_dev = m->logits;
+    if (next_dev) *next_dev = m->next;
+    return POX_OK;
+}

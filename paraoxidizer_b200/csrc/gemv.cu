@@ -59,9 +59,45 @@ XPrep xprep_view(void* scratch, int kind, int K) {
 }
 
 
+// Element k of batch row b of the GEMV input, after the fused pre-op: x itself, RMSNorm
+// (crates/paraoxidizer-runtime/src/engine.rs:294-350: x * (1 / sqrt(sum x^2 / n + eps)) then * w),
+// or SwiGLU (engine.rs:671-677: g / (1 + exp(-g)) * u).
+struct PrepRow {
+    const float* x;
+    const float* up;
+    float inv;  // RMSNorm scale of this row
+};
+__device__ __forceinline__ float prep_elem(const PrepOp& op, const PrepRow& r, int k, float v) {
+    if (op.mode == kPrepNorm) {
+        const float t = v * r.inv;
+        return op.norm_w ? t * half_bits_to_float(op.norm_w[k]) : t;
+    }
+    if (op.mode == kPrepSwiGLU) {
+        const float u = r.up[k];
+        return v / (1.0f + expf(-v)) * u;
+    }
+    return v;
+}
+// Per-row RMSNorm scale, computed by a whole warp in a fixed order (every warp of the row gets the
+// same value): lane-sequential sums over k = 4 lane + 128 j, then a butterfly.
+__device__ __forceinline__ float row_rms_inv(const float* x, int K, float eps) {
+    const int lane = threadIdx.x & 31;
+    float s = 0.f;
+    for (int k = 4 * lane; k < K; k += 128) {
+        const float4 v = *reinterpret_cast<const float4*>(x + k);
+        s = fmaf(v.x, v.x, s);
+        s = fmaf(v.y, v.y, s);
+        s = fmaf(v.z, v.z, s);
+        s = fmaf(v.w, v.w, s);
+    }
+    s = warp_sum(s);
+    const float rms = sqrtf(s / (float)K + eps);
+    return 1.0f / rms;
+}
+
 // One warp per (batch row, 128-k block); lane l covers k = 4l .. 4l+3 of the block.
 __global__ void __launch_bounds__(256) xprep_int_kernel(const float* __restrict__ x, int B, int K, uint8_t* cols,
-                                                        float2* meta, int Kp, int nxb, int nxbs) {
+                                                        float2* meta, int Kp, int nxb, int nxbs, PrepOp op) {
     pdl_launch_dependents();
     pdl_wait();
     const int wid = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -69,8 +105,18 @@ __global__ void __launch_bounds__(256) xprep_int_kernel(const float* __restrict_
     if (wid >= B * nxb) return;
     const int b = wid / nxb, blk = wid % nxb;
     const int k = blk * kXBlock + lane * 4;
+    PrepRow r;
+    r.x = x + (size_t)b * op.ld_x;
+    r.up = op.up ? op.up + (size_t)b * op.ld_up : nullptr;
+    r.inv = op.mode == kPrepNorm ? row_rms_inv(r.x, K, op.eps) : 1.f;
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (k < K) v = *reinterpret_cast<const float4*>(x + (size_t)b * K + k);  // K % 4 == 0 on this path
+    if (k < K) {
+        v = *reinterpret_cast<const float4*>(r.x + k);  // K % 4 == 0 on this path
+        v.x = prep_elem(op, r, k, v.x);
+        v.y = prep_elem(op, r, k + 1, v.y);
+        v.z = prep_elem(op, r, k + 2, v.z);
+        v.w = prep_elem(op, r, k + 3, v.w);
+    }
     float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -90,24 +136,36 @@ __global__ void __launch_bounds__(256) xprep_int_kernel(const float* __restrict_
     if (lane == 0) meta[(size_t)b * nxbs + blk] = make_float2(m > 0.f ? m / (float)kXLimbMax : 0.f, s);
 }
 
-// One thread per 2 elements: hi = f16(x), lo = f16(x - hi).
+// One warp per (batch row, 64 elements); lane l covers 2 elements: hi = f16(x), lo = f16(x - hi).
 __global__ void __launch_bounds__(256) xprep_f16_kernel(const float* __restrict__ x, int B, int K, __half* cols,
-                                                        int Kp) {
+                                                        int Kp, PrepOp op) {
     pdl_launch_dependents();
     pdl_wait();
-    const int per = Kp / 2;
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= B * per) return;
-    const int b = i / per, k = (i % per) * 2;
+    const int per = Kp / 64;  // warps per row
+    const int wid = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (wid >= B * per) return;
+    const int b = wid / per, k = (wid % per) * 64 + 2 * lane;
+    PrepRow r;
+    r.x = x + (size_t)b * op.ld_x;
+    r.up = op.up ? op.up + (size_t)b * op.ld_up : nullptr;
+    r.inv = op.mode == kPrepNorm ? row_rms_inv(r.x, K, op.eps) : 1.f;
     float2 v = make_float2(0.f, 0.f);
-    if (k < K) v = *reinterpret_cast<const float2*>(x + (size_t)b * K + k);  // K % 32 == 0 on this path
+    if (k < K) {
+        v = *reinterpret_cast<const float2*>(r.x + k);  // K % 32 == 0 on this path
+        v.x = prep_elem(op, r, k, v.x);
+        v.y = prep_elem(op, r, k + 1, v.y);
+    }
     const __half h0 = __float2half_rn(v.x), h1 = __float2half_rn(v.y);
     const __half l0 = __float2half_rn(v.x - __half2float(h0)), l1 = __float2half_rn(v.y - __half2float(h1));
     *reinterpret_cast<__half2*>(cols + (size_t)(2 * b) * Kp + k) = __halves2half2(h0, h1);
     *reinterpret_cast<__half2*>(cols + (size_t)(2 * b + 1) * Kp + k) = __halves2half2(l0, l1);
 }
 
-cudaError_t launch_xprep(int kind, const float* x, int B, int K, const XPrep& xp, bool pdl, cudaStream_t st) {
+cudaError_t launch_xprep(int kind, const float* x, int B, int K, const XPrep& xp, const PrepOp& op_in, bool pdl,
+                         cudaStream_t st) {
+    PrepOp op = op_in;
+    if (op.ld_x == 0) op.ld_x = K;
     cudaLaunchConfig_t cfg = {};
     cfg.blockDim = dim3(256, 1, 1);
     cfg.stream = st;
@@ -117,13 +175,14 @@ cudaError_t launch_xprep(int kind, const float* x, int B, int K, const XPrep& xp
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
     if (kind == kKindF16) {
-        const int n = B * (xp.Kp / 2);
-        cfg.gridDim = dim3((n + 255) / 256, 1, 1);
-        return cudaLaunchKernelEx(&cfg, xprep_f16_kernel, x, B, K, (__half*)xp.cols, xp.Kp);
+        const int warps = B * (xp.Kp / 64);
+        cfg.gridDim = dim3((warps + 7) / 8, 1, 1);
+        return cudaLaunchKernelEx(&cfg, xprep_f16_kernel, x, B, K, (__half*)xp.cols, xp.Kp, op);
     }
     const int warps = B * xp.nxb;
     cfg.gridDim = dim3((warps + 7) / 8, 1, 1);
-    return cudaLaunchKernelEx(&cfg, xprep_int_kernel, x, B, K, (uint8_t*)xp.cols, xp.meta, xp.Kp, xp.nxb, xp.nxbs);
+    return cudaLaunchKernelEx(&cfg, xprep_int_kernel, x, B, K, (uint8_t*)xp.cols, xp.meta, xp.Kp, xp.nxb, xp.nxbs,
+                              op);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -477,13 +536,19 @@ __global__ void __launch_bounds__(512, 2) gemv_tc_kernel(const GemvArgs a) {
     const float oscale = KIND == kKindI8 ? a.i8_scale : 1.f;
     const int row = T * 16 + rr;
     if (S == 1) {
-        if (tid < 128 && bb < B && row < a.N) a.y[(size_t)bb * a.N + row] = p * oscale;
+        if (tid < 128 && bb < B && row < a.N) {
+            const size_t o = (size_t)bb * a.N + row;
+            a.y[o] = a.resid ? a.resid[o] + p * oscale : p * oscale;
+        }
     } else {
         if (tid < 128) part[tid] = p;
         cluster_sync_all();
         if (s == 0 && tid < 128 && bb < B) {
             for (int r = 1; r < S; r++) p += ld_dsmem_f32(part + tid, (uint32_t)r);
-            if (row < a.N) a.y[(size_t)bb * a.N + row] = p * oscale;
+            if (row < a.N) {
+                const size_t o = (size_t)bb * a.N + row;
+                a.y[o] = a.resid ? a.resid[o] + p * oscale : p * oscale;
+            }
         }
         cluster_sync_all();  // remote shared memory stays valid until rank 0 has read it
     }

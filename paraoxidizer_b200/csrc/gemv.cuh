@@ -57,6 +57,17 @@ struct XPrep {
     int Kp, nxb, nxbs;
 };
 
+// Operation fused into the x preparation of a GEMV (decode step): the GEMV input row b is
+// op(x + b * ld_x), element-wise after the row's RMSNorm scale where that applies.
+enum { kPrepNone = 0, kPrepNorm = 1, kPrepSwiGLU = 2 };
+struct PrepOp {
+    int mode = kPrepNone;
+    const uint16_t* norm_w = nullptr;  // kPrepNorm: [K] f16 weight (nullptr: none)
+    float eps = 1e-5f;                 // kPrepNorm
+    const float* up = nullptr;         // kPrepSwiGLU: up rows (x holds the gate rows)
+    int ld_x = 0, ld_up = 0;           // row strides in elements (0: K)
+};
+
 struct GemvArgs {
     const uint8_t* w;        // tile blobs (TileLayout)
     float i8_scale;          // INT8 per-tensor scale
@@ -66,6 +77,7 @@ struct GemvArgs {
     const float2* xm;        // prepared x meta
     const float* x;          // original x [B][K] f32 (outlier correction)
     float* y;                // [B][N]
+    const float* resid;      // nullptr, or [B][N] added to the result (y may alias it)
     int* err;                // kernel error flag (a bounded wait expired)
     int N, K, Kp, B, nxb, nxbs;
     int nT, nkb, S;          // row tiles, k-blocks, k-splits (cluster size)
@@ -75,7 +87,8 @@ struct GemvArgs {
 size_t xprep_bytes(int kind, int K);
 XPrep xprep_view(void* scratch, int kind, int K);
 
-cudaError_t launch_xprep(int kind, const float* x, int B, int K, const XPrep& xp, bool pdl, cudaStream_t st);
+cudaError_t launch_xprep(int kind, const float* x, int B, int K, const XPrep& xp, const PrepOp& op, bool pdl,
+                         cudaStream_t st);
 // Plans and launches the tensor-core GEMV (B <= kMaxBatch). pdl lets the weight stream start
 // before the previous kernel in the stream (the x preparation) has finished.
 cudaError_t launch_gemv_tc(int kind, const GemvArgs& a, bool pdl, cudaStream_t st);

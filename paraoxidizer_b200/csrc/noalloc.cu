@@ -81,7 +81,7 @@ extern "C" int pox_cuda_tensor_gemv_noalloc(pox_cuda_ctx* ctx, const pox_tensor*
         if (t->tiled) {
             const TileLayout TL(kind, N, K);
             const XPrep xp = xprep_view(scratch, kind, K);
-            e = launch_xprep(kind, xb, b, K, xp, true, st);
+            e = launch_xprep(kind, xb, b, K, xp, PrepOp(), true, st);
             if (e != cudaSuccess) return cuda_error(e, "x preparation launch");
             GemvArgs a = {};
             a.w = (const uint8_t*)t->w;

@@ -116,6 +116,7 @@ static void free_tensor_mem(pox_tensor* t) {
 
 extern "C" void pox_cuda_destroy(pox_cuda_ctx* ctx) {
     if (!ctx) return;
+    pox::destroy_ctx_extras(ctx);  // models still alive (they own resident tensors of this context)
     {
         std::lock_guard<std::mutex> lk(ctx->mu);
         cudaSetDevice(ctx->device);
@@ -130,7 +131,6 @@ extern "C" void pox_cuda_destroy(pox_cuda_ctx* ctx) {
         cudaFreeHost(ctx->err_host);
         cudaStreamDestroy(ctx->stream);
     }
-    pox::destroy_ctx_extras(ctx);
     delete ctx;
 }
 
@@ -442,21 +442,27 @@ extern "C" int pox_cuda_tensor_info(const pox_tensor* t, size_t* rows, size_t* c
 // GEMV
 // ------------------------------------------------------------------------------------------
 int pox::gemv_launch(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x, size_t batch, float* y,
-                     cudaStream_t st) {
+                     cudaStream_t st, const PrepOp* op_in, const float* resid) {
     if (t->rows == 0 || t->cols == 0 || batch == 0) return POX_OK;
     if (((uintptr_t)x & 15) != 0) return set_error(POX_ERR_INVALID, "x must be 16-byte aligned");
+    const PrepOp op = op_in ? *op_in : PrepOp();
+    if ((op.mode != kPrepNone || resid) && !t->tiled)
+        return set_error(POX_ERR_UNSUPPORTED, "fused pre-ops need a tensor in the tiled layout");
     const int kind = t->dtype == POX_I4 ? kKindI4 : (t->dtype == POX_I8 ? kKindI8 : kKindF16);
     const int N = (int)t->rows, K = (int)t->cols;
+    const size_t ldx = op.ld_x ? (size_t)op.ld_x : t->cols;
     size_t done = 0;
     while (done < batch) {
         size_t b = std::min<size_t>(batch - done, 8);
-        const float* xb = x + done * t->cols;
+        const float* xb = x + done * ldx;
         float* yb = y + done * t->rows;
+        PrepOp opb = op;
+        if (opb.up) opb.up += done * (size_t)opb.ld_up;
         cudaError_t e;
         if (t->tiled) {
             const TileLayout TL(kind, N, K);
             const XPrep xp = xprep_view(t->scratch, kind, K);
-            e = launch_xprep(kind, xb, (int)b, K, xp, true, st);
+            e = launch_xprep(kind, xb, (int)b, K, xp, opb, true, st);
             if (e != cudaSuccess) return cuda_error(e, "x preparation launch");
             GemvArgs a = {};
             a.w = (const uint8_t*)t->w;
@@ -466,6 +472,7 @@ int pox::gemv_launch(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x, siz
             a.xq = xp.cols;
             a.xm = xp.meta;
             a.x = xb;
+            a.resid = resid ? resid + done * t->rows : nullptr;
             a.y = yb;
             a.N = N;
             a.K = K;
@@ -507,6 +514,26 @@ extern "C" int pox_cuda_tensor_gemv(pox_cuda_ctx* ctx, const pox_tensor* t, cons
     CK(cudaSetDevice(ctx->device), "cudaSetDevice");
     cudaStream_t st = stream ? (cudaStream_t)stream : ctx->stream;
     return gemv_launch(ctx, t, x_dev, batch, y_dev, st);
+}
+
+extern "C" int pox_cuda_tensor_gemv_ex(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x_dev, size_t batch,
+                                       float* y_dev, const pox_gemv_op* op, const float* resid_dev, void* stream) {
+    if (!ctx || !t) return set_error(POX_ERR_INVALID, "ctx/tensor is NULL");
+    if (batch && (!x_dev || !y_dev)) return set_error(POX_ERR_INVALID, "x/y is NULL");
+    PrepOp p;
+    if (op) {
+        if (op->mode < POX_OP_NONE || op->mode > POX_OP_SWIGLU) return set_error(POX_ERR_INVALID, "bad op mode");
+        if (op->mode == POX_OP_SWIGLU && !op->up) return set_error(POX_ERR_INVALID, "SwiGLU needs up");
+        p.mode = op->mode == POX_OP_RMSNORM ? kPrepNorm : (op->mode == POX_OP_SWIGLU ? kPrepSwiGLU : kPrepNone);
+        p.norm_w = op->norm_w;
+        p.eps = op->eps;
+        p.up = op->up;
+        p.ld_x = (int)op->ld_x;
+        p.ld_up = (int)(op->ld_up ? op->ld_up : (uint32_t)t->cols);
+    }
+    CK(cudaSetDevice(ctx->device), "cudaSetDevice");
+    cudaStream_t st = stream ? (cudaStream_t)stream : ctx->stream;
+    return gemv_launch(ctx, t, x_dev, batch, y_dev, st, &p, resid_dev);
 }
 
 // Host x in, host y out, synchronous. Caller holds ctx->mu.

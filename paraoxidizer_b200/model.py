@@ -1,0 +1,114 @@
+"""CudaModel: batched decode of a Llama-architecture model on B200 through libpox_cuda.so.
+
+Host-side mirror of the reference's decode interface: PoxEngine::forward_token(token, pos,
+&mut KvCache) -> logits (crates/paraoxidizer-runtime/src/engine.rs:411-716) and the greedy
+sampler (crates/paraoxidizer-runtime/src/sampler.rs:55-65), for a batch of sequences whose KV
+cache lives in fp16 pages of 16 tokens tracked by the BlockManager / BlockTable bookkeeping of
+paged_cache.rs (paged.py). Weights are the .pox payloads the reference's `pox quantize` writes:
+INT4 g128 projections (optional outlier tables), f16 embedding / lm_head / norms.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import weakref
+from typing import Optional, Sequence
+
+import numpy as np
+
+from . import _lib as L
+from .paged import DEFAULT_BLOCK_SIZE, BlockManager, BlockTable
+
+PROJ = ("q", "k", "v", "o", "gate", "up", "down")
+
+
+def _u8(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a)).view(np.uint8).reshape(-1)
+
+
+def _u16(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=np.uint16)).reshape(-1)
+
+
+class CudaModel:
+    """A model resident on one B200: weights uploaded once, paged fp16 KV cache in HBM."""
+
+    def __init__(self, backend, cfg: dict, max_batch: int, kv_blocks: int, max_blocks_per_seq: int):
+        self.backend = backend
+        self.cfg = dict(cfg)
+        c = L.LlamaConfig(cfg["hidden"], cfg["inter"], cfg["layers"], cfg["n_heads"], cfg["n_kv_heads"],
+                          cfg["vocab"], np.float32(cfg.get("rms_eps", 1e-5)), np.float32(cfg.get("rope_theta", 500000.0)))
+        h = C.c_void_p()
+        L.check(L.lib().pox_cuda_model_create(backend.ctx, C.byref(c), max_batch, kv_blocks, max_blocks_per_seq,
+                                              C.byref(h)))
+        self.handle = h.value
+        backend._children.append(weakref.ref(self))
+        self.max_batch = max_batch
+        self.max_blocks_per_seq = max_blocks_per_seq
+        self.blocks = BlockManager(kv_blocks, DEFAULT_BLOCK_SIZE)
+
+    def close(self) -> None:
+        if self.handle:
+            L.lib().pox_cuda_model_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # ---- weights ------------------------------------------------------------------------
+    def set_embeddings(self, embed, final_norm, lm_head) -> None:
+        e, f, hd = _u16(embed), _u16(final_norm), _u16(lm_head)
+        L.check(L.lib().pox_cuda_model_set_embeddings(self.handle, e.ctypes.data, f.ctypes.data, hd.ctypes.data))
+
+    def set_layer(self, layer: int, proj: dict, attn_norm, mlp_norm) -> None:
+        """proj[name] = {"packed", "scales", "rows", "cols", "group_size", "outliers": .pox table bytes or None}
+        for name in q, k, v, o, gate, up, down."""
+        descs = (L.TensorDesc * 7)()
+        keep = []
+        for i, name in enumerate(PROJ):
+            t = proj[name]
+            p, s = _u8(t["packed"]), _u8(t["scales"])
+            o = None if t.get("outliers") is None else _u8(t["outliers"])
+            keep += [p, s, o]
+            d = descs[i]
+            d.dtype, d.rows, d.cols, d.group_size = L.POX_I4, t["rows"], t["cols"], t["group_size"]
+            d.data, d.data_len = p.ctypes.data, p.size
+            d.scales, d.scale_len = s.ctypes.data, s.size
+            d.outliers, d.outlier_len = (None, 0) if o is None else (o.ctypes.data, o.size)
+        a, m = _u16(attn_norm), _u16(mlp_norm)
+        L.check(L.lib().pox_cuda_model_set_layer(self.handle, layer, descs, a.ctypes.data, m.ctypes.data))
+
+    # ---- decode -------------------------------------------------------------------------
+    def new_sequence(self) -> BlockTable:
+        return BlockTable(DEFAULT_BLOCK_SIZE)
+
+    def decode(self, tokens: Sequence[int], seqs: Sequence[BlockTable], want_logits: bool = True):
+        """One forward_token per sequence (engine.rs:411-716) at its next position; appends the
+        token to each sequence's block table. Returns (logits [batch][vocab] or None, greedy next
+        tokens [batch])."""
+        B = len(tokens)
+        assert B == len(seqs) and B > 0
+        pos = np.zeros(B, np.uint32)
+        tab = np.full((B, self.max_blocks_per_seq), -1, np.int32)
+        for b, s in enumerate(seqs):
+            pos[b] = s.sequence_len
+            s.append_token(self.blocks)
+            tab[b] = s.as_array(self.max_blocks_per_seq)
+        tok = np.asarray(tokens, np.uint32)
+        logits = np.zeros((B, self.cfg["vocab"]), np.float32) if want_logits else None
+        nxt = np.zeros(B, np.uint32)
+        L.check(L.lib().pox_cuda_model_decode(self.handle, B, tok.ctypes.data, pos.ctypes.data, tab.ctypes.data,
+                                              None if logits is None else logits.ctypes.data, nxt.ctypes.data))
+        return logits, nxt
+
+    def buffers(self):
+        ptrs = [C.c_void_p() for _ in range(5)]
+        L.check(L.lib().pox_cuda_model_buffers(self.handle, *[C.byref(p) for p in ptrs]))
+        return [p.value for p in ptrs]  # tokens, positions, block tables, logits, next
+
+    def decode_device(self, batch: int, advance: bool, stream: int = 0) -> None:
+        """Asynchronous step on the model's device buffers (see pox_cuda_model_decode_device)."""
+        L.check(L.lib().pox_cuda_model_decode_device(self.handle, batch, None, None, None, None, None,
+                                                     1 if advance else 0, stream or None))

@@ -1,0 +1,69 @@
+"""Synthetic Llama-architecture weights in the .pox layout, for tests and benchmarks.
+
+Random-init N(0, sigma) f32 projections quantized with the reference's quantizer
+(quantize_int4_group, crates/paraoxidizer-quant/src/kernels.rs:26-82; optional outlier extraction,
+outlier.rs:57-85), f16 embedding / lm_head, f16 norms (1.0 like the reference's fixtures,
+tests/common/mod.rs) -- there is no network for real checkpoints.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+from . import quant as Q
+
+
+def _f16(a) -> np.ndarray:
+    return np.asarray(a, np.float32).astype(np.float16).view(np.uint16)
+
+
+def make_llama(cfg: dict, seed: int = 0, sigma: float = 0.02, group_size: int = 128, outlier_policy=None,
+               norm_jitter: float = 0.0) -> dict:
+    rng = np.random.default_rng(seed)
+    H, I, V = cfg["hidden"], cfg["inter"], cfg["vocab"]
+    hd = H // cfg["n_heads"]
+    qd, kvd = cfg["n_heads"] * hd, cfg["n_kv_heads"] * hd
+    shapes = {"q": (qd, H), "k": (kvd, H), "v": (kvd, H), "o": (H, qd), "gate": (I, H), "up": (I, H), "down": (H, I)}
+    layers = []
+    for _ in range(cfg["layers"]):
+        lay = {}
+        for name, (r, c) in shapes.items():
+            w = rng.standard_normal(r * c, dtype=np.float32) * np.float32(sigma)
+            tab = Q.extract_and_zero_outliers(w, outlier_policy) if outlier_policy else None
+            packed, scales = Q.quantize_int4_group(w, group_size)
+            lay[name] = {"packed": packed, "scales": scales, "rows": r, "cols": c, "group_size": group_size,
+                         "outliers": None if tab is None else tab,
+                         "outlier_bytes": None if tab is None else Q.outliers_to_bytes(*tab)}
+        jit = (lambda: 1.0 + norm_jitter * rng.standard_normal(H, dtype=np.float32)) if norm_jitter else (
+            lambda: np.ones(H, np.float32))
+        lay["attn_norm"] = _f16(jit())
+        lay["mlp_norm"] = _f16(jit())
+        layers.append(lay)
+    embed = _f16(rng.standard_normal(V * H, dtype=np.float32) * np.float32(sigma))
+    lm_head = _f16(rng.standard_normal(V * H, dtype=np.float32) * np.float32(sigma))
+    final_norm = _f16(np.ones(H, np.float32))
+    return {"layers": layers, "embed": embed, "lm_head": lm_head, "final_norm": final_norm}
+
+
+def load_into(model, weights: dict) -> None:
+    """Uploads make_llama() weights into a CudaModel."""
+    for l, lay in enumerate(weights["layers"]):
+        proj = {}
+        for name in ("q", "k", "v", "o", "gate", "up", "down"):
+            t = dict(lay[name])
+            t["outliers"] = t.get("outlier_bytes")
+            proj[name] = t
+        model.set_layer(l, proj, lay["attn_norm"], lay["mlp_norm"])
+    model.set_embeddings(weights["embed"], weights["final_norm"], weights["lm_head"])
+
+
+def oracle_weights(weights: dict) -> dict:
+    """The same weights in the form oracle.OracleModel takes (outliers as (idx, val) arrays)."""
+    out = {"embed": weights["embed"], "lm_head": weights["lm_head"], "final_norm": weights["final_norm"], "layers": []}
+    for lay in weights["layers"]:
+        d = {"attn_norm": lay["attn_norm"], "mlp_norm": lay["mlp_norm"]}
+        for name in ("q", "k", "v", "o", "gate", "up", "down"):
+            t = lay[name]
+            d[name] = {"packed": t["packed"], "scales": t["scales"], "rows": t["rows"], "cols": t["cols"],
+                       "group_size": t["group_size"], "outliers": t["outliers"]}
+        out["layers"].append(d)
+    return out

@@ -1,0 +1,92 @@
+"""GPU parity of the batched decode step (CudaModel) against the oracle's forward_token.
+
+Reference: PoxEngine::forward_token (crates/paraoxidizer-runtime/src/engine.rs:411-716) over a
+KvCache (engine.rs:10-84); the CUDA path keeps K/V in fp16 pages of 16 tokens, so the oracle runs
+with K/V rounded to f16 on store. Bar: end-to-end logits within 1e-2 max abs per step,
+teacher-forced on the oracle's tokens, and identical greedy tokens wherever the oracle's top-2
+margin exceeds the tolerance.
+"""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+from paraoxidizer_b200.backend import CudaBackend
+from paraoxidizer_b200.model import CudaModel
+from paraoxidizer_b200.synth import load_into, make_llama, oracle_weights
+
+pytestmark = pytest.mark.gpu
+
+E2E_TOL = 1e-2
+
+CONFIGS = {
+    # head_dim 128, 2 query heads per kv head
+    "hd128": {"hidden": 512, "inter": 1024, "layers": 2, "n_heads": 4, "n_kv_heads": 2, "vocab": 1000,
+              "rms_eps": 1e-5, "rope_theta": 500000.0},
+    # the reference's synthetic Llama fixture shape (tests/common/mod.rs:32-163): d 256, 8 / 2 heads
+    "fixture": {"hidden": 256, "inter": 512, "layers": 2, "n_heads": 8, "n_kv_heads": 2, "vocab": 1000,
+                "rms_eps": 1e-5, "rope_theta": 500000.0},
+    # head_dim 64, 8 query heads per kv head
+    "hd64": {"hidden": 512, "inter": 512, "layers": 1, "n_heads": 8, "n_kv_heads": 1, "vocab": 512,
+             "rms_eps": 1e-5, "rope_theta": 10000.0},
+}
+
+
+@pytest.fixture(scope="module")
+def be():
+    b = CudaBackend.create(0)
+    yield b
+    b.close()
+
+
+@pytest.mark.parametrize("name,outliers", [("hd128", None), ("hd128", "automatic"), ("fixture", None),
+                                           ("hd64", "aggressive")])
+def test_decode_matches_forward_token(be, name, outliers):
+    cfg = CONFIGS[name]
+    w = make_llama(cfg, seed=11, outlier_policy=outliers, norm_jitter=0.1)
+    model = CudaModel(be, cfg, max_batch=3, kv_blocks=48, max_blocks_per_seq=16)
+    load_into(model, w)
+    ow = oracle_weights(w)
+    rng = np.random.default_rng(5)
+    # three sequences; one runs past 128 positions so attention uses two context splits
+    prompts = [list(rng.integers(0, cfg["vocab"], n)) for n in (6, 150, 21)]
+    steps = 12
+    oracles = [O.OracleModel(cfg, ow, max_seq=256, kv_f16=True) for _ in prompts]
+    seqs = [model.new_sequence() for _ in prompts]
+    feeds = [list(p) for p in prompts]
+    worst = 0.0
+    agree = total = 0
+    horizon = max(len(p) for p in prompts) + steps
+    for t in range(horizon):
+        active = [i for i in range(len(prompts)) if t < len(prompts[i]) + steps]
+        tokens = [int(feeds[i][t]) for i in active]
+        logits, nxt = model.decode(tokens, [seqs[i] for i in active])
+        for j, i in enumerate(active):
+            ref = oracles[i].forward_token(tokens[j], t)
+            err = float(np.max(np.abs(logits[j] - ref)))
+            worst = max(worst, err)
+            assert err <= E2E_TOL, (name, i, t, err)
+            top = np.sort(ref)[-2:]
+            ref_tok = int(np.argmax(ref))
+            if top[1] - top[0] > E2E_TOL:
+                total += 1
+                agree += int(nxt[j]) == ref_tok
+            if t + 1 >= len(prompts[i]):  # greedy continuation, teacher-forced on the oracle's token
+                feeds[i].append(ref_tok)
+    assert total > 0 and agree == total, (agree, total)
+    model.close()
+
+
+def test_decode_rejects_bad_inputs(be):
+    from paraoxidizer_b200 import _lib as L
+
+    cfg = CONFIGS["fixture"]
+    model = CudaModel(be, cfg, max_batch=2, kv_blocks=4, max_blocks_per_seq=2)
+    load_into(model, make_llama(cfg, seed=3))
+    seq = model.new_sequence()
+    with pytest.raises(L.PoxError):
+        model.decode([1, 2, 3], [seq, seq, seq])  # batch above max_batch
+    seq.sequence_len = 40  # position 40 needs a third page: beyond max_blocks_per_seq
+    seq.allocated_block_ids = [0, 1]
+    with pytest.raises(L.PoxError):
+        model.decode([1], [seq])
+    model.close()

@@ -222,6 +222,76 @@ def run_reference(args):
     return 0
 
 
+LLAMA_8B = {"hidden": 4096, "inter": 14336, "layers": 32, "n_heads": 32, "n_kv_heads": 8, "vocab": 128256,
+            "rms_eps": 1e-5, "rope_theta": 500000.0}
+
+
+def decode_bench(be, cfg=LLAMA_8B, batches=(1, 8, 32), prefill=512, steps=256, warm=3, seed=0):
+    """Llama-3-8B-architecture INT4 g128 decode (random-init weights): prefill of `prefill` random
+    token ids fed token by token (the reference prefills through forward_token, engine.rs:760-762),
+    then `steps` greedy decode steps timed as CUDA-graph replays of one step on the device."""
+    import torch
+
+    from paraoxidizer_b200.synth import build_llama_on_device
+
+    max_b = max(batches)
+    bps = (prefill + steps + warm + 15) // 16
+    t0 = time.perf_counter()
+    model = build_llama_on_device(be, cfg, max_b, max_b * bps, bps, seed=seed)
+    build_s = time.perf_counter() - t0
+    H, L_, nkv = cfg["hidden"], cfg["layers"], cfg["n_kv_heads"]
+    hd = H // cfg["n_heads"]
+    rng = np.random.default_rng(2)
+    out = {}
+    stream = torch.cuda.Stream()
+    for B in batches:
+        seqs = [model.new_sequence() for _ in range(B)]
+        prompts = rng.integers(0, cfg["vocab"], (B, prefill))
+        t0 = time.perf_counter()
+        nxt = None
+        for p in range(prefill):
+            _, nxt = model.decode(prompts[:, p], seqs, want_logits=False)
+        prefill_s = time.perf_counter() - t0
+        for sq in seqs:
+            sq.reserve(model.blocks, steps + warm)
+        model.set_state(nxt, seqs)
+        with torch.cuda.stream(stream):
+            for _ in range(warm):
+                model.decode_device(B, True, stream.cuda_stream)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(g, stream=stream):
+                model.decode_device(B, True, torch.cuda.current_stream().cuda_stream)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(steps - 1):
+                g.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        n = steps - 1
+        sec = e0.elapsed_time(e1) * 1e-3 / n
+        ctx_avg = prefill + warm + 1 + n / 2.0
+        kv_bytes = B * ctx_avg * L_ * nkv * hd * 2 * 2
+        bytes_step = model.weight_bytes + kv_bytes
+        peak, _ = measured_peak()
+        out[str(B)] = {"tokens_per_s": round(B / sec, 1), "ms_per_step": round(sec * 1e3, 4),
+                       "bytes_per_step": int(bytes_step), "achieved_gbs": round(bytes_step / sec / 1e9, 1),
+                       "roofline_frac": round(bytes_step / sec / 1e9 / peak, 4),
+                       "roofline_tokens_per_s": round(B * peak * 1e9 / bytes_step, 1),
+                       "prefill_tokens_per_s": round(B * prefill / prefill_s, 1)}
+        del g
+        for sq in seqs:
+            sq.free(model.blocks)
+    model.close()
+    torch.cuda.empty_cache()
+    return {"model": "llama-3-8b architecture, INT4 g128 projections (GPU quantizer), f16 embed/lm_head, "
+                     "random-init N(0,0.02)", "kv": "fp16 pages of 16 tokens", "prefill": prefill,
+            "decode_steps_timed": steps - 1, "build_s": round(build_s, 1), "per_batch": out}
+
+
 def run_ours(args):
     import torch
 
@@ -321,6 +391,10 @@ def run_ours(args):
     e2e_s = float(t.item())
     e2e_gbs = bytes_per * e2e_steps * world / e2e_s / 1e9
 
+    decode = None
+    if world == 1 and not args.no_decode:
+        decode = decode_bench(be)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cgbs, crows, ct = cpu_baseline_sample(packed, scales, tab)
@@ -347,7 +421,7 @@ def run_ours(args):
                         "d2h_bytes_per_step": ROWS * 4, "steps": e2e_steps,
                         "us_per_call": e2e_s / e2e_steps * 1e6},
                 "gpu_launches": 2 * args.steps, "clocks": clocks, "check_max_rel": rel,
-                "cpu_baseline": cpu}
+                "cpu_baseline": cpu, "decode": decode}
         print(json.dumps(line), flush=True)
     for tt in tensors:
         tt.free()
@@ -365,6 +439,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=200)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true", help="skip the Llama-8B-architecture decode benchmark")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -115,7 +115,8 @@ typedef struct {
     const uint8_t* outliers; size_t outlier_len; /* may be NULL; ignored for I8 (engine.rs:232) */
 } pox_tensor_desc;
 
-/* Uploads the tensor to HBM once, in the backend's device layout (INT4/INT8 weights re-tiled
+/* Uploads the tensor to HBM once, in the backend's device layout (data and scales may be host or
+ * device memory; outlier tables are read on the host) (INT4/INT8 weights re-tiled
  * for 128-bit loads and tensor-core fragments; outlier table turned into a per-row CSR with
  * precomputed corrections). Replaces the per-call copies of metal_backend.rs:111-129 and the
  * per-call SparseOutlierTable::from_bytes of engine.rs:150-151. The host pointers are
@@ -169,6 +170,12 @@ typedef struct {
  * POX_ERR_UNSUPPORTED. */
 int pox_cuda_tensor_gemv_ex(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x_dev, size_t batch, float* y_dev,
                             const pox_gemv_op* op, const float* resid_dev, void* stream);
+/* quantize_int4_group (crates/paraoxidizer-quant/src/kernels.rs:26-82) on the GPU, bit-exact:
+ * w_dev [numel] f32 (device) -> packed_dev [numel / 2] and scales_dev [numel / group_size * 4]
+ * (device), the .pox INT4 payloads. numel must be a multiple of an even group_size.
+ * Asynchronous on `stream` (NULL: the context's stream). */
+int pox_cuda_quantize_int4(pox_cuda_ctx* ctx, const float* w_dev, size_t numel, size_t group_size,
+                           uint8_t* packed_dev, uint8_t* scales_dev, void* stream);
 /* Dequantizes a resident tensor into out_dev ([rows][cols] f32, device), bit-exact with
  * dequantize_int4_group / dequantize_int8_symmetric (kernels.rs:85-128,157-173) followed by
  * SparseOutlierTable::apply_to (outlier.rs:88-95). Asynchronous on `stream`. */
@@ -203,6 +210,11 @@ int pox_cuda_model_set_embeddings(pox_model* m, const uint16_t* embed, const uin
  * gate/up are concatenated into one resident tensor each. */
 int pox_cuda_model_set_layer(pox_model* m, uint32_t layer, const pox_tensor_desc* proj, const uint16_t* attn_norm,
                              const uint16_t* mlp_norm);
+/* Layer `layer` from resident tensors (e.g. uploaded from device payloads): qkv = q, k, v
+ * projections stacked by rows, gate_up = gate, up stacked by rows, all INT4 in the tiled layout.
+ * The model takes ownership of the four tensors (freed with it). Norm weights: host f16. */
+int pox_cuda_model_set_layer_tensors(pox_model* m, uint32_t layer, pox_tensor* qkv, pox_tensor* o, pox_tensor* gate_up,
+                                     pox_tensor* down, const uint16_t* attn_norm, const uint16_t* mlp_norm);
 /* One decode step for `batch` sequences (engine.rs:411-716 forward_token, batched): row b feeds
  * tokens[b] at positions[b], its KV pages listed in block_tables[b * max_blocks_per_seq + j]
  * (page j holds positions 16 j .. 16 j + 15; paged_cache.rs:149-162). logits [batch][vocab]
@@ -216,6 +228,11 @@ int pox_cuda_model_decode(pox_model* m, uint32_t batch, const uint32_t* tokens, 
 int pox_cuda_model_decode_device(pox_model* m, uint32_t batch, const uint32_t* tokens_dev,
                                  const uint32_t* positions_dev, const int32_t* block_tables_dev, float* logits_dev,
                                  uint32_t* next_dev, int advance, void* stream);
+/* Loads a batch state into the model's device buffers without running a step (host arrays:
+ * tokens [batch], positions [batch], block_tables [batch][max_blocks_per_seq]); a following
+ * pox_cuda_model_decode_device with NULL inputs continues from it. Synchronous. */
+int pox_cuda_model_set_state(pox_model* m, uint32_t batch, const uint32_t* tokens, const uint32_t* positions,
+                             const int32_t* block_tables);
 /* The model's device buffers (any out pointer may be NULL): tokens [max_batch], positions
  * [max_batch], block tables [max_batch][max_blocks_per_seq], logits [max_batch][vocab], next
  * tokens [max_batch]. */

@@ -94,10 +94,13 @@ def _declare(L):
         "pox_cuda_tensor_gemv_ex": (i32, [vp, vp, vp, sz, vp, C.POINTER(GemvOp), vp, vp]),
         "pox_cuda_model_create": (i32, [vp, C.POINTER(LlamaConfig), u32, u32, u32, C.POINTER(vp)]),
         "pox_cuda_model_destroy": (None, [vp]),
+        "pox_cuda_model_set_layer_tensors": (i32, [vp, u32, vp, vp, vp, vp, vp, vp]),
+        "pox_cuda_quantize_int4": (i32, [vp, vp, sz, sz, vp, vp, vp]),
         "pox_cuda_model_set_embeddings": (i32, [vp, vp, vp, vp]),
         "pox_cuda_model_set_layer": (i32, [vp, u32, C.POINTER(TensorDesc), vp, vp]),
         "pox_cuda_model_decode": (i32, [vp, u32, vp, vp, vp, vp, vp]),
         "pox_cuda_model_decode_device": (i32, [vp, u32, vp, vp, vp, vp, vp, i32, vp]),
+        "pox_cuda_model_set_state": (i32, [vp, u32, vp, vp, vp]),
         "pox_cuda_model_buffers": (i32, [vp, C.POINTER(vp), C.POINTER(vp), C.POINTER(vp), C.POINTER(vp),
                                          C.POINTER(vp)]),
         "pox_cuda_tensor_dequant": (i32, [vp, vp, vp, vp]),

@@ -16,7 +16,7 @@ CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libpox_cuda.so")
 BUILD_DIR = os.path.join(PKG, "_build")
 
-SOURCES = ["pox_api.cu", "gemv.cu", "engine.cu", "noalloc.cu"]
+SOURCES = ["pox_api.cu", "gemv.cu", "engine.cu", "quantize.cu", "noalloc.cu"]
 HEADERS = ["common.cuh", "gemv.cuh", "api_internal.h"]
 
 

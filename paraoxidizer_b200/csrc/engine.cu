@@ -424,7 +424,7 @@ static int concat_i4(const pox_tensor_desc* parts, int n, std::vector<uint8_t>& 
 static int upload_f16(const uint16_t* h, size_t n, uint16_t** d, cudaStream_t st) {
     if (!h) return set_error(POX_ERR_INVALID, "f16 buffer is NULL");
     cudaError_t e = cudaMalloc(d, n * 2);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(*d, h, n * 2, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(*d, h, n * 2, cudaMemcpyDefault, st);  // host or device source
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     return e == cudaSuccess ? POX_OK : cuda_error(e, "f16 upload");
 }
@@ -653,6 +653,41 @@ extern "C" int pox_cuda_model_set_layer(pox_model* m, uint32_t layer, const pox_
     return rc;
 }
 
+extern "C" int pox_cuda_model_set_layer_tensors(pox_model* m, uint32_t layer, pox_tensor* qkv, pox_tensor* o,
+                                                pox_tensor* gate_up, pox_tensor* down, const uint16_t* attn_norm,
+                                                const uint16_t* mlp_norm) {
+    if (!m || !qkv || !o || !gate_up || !down) return set_error(POX_ERR_INVALID, "NULL argument");
+    if (layer >= (uint32_t)m->L) return set_error(POX_ERR_INVALID, "layer %u out of range", layer);
+    const size_t H = m->H, I = m->I, qd = (size_t)m->nq * m->hd;
+    struct Want { pox_tensor* t; size_t rows, cols; } want[4] = {
+        {qkv, (size_t)m->qkv_rows, H}, {o, H, qd}, {gate_up, 2 * I, H}, {down, H, I}};
+    for (const Want& w : want) {
+        if (w.t->rows != w.rows || w.t->cols != w.cols)
+            return set_error(POX_ERR_LAYOUT, "tensor is %zux%zu, expected %zux%zu", w.t->rows, w.t->cols, w.rows,
+                             w.cols);
+        if (w.t->dtype != POX_I4 || !w.t->tiled)
+            return set_error(POX_ERR_UNSUPPORTED, "layer tensors must be INT4 in the tiled layout");
+    }
+    pox_cuda_ctx* ctx = m->ctx;
+    LayerW& lw = m->layers[layer];
+    free_tensor(ctx, lw.qkv);
+    free_tensor(ctx, lw.o);
+    free_tensor(ctx, lw.gu);
+    free_tensor(ctx, lw.down);
+    lw.qkv = qkv;
+    lw.o = o;
+    lw.gu = gate_up;
+    lw.down = down;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    cudaSetDevice(ctx->device);
+    cudaFree(lw.attn_norm);
+    cudaFree(lw.mlp_norm);
+    lw.attn_norm = lw.mlp_norm = nullptr;
+    int rc = upload_f16(attn_norm, H, &lw.attn_norm, ctx->stream);
+    if (!rc) rc = upload_f16(mlp_norm, H, &lw.mlp_norm, ctx->stream);
+    return rc;
+}
+
 extern "C" int pox_cuda_model_decode_device(pox_model* m, uint32_t batch, const uint32_t* tokens_dev,
                                             const uint32_t* positions_dev, const int32_t* block_tables_dev,
                                             float* logits_dev, uint32_t* next_dev, int advance, void* stream) {
@@ -718,6 +753,25 @@ extern "C" int pox_cuda_model_decode(pox_model* m, uint32_t batch, const uint32_
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     if (e != cudaSuccess) return cuda_error(e, "decode step");
     return take_kernel_error(ctx);
+}
+
+extern "C" int pox_cuda_model_set_state(pox_model* m, uint32_t batch, const uint32_t* tokens, const uint32_t* positions,
+                                        const int32_t* block_tables) {
+    if (!m || !tokens || !positions || !block_tables) return set_error(POX_ERR_INVALID, "NULL argument");
+    if (batch == 0 || batch > m->max_batch) return set_error(POX_ERR_INVALID, "batch %u out of range", batch);
+    for (uint32_t b = 0; b < batch * m->max_blocks_per_seq; b++)
+        if (block_tables[b] >= (int32_t)m->kv_blocks)
+            return set_error(POX_ERR_INVALID, "block table entry %d out of range", block_tables[b]);
+    pox_cuda_ctx* ctx = m->ctx;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    cudaError_t e = cudaSetDevice(ctx->device);
+    const size_t B = batch;
+    if (e == cudaSuccess) e = cudaMemcpyAsync(m->tok, tokens, B * 4, cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(m->pos, positions, B * 4, cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(m->btab, block_tables, B * m->max_blocks_per_seq * 4, cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    return e == cudaSuccess ? POX_OK : cuda_error(e, "set_state");
 }
 
 extern "C" int pox_cuda_model_buffers(pox_model* m, uint32_t** tokens_dev, uint32_t** positions_dev,

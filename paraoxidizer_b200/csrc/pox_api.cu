@@ -214,6 +214,15 @@ static int validate_desc(const pox_tensor_desc* d) {
 // Builds the per-row CSR of an INT4 outlier table. Entries are applied in table order by the
 // reference (kernels.rs:211-219), so for a repeated slot the last entry wins. The stored
 // correction is v - dequant(q): adding corr * x to the tiled GEMV reproduces "replace".
+static bool is_device_memory(const void* p) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeDevice;
+}
+
 static int build_outlier_csr(const pox_tensor_desc* d, std::vector<uint32_t>& row_ptr, std::vector<uint32_t>& cols,
                              std::vector<float>& corr, std::vector<uint16_t>& vals) {
     row_ptr.assign(d->rows + 1, 0);
@@ -221,6 +230,8 @@ static int build_outlier_csr(const pox_tensor_desc* d, std::vector<uint32_t>& ro
     corr.clear();
     vals.clear();
     if (!d->outliers || d->outlier_len < 4) return POX_OK;  // outlier.rs:113-115
+    if (is_device_memory(d->outliers) || is_device_memory(d->data) || is_device_memory(d->scales))
+        return set_error(POX_ERR_UNSUPPORTED, "a tensor with an outlier table needs its payloads in host memory");
     const uint8_t* b = d->outliers;
     const uint64_t count = (uint64_t)b[0] | ((uint64_t)b[1] << 8) | ((uint64_t)b[2] << 16) | ((uint64_t)b[3] << 24);
     if (4 + 6 * count > d->outlier_len)
@@ -319,13 +330,13 @@ int pox::upload_tensor_locked(pox_cuda_ctx* ctx, const pox_tensor_desc* d, pox_t
         t->groups = (int)groups;
         t->tiled = (K % 128 == 0) && (d->group_size % 128 == 0);
         CKF(cudaMalloc(&tmp, raw_bytes), "cudaMalloc(raw)");
-        CKF(cudaMemcpyAsync(tmp, d->data, raw_bytes, cudaMemcpyHostToDevice, st), "cudaMemcpy(raw)");
+        CKF(cudaMemcpyAsync(tmp, d->data, raw_bytes, cudaMemcpyDefault, st), "cudaMemcpy(raw)");
         if (t->tiled) {
             const TileLayout TL(kKindI4, N, K);
             CKF(cudaMalloc(&t->w, TL.bytes()), "cudaMalloc(tiles)");
             CKF(launch_repack(kKindI4, (const uint8_t*)tmp, (uint8_t*)t->w, N, K, st), "repack_i4");
             CKF(cudaMalloc(&tmp_s, sbytes), "cudaMalloc(raw scales)");
-            CKF(cudaMemcpyAsync(tmp_s, d->scales, sbytes, cudaMemcpyHostToDevice, st), "cudaMemcpy(scales)");
+            CKF(cudaMemcpyAsync(tmp_s, d->scales, sbytes, cudaMemcpyDefault, st), "cudaMemcpy(scales)");
             CKF(launch_repack_i4_scales((const uint8_t*)tmp_s, (uint8_t*)t->w, N, K, (int)d->group_size, st),
                 "repack_i4_scales");
             t->bytes += TL.bytes();
@@ -334,7 +345,7 @@ int pox::upload_tensor_locked(pox_cuda_ctx* ctx, const pox_tensor_desc* d, pox_t
             tmp = nullptr;
             t->bytes += raw_bytes;
             CKF(cudaMalloc(&t->scales_dev, sbytes), "cudaMalloc(scales)");
-            CKF(cudaMemcpyAsync(t->scales_dev, d->scales, sbytes, cudaMemcpyHostToDevice, st), "cudaMemcpy(scales)");
+            CKF(cudaMemcpyAsync(t->scales_dev, d->scales, sbytes, cudaMemcpyDefault, st), "cudaMemcpy(scales)");
             t->bytes += sbytes;
         }
         std::vector<uint32_t> rp, cols;
@@ -359,11 +370,11 @@ int pox::upload_tensor_locked(pox_cuda_ctx* ctx, const pox_tensor_desc* d, pox_t
             CKF(cudaStreamSynchronize(st), "cudaStreamSynchronize(upload)");
         }
     } else if (d->dtype == POX_I8) {
-        std::memcpy(&t->i8_scale, d->scales, 4);  // one f32 LE (kernels.rs:150-151)
+        CKF(cudaMemcpy(&t->i8_scale, d->scales, 4, cudaMemcpyDefault), "cudaMemcpy(int8 scale)");  // one f32 LE (kernels.rs:150-151)
         const size_t raw_bytes = d->rows * d->cols;
         t->tiled = (K % 64 == 0);
         CKF(cudaMalloc(&tmp, raw_bytes), "cudaMalloc(raw)");
-        CKF(cudaMemcpyAsync(tmp, d->data, raw_bytes, cudaMemcpyHostToDevice, st), "cudaMemcpy(raw)");
+        CKF(cudaMemcpyAsync(tmp, d->data, raw_bytes, cudaMemcpyDefault, st), "cudaMemcpy(raw)");
         if (t->tiled) {
             const size_t tiles_bytes = TileLayout(kKindI8, N, K).bytes();
             CKF(cudaMalloc(&t->w, tiles_bytes), "cudaMalloc(tiles)");
@@ -378,7 +389,7 @@ int pox::upload_tensor_locked(pox_cuda_ctx* ctx, const pox_tensor_desc* d, pox_t
         const size_t raw_bytes = d->rows * d->cols * 2;
         t->tiled = (K % 32 == 0);
         CKF(cudaMalloc(&tmp, raw_bytes), "cudaMalloc(raw)");
-        CKF(cudaMemcpyAsync(tmp, d->data, raw_bytes, cudaMemcpyHostToDevice, st), "cudaMemcpy(raw)");
+        CKF(cudaMemcpyAsync(tmp, d->data, raw_bytes, cudaMemcpyDefault, st), "cudaMemcpy(raw)");
         if (t->tiled) {
             const size_t tiles_bytes = TileLayout(kKindF16, N, K).bytes();
             CKF(cudaMalloc(&t->w, tiles_bytes), "cudaMalloc(tiles)");

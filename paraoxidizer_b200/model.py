@@ -80,6 +80,17 @@ class CudaModel:
         a, m = _u16(attn_norm), _u16(mlp_norm)
         L.check(L.lib().pox_cuda_model_set_layer(self.handle, layer, descs, a.ctypes.data, m.ctypes.data))
 
+    def set_embeddings_device(self, embed_ptr: int, final_norm_ptr: int, lm_head_ptr: int) -> None:
+        """Same as set_embeddings with device pointers (f16 [vocab][hidden], [hidden], [vocab][hidden])."""
+        L.check(L.lib().pox_cuda_model_set_embeddings(self.handle, embed_ptr, final_norm_ptr, lm_head_ptr))
+
+    def set_layer_tensors(self, layer: int, qkv: int, o: int, gate_up: int, down: int, attn_norm, mlp_norm) -> None:
+        """Adopts resident tensors (handles of pox_tensor) as layer `layer`; see
+        pox_cuda_model_set_layer_tensors."""
+        a, m = _u16(attn_norm), _u16(mlp_norm)
+        L.check(L.lib().pox_cuda_model_set_layer_tensors(self.handle, layer, qkv, o, gate_up, down, a.ctypes.data,
+                                                         m.ctypes.data))
+
     # ---- decode -------------------------------------------------------------------------
     def new_sequence(self) -> BlockTable:
         return BlockTable(DEFAULT_BLOCK_SIZE)
@@ -102,6 +113,15 @@ class CudaModel:
         L.check(L.lib().pox_cuda_model_decode(self.handle, B, tok.ctypes.data, pos.ctypes.data, tab.ctypes.data,
                                               None if logits is None else logits.ctypes.data, nxt.ctypes.data))
         return logits, nxt
+
+    def set_state(self, tokens, seqs: Sequence[BlockTable]) -> None:
+        """Loads tokens, the sequences' next positions and their block tables into the device
+        buffers (pox_cuda_model_set_state) for decode_device steps."""
+        B = len(tokens)
+        pos = np.array([s.sequence_len for s in seqs], np.uint32)
+        tab = np.stack([s.as_array(self.max_blocks_per_seq) for s in seqs]).astype(np.int32)
+        tok = np.asarray(tokens, np.uint32)
+        L.check(L.lib().pox_cuda_model_set_state(self.handle, B, tok.ctypes.data, pos.ctypes.data, tab.ctypes.data))
 
     def buffers(self):
         ptrs = [C.c_void_p() for _ in range(5)]

@@ -67,3 +67,57 @@ def oracle_weights(weights: dict) -> dict:
                        "group_size": t["group_size"], "outliers": t["outliers"]}
         out["layers"].append(d)
     return out
+
+
+def build_llama_on_device(backend, cfg: dict, max_batch: int, kv_blocks: int, max_blocks_per_seq: int, seed: int = 0,
+                          sigma: float = 0.02):
+    """A CudaModel with random-init N(0, sigma) weights generated on the GPU: projections quantized
+    INT4 g128 by the GPU quantizer (bit-exact with quantize_int4_group) and uploaded from device
+    memory; embedding and lm_head f16; norms 1.0. q/k/v and gate/up are drawn as stacked
+    tensors (per-row quantization makes that identical to quantizing them separately)."""
+    import ctypes as C
+
+    import torch
+
+    from . import _lib as L
+    from .model import CudaModel
+
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(seed)
+    H, I, V = cfg["hidden"], cfg["inter"], cfg["vocab"]
+    hd = H // cfg["n_heads"]
+    qd, kvd = cfg["n_heads"] * hd, cfg["n_kv_heads"] * hd
+    model = CudaModel(backend, cfg, max_batch, kv_blocks, max_blocks_per_seq)
+    lib = L.lib()
+
+    def tensor(rows, cols):
+        w = torch.randn(rows * cols, device="cuda", generator=gen, dtype=torch.float32).mul_(sigma)
+        p = torch.empty(rows * cols // 2, dtype=torch.uint8, device="cuda")
+        s = torch.empty(rows * cols // 128 * 4, dtype=torch.uint8, device="cuda")
+        torch.cuda.synchronize()
+        L.check(lib.pox_cuda_quantize_int4(backend.ctx, w.data_ptr(), rows * cols, 128, p.data_ptr(), s.data_ptr(),
+                                           None))
+        backend.synchronize()
+        d = L.TensorDesc()
+        d.dtype, d.rows, d.cols, d.group_size = L.POX_I4, rows, cols, 128
+        d.data, d.data_len, d.scales, d.scale_len = p.data_ptr(), p.numel(), s.data_ptr(), s.numel()
+        h = C.c_void_p()
+        L.check(lib.pox_cuda_tensor_upload(backend.ctx, C.byref(d), C.byref(h)))
+        return h.value
+
+    ones = np.ones(H, np.float32).astype(np.float16).view(np.uint16)
+    weight_bytes = 0
+    for l in range(cfg["layers"]):
+        shapes = [(qd + 2 * kvd, H), (H, qd), (2 * I, H), (H, I)]
+        hs = [tensor(r, c) for r, c in shapes]
+        weight_bytes += sum(r * c // 2 + r * c // 128 * 4 for r, c in shapes)
+        model.set_layer_tensors(l, *hs, ones, ones)
+    embed = torch.randn(V * H, device="cuda", generator=gen).mul_(sigma).half()
+    head = torch.randn(V * H, device="cuda", generator=gen).mul_(sigma).half()
+    fn = torch.ones(H, device="cuda", dtype=torch.float16)
+    torch.cuda.synchronize()
+    model.set_embeddings_device(embed.data_ptr(), fn.data_ptr(), head.data_ptr())
+    del embed, head, fn
+    torch.cuda.empty_cache()
+    model.weight_bytes = weight_bytes + V * H * 2 + (2 * cfg["layers"] + 1) * H * 2
+    return model

@@ -226,20 +226,26 @@ LLAMA_8B = {"hidden": 4096, "inter": 14336, "layers": 32, "n_heads": 32, "n_kv_h
             "rms_eps": 1e-5, "rope_theta": 500000.0}
 
 
-def decode_bench(be, cfg=LLAMA_8B, batches=(1, 8, 32), prefill=512, steps=256, warm=3, seed=0):
+def decode_bench(be, cfg=LLAMA_8B, batches=(1, 8, 32), prefill=512, steps=256, warm=3, seed=0, world=1, rank=0,
+                 modes=("peer", "nccl")):
     """Llama-3-8B-architecture INT4 g128 decode (random-init weights): prefill of `prefill` random
     token ids fed token by token (the reference prefills through forward_token, engine.rs:760-762),
-    then `steps` greedy decode steps timed as CUDA-graph replays of one step on the device."""
+    then `steps` greedy decode steps timed as CUDA-graph replays of one step on the device. With
+    world > 1 every rank holds a tensor-parallel shard and the step time is the max over ranks;
+    each exchange implementation in `modes` is timed (the first is the default)."""
     import torch
 
     from paraoxidizer_b200.synth import build_llama_on_device
 
     max_b = max(batches)
-    bps = (prefill + steps + warm + 15) // 16
+    runs = len(modes) if world > 1 else 1
+    bps = (prefill + steps * runs + warm + 15) // 16
     t0 = time.perf_counter()
-    model = build_llama_on_device(be, cfg, max_b, max_b * bps, bps, seed=seed)
+    model = build_llama_on_device(be, cfg, max_b, max_b * bps, bps, seed=seed, tp_rank=rank, tp_size=world)
+    if world > 1:
+        model.init_comm(modes=modes)
     build_s = time.perf_counter() - t0
-    H, L_, nkv = cfg["hidden"], cfg["layers"], cfg["n_kv_heads"]
+    H, L_, nkv = cfg["hidden"], cfg["layers"], cfg["n_kv_heads"] // world
     hd = H // cfg["n_heads"]
     rng = np.random.default_rng(2)
     out = {}
@@ -253,26 +259,37 @@ def decode_bench(be, cfg=LLAMA_8B, batches=(1, 8, 32), prefill=512, steps=256, w
             _, nxt = model.decode(prompts[:, p], seqs, want_logits=False)
         prefill_s = time.perf_counter() - t0
         for sq in seqs:
-            sq.reserve(model.blocks, steps + warm)
+            sq.reserve(model.blocks, steps * runs + warm)
         model.set_state(nxt, seqs)
         with torch.cuda.stream(stream):
             for _ in range(warm):
                 model.decode_device(B, True, stream.cuda_stream)
         torch.cuda.synchronize()
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.stream(stream):
-            with torch.cuda.graph(g, stream=stream):
-                model.decode_device(B, True, torch.cuda.current_stream().cuda_stream)
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(stream):
-            e0.record(stream)
-            for _ in range(steps - 1):
-                g.replay()
-            e1.record(stream)
-        torch.cuda.synchronize()
         n = steps - 1
-        sec = e0.elapsed_time(e1) * 1e-3 / n
+        per_mode = {}
+        for mode in (modes if world > 1 else ("single",)):
+            if world > 1:
+                model.set_comm_mode(mode)
+            g = torch.cuda.CUDAGraph()  # with tp, the exchange kernels / NCCL calls are part of the graph
+            with torch.cuda.stream(stream):
+                with torch.cuda.graph(g, stream=stream):
+                    model.decode_device(B, True, torch.cuda.current_stream().cuda_stream)
+            torch.cuda.synchronize()
+            if world > 1:
+                torch.distributed.barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream):
+                e0.record(stream)
+                for _ in range(n):
+                    g.replay()
+                e1.record(stream)
+            torch.cuda.synchronize()
+            t = torch.tensor([e0.elapsed_time(e1) * 1e-3 / n], dtype=torch.float64, device="cuda")
+            if world > 1:
+                torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+            per_mode[mode] = float(t.item())
+            del g
+        sec = per_mode[modes[0] if world > 1 else "single"]
         ctx_avg = prefill + warm + 1 + n / 2.0
         kv_bytes = B * ctx_avg * L_ * nkv * hd * 2 * 2
         bytes_step = model.weight_bytes + kv_bytes
@@ -282,14 +299,41 @@ def decode_bench(be, cfg=LLAMA_8B, batches=(1, 8, 32), prefill=512, steps=256, w
                        "roofline_frac": round(bytes_step / sec / 1e9 / peak, 4),
                        "roofline_tokens_per_s": round(B * peak * 1e9 / bytes_step, 1),
                        "prefill_tokens_per_s": round(B * prefill / prefill_s, 1)}
-        del g
+        if world > 1:
+            out[str(B)]["exchange"] = modes[0]
+            out[str(B)]["tokens_per_s_by_exchange"] = {k: round(B / v, 1) for k, v in per_mode.items()}
         for sq in seqs:
             sq.free(model.blocks)
     model.close()
     torch.cuda.empty_cache()
     return {"model": "llama-3-8b architecture, INT4 g128 projections (GPU quantizer), f16 embed/lm_head, "
                      "random-init N(0,0.02)", "kv": "fp16 pages of 16 tokens", "prefill": prefill,
+            "parallelism": f"tp{world}" if world > 1 else "single GPU",
+            "bytes_per_step": "per GPU: its weight shard + its kv heads' pages (roofline = that / measured HBM peak)",
             "decode_steps_timed": steps - 1, "build_s": round(build_s, 1), "per_batch": out}
+
+
+def decode_batches(args):
+    return tuple(int(b) for b in args.decode_batches.split(","))
+
+
+def run_decode_only(args):
+    import torch
+
+    world, rank, local = dist_setup(args.gpus)
+    torch.cuda.set_device(local)
+    from paraoxidizer_b200.backend import CudaBackend
+
+    be = CudaBackend.create(local)
+    d = decode_bench(be, batches=decode_batches(args), prefill=args.decode_prefill, steps=args.decode_steps,
+                     world=world, rank=rank)
+    if rank == 0:
+        print(json.dumps({"decode": d}), flush=True)
+    be.close()
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    return 0
 
 
 def run_ours(args):
@@ -392,8 +436,9 @@ def run_ours(args):
     e2e_gbs = bytes_per * e2e_steps * world / e2e_s / 1e9
 
     decode = None
-    if world == 1 and not args.no_decode:
-        decode = decode_bench(be)
+    if not args.no_decode:
+        decode = decode_bench(be, batches=decode_batches(args), prefill=args.decode_prefill,
+                              steps=args.decode_steps, world=world, rank=rank)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -440,11 +485,18 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the Llama-8B-architecture decode benchmark")
+    ap.add_argument("--decode-only", action="store_true",
+                    help="run only the decode benchmark (one JSON object; for launch lists and captures)")
+    ap.add_argument("--decode-batches", default="1,8,32")
+    ap.add_argument("--decode-prefill", type=int, default=512)
+    ap.add_argument("--decode-steps", type=int, default=256)
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         return run_reference(args)
+    if args.decode_only:
+        return run_decode_only(args)
     return run_ours(args)
 
 

@@ -239,6 +239,40 @@ int pox_cuda_model_set_state(pox_model* m, uint32_t batch, const uint32_t* token
 int pox_cuda_model_buffers(pox_model* m, uint32_t** tokens_dev, uint32_t** positions_dev, int32_t** block_tables_dev,
                            float** logits_dev, uint32_t** next_dev);
 
+/* ---- tensor-parallel decode across the GPUs of one node (one process and context per GPU) ----
+ * The reference decodes on one device; the shard layout is the standard Megatron split, chosen so
+ * that every .pox payload shards into contiguous row ranges or 128-aligned column ranges:
+ *   q, k, v, gate, up, lm_head: split by rows (rank r holds heads [r nq/tp, (r+1) nq/tp), kv heads
+ *     [r nkv/tp, ...), FFN rows [r I/tp, ...), vocab rows [r V/tp, ...));
+ *   o, down: split by columns (K), their partial outputs summed by one allreduce each per layer;
+ *   embedding and norms: replicated.
+ * Rank r of tp_size is created with the whole model's configuration; the tensors given to
+ * set_layer / set_layer_tensors and the lm_head given to set_embeddings are rank r's shards, and
+ * logits are the rank's vocab slice [batch][vocab / tp_size]. Every rank calls every decode entry
+ * point with the same batch state; the greedy tokens (first maximum over the whole vocab) are the
+ * same on every rank. tp_size 1 is pox_cuda_model_create. Requires heads, kv_heads and vocab
+ * divisible by tp_size and intermediate by 128 tp_size. */
+int pox_cuda_model_create_tp(pox_cuda_ctx* ctx, const pox_llama_config* cfg, uint32_t max_batch, uint32_t kv_blocks,
+                             uint32_t max_blocks_per_seq, uint32_t tp_rank, uint32_t tp_size, pox_model** out);
+
+/* Allreduce / gather implementation of a tensor-parallel model. */
+#define POX_COMM_NCCL 1 /* ncclAllReduce / ncclAllGather on the decode stream */
+#define POX_COMM_PEER 2 /* one-shot exchange over CUDA IPC peer memory (NVLink loads, flag handshake) */
+
+/* A fresh NCCL unique id (128 bytes), made by one rank and sent to the others. */
+int pox_cuda_comm_unique_id(uint8_t id[128]);
+/* Joins the NCCL communicator of the tp_size ranks; collective (every rank, same id). */
+int pox_cuda_model_comm_nccl(pox_model* m, const uint8_t id[128]);
+/* The CUDA IPC handle (64 bytes) of this rank's exchange buffer (flags + two data slots). */
+int pox_cuda_model_comm_ipc_handle(pox_model* m, uint8_t handle[64]);
+/* Opens every rank's exchange buffer: handles = tp_size x 64 bytes in rank order (this rank's own
+ * entry is ignored). A waiting rank gives up after about two seconds and the step reports
+ * POX_ERR_TIMEOUT. */
+int pox_cuda_model_comm_peer(pox_model* m, const uint8_t* handles);
+/* Selects the exchange of the decode step (POX_COMM_NCCL or POX_COMM_PEER; set up first). Every
+ * rank must select the same mode. */
+int pox_cuda_model_comm_mode(pox_model* m, int mode);
+
 #ifdef __cplusplus
 }
 #endif

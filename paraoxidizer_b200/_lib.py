@@ -72,6 +72,9 @@ def declared_symbols() -> list[str]:
     return sorted(set(re.findall(r"\b(pox_cuda_\w+)\s*\(", src)))
 
 
+POX_COMM_NCCL, POX_COMM_PEER = 1, 2
+
+
 def _declare(L):
     vp, sz, i32, u32 = C.c_void_p, C.c_size_t, C.c_int, C.c_uint32
     sig = {
@@ -93,6 +96,12 @@ def _declare(L):
         "pox_cuda_tensor_gemv_noalloc": (i32, [vp, vp, vp, sz, vp, vp]),
         "pox_cuda_tensor_gemv_ex": (i32, [vp, vp, vp, sz, vp, C.POINTER(GemvOp), vp, vp]),
         "pox_cuda_model_create": (i32, [vp, C.POINTER(LlamaConfig), u32, u32, u32, C.POINTER(vp)]),
+        "pox_cuda_model_create_tp": (i32, [vp, C.POINTER(LlamaConfig), u32, u32, u32, u32, u32, C.POINTER(vp)]),
+        "pox_cuda_comm_unique_id": (i32, [vp]),
+        "pox_cuda_model_comm_nccl": (i32, [vp, vp]),
+        "pox_cuda_model_comm_ipc_handle": (i32, [vp, vp]),
+        "pox_cuda_model_comm_peer": (i32, [vp, vp]),
+        "pox_cuda_model_comm_mode": (i32, [vp, i32]),
         "pox_cuda_model_destroy": (None, [vp]),
         "pox_cuda_model_set_layer_tensors": (i32, [vp, u32, vp, vp, vp, vp, vp, vp]),
         "pox_cuda_quantize_int4": (i32, [vp, vp, sz, sz, vp, vp, vp]),

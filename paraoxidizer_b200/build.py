@@ -16,8 +16,8 @@ CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libpox_cuda.so")
 BUILD_DIR = os.path.join(PKG, "_build")
 
-SOURCES = ["pox_api.cu", "gemv.cu", "engine.cu", "quantize.cu", "noalloc.cu"]
-HEADERS = ["common.cuh", "gemv.cuh", "api_internal.h"]
+SOURCES = ["pox_api.cu", "gemv.cu", "engine.cu", "comm.cu", "quantize.cu", "noalloc.cu"]
+HEADERS = ["common.cuh", "gemv.cuh", "api_internal.h", "model.h", "comm.cuh"]
 
 
 def _nvcc() -> str:
@@ -64,7 +64,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
     nccl_inc, nccl_lib = _nccl_dirs()
     inc = ["-I", os.path.join(ROOT, "include"), "-I", CSRC]
     if nccl_inc:
-        inc += ["-I", nccl_inc]
+        inc += ["-I", nccl_inc, "-DPOX_HAVE_NCCL"]
     objs = []
     procs = []
     for s in SOURCES:

@@ -23,46 +23,11 @@
 #include "api_internal.h"
 #include "common.cuh"
 #include "gemv.cuh"
+#include "model.h"
 
-namespace pox {
-
-constexpr int kPage = 16;       // tokens per KV page (paged_cache.rs DEFAULT_BLOCK_SIZE)
-constexpr int kSplitTok = 128;  // context tokens per attention CTA
-
-struct LayerW {
-    pox_tensor* qkv = nullptr;
-    pox_tensor* o = nullptr;
-    pox_tensor* gu = nullptr;
-    pox_tensor* down = nullptr;
-    uint16_t* attn_norm = nullptr;
-    uint16_t* mlp_norm = nullptr;
-};
-
-}  // namespace pox
-
-struct pox_model {
-    pox_cuda_ctx* ctx = nullptr;
-    pox_llama_config cfg{};
-    int H = 0, I = 0, V = 0, L = 0, nq = 0, nkv = 0, hd = 0, G = 0, qkv_rows = 0;
-    uint32_t max_batch = 0, kv_blocks = 0, max_blocks_per_seq = 0;
-    uint16_t* embed = nullptr;
-    uint16_t* final_norm = nullptr;
-    pox_tensor* lm_head = nullptr;
-    std::vector<pox::LayerW> layers;
-    __half* kc = nullptr;  // [kv_blocks][L][nkv][16][hd]
-    __half* vc = nullptr;
-    float* x = nullptr;       // [B][H] residual stream
-    float* qkv = nullptr;     // [B][qkv_rows]
-    float* att = nullptr;     // [B][nq * hd]
-    float* gu = nullptr;      // [B][2 I]
-    float* logits = nullptr;  // [B][V]
-    float* apart = nullptr;   // [B][nkv][max_splits][G][hd + 2]
-    uint32_t* tok = nullptr;  // [B]
-    uint32_t* pos = nullptr;  // [B]
-    uint32_t* next = nullptr; // [B]
-    int32_t* btab = nullptr;  // [B][max_blocks_per_seq]
-    int max_splits = 0;
-};
+#ifdef POX_HAVE_NCCL
+#include <nccl.h>
+#endif
 
 namespace pox {
 
@@ -288,13 +253,23 @@ __global__ void attn_combine_kernel(const uint32_t* __restrict__ pos, int nq, in
 }
 
 // Non-finite logits -> 0 (engine.rs:709-713), then greedy argmax: the first index of the maximum
-// (sampler.rs:55-65, strict >).
-__global__ void __launch_bounds__(1024) argmax_kernel(float* __restrict__ logits, int V, uint32_t* __restrict__ next) {
-    const int b = blockIdx.x;
+// (sampler.rs:55-65, strict >), in two passes. Pass 1: block (p, b) takes vocab entries
+// [p chunk, (p + 1) chunk) of row b and writes its first maximum as (logit, index bits).
+__device__ __forceinline__ void first_max(float& v, int& i, float ov, int oi) {
+    if (ov > v || (ov == v && oi < i)) {
+        v = ov;
+        i = oi;
+    }
+}
+
+__global__ void __launch_bounds__(256) argmax_part_kernel(float* __restrict__ logits, int V, int chunk,
+                                                          float2* __restrict__ part) {
+    const int p = blockIdx.x, b = blockIdx.y;
     float* lr = logits + (size_t)b * V;
+    const int i1 = min(V, (p + 1) * chunk);
     float bv = -INFINITY;
     int bi = 0x7fffffff;
-    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    for (int i = p * chunk + threadIdx.x; i < i1; i += blockDim.x) {
         float v = lr[i];
         if (!isfinite(v)) {
             v = 0.f;
@@ -305,37 +280,43 @@ __global__ void __launch_bounds__(1024) argmax_kernel(float* __restrict__ logits
             bi = i;
         }
     }
-    __shared__ float sv[32];
-    __shared__ int si[32];
+    __shared__ float sv[8];
+    __shared__ int si[8];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > bv || (ov == bv && oi < bi)) {
-            bv = ov;
-            bi = oi;
-        }
-    }
+    for (int o = 16; o > 0; o >>= 1)
+        first_max(bv, bi, __shfl_xor_sync(0xffffffffu, bv, o), __shfl_xor_sync(0xffffffffu, bi, o));
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (lane == 0) {
         sv[warp] = bv;
         si[warp] = bi;
     }
     __syncthreads();
-    if (warp == 0) {
-        const int nw = blockDim.x >> 5;
-        bv = lane < nw ? sv[lane] : -INFINITY;
-        bi = lane < nw ? si[lane] : 0x7fffffff;
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); w++) first_max(bv, bi, sv[w], si[w]);
+        part[(size_t)b * kArgmaxParts + p] = make_float2(bv, __int_as_float(bi));
+    }
+}
+
+// Pass 2: one warp per row over its parts. One rank: next[b]. Tensor parallel: the rank's pair
+// (logit, token index in the whole vocabulary) for the pick across ranks.
+__global__ void argmax_final_kernel(const float2* __restrict__ part, int parts, int B, int vocab_off,
+                                    uint32_t* __restrict__ next, float2* __restrict__ pairs) {
+    const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (b >= B) return;
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int p = lane; p < parts; p += 32) {
+        const float2 q = part[(size_t)b * kArgmaxParts + p];
+        first_max(bv, bi, q.x, __float_as_int(q.y));
+    }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (ov > bv || (ov == bv && oi < bi)) {
-                bv = ov;
-                bi = oi;
-            }
-        }
-        if (lane == 0) next[b] = bi == 0x7fffffff ? 0u : (uint32_t)bi;
+    for (int o = 16; o > 0; o >>= 1)
+        first_max(bv, bi, __shfl_xor_sync(0xffffffffu, bv, o), __shfl_xor_sync(0xffffffffu, bi, o));
+    if (lane == 0) {
+        if (pairs)
+            pairs[b] = make_float2(bv, __int_as_float(bi == 0x7fffffff ? bi : bi + vocab_off));
+        else
+            next[b] = bi == 0x7fffffff ? 0u : (uint32_t)bi;
     }
 }
 
@@ -434,11 +415,24 @@ static void free_tensor(pox_cuda_ctx* ctx, pox_tensor*& t) {
     t = nullptr;
 }
 
+// x += W x_in for a row-split projection (o_proj, down_proj). One rank: the residual is added in
+// the GEMV epilogue. Tensor parallel: each rank's GEMV writes its partial (rank 0's carrying the
+// residual) where exchange `call` expects it, and the exchange leaves the sum over ranks in x.
+static int row_split_gemv(pox_model* m, const pox_tensor* t, const float* xin, int B, int call, const PrepOp* op,
+                          cudaStream_t st) {
+    if (m->comm.tp == 1) return gemv_launch(m->ctx, t, xin, B, m->x, st, op, m->x);
+    float* y = comm_partial(m->comm, call, m->x);
+    int rc = gemv_launch(m->ctx, t, xin, B, y, st, op, m->comm.rank == 0 ? m->x : nullptr);
+    if (rc) return rc;
+    return comm_allreduce(m->comm, call, 2 * m->L + 1, m->x, (size_t)B * m->H, st);
+}
+
 // The decode step on device buffers already filled (m->tok, m->pos, m->btab).
 static int decode_step(pox_model* m, int B, cudaStream_t st) {
     pox_cuda_ctx* ctx = m->ctx;
     int rc;
-    embed_kernel<<<B, 256, 0, st>>>(m->tok, m->embed, m->V, m->H, m->x);
+    if (m->comm.tp > 1 && !m->comm.mode) return set_error(POX_ERR_INVALID, "tensor-parallel exchange not set up");
+    embed_kernel<<<B, 256, 0, st>>>(m->tok, m->embed, m->V_full, m->H, m->x);
     if ((rc = check_launch("embed"))) return rc;
     PrepOp norm;
     norm.mode = kPrepNorm;
@@ -469,7 +463,7 @@ static int decode_step(pox_model* m, int B, cudaStream_t st) {
         attn_combine_kernel<<<dim3(m->nq, B), std::max(32, m->hd), 0, st>>>(m->pos, m->nq, m->nkv, m->G, m->hd,
                                                                            m->max_splits, m->apart, m->att);
         if ((rc = check_launch("attn_combine"))) return rc;
-        if ((rc = gemv_launch(ctx, w.o, m->att, B, m->x, st, nullptr, m->x))) return rc;
+        if ((rc = row_split_gemv(m, w.o, m->att, B, 2 * l, nullptr, st))) return rc;
         norm.norm_w = w.mlp_norm;
         if ((rc = gemv_launch(ctx, w.gu, m->x, B, m->gu, st, &norm))) return rc;
         PrepOp sw;
@@ -477,12 +471,20 @@ static int decode_step(pox_model* m, int B, cudaStream_t st) {
         sw.up = m->gu + m->I;
         sw.ld_x = 2 * m->I;
         sw.ld_up = 2 * m->I;
-        if ((rc = gemv_launch(ctx, w.down, m->gu, B, m->x, st, &sw, m->x))) return rc;
+        if ((rc = row_split_gemv(m, w.down, m->gu, B, 2 * l + 1, &sw, st))) return rc;
     }
     norm.norm_w = m->final_norm;
     if ((rc = gemv_launch(ctx, m->lm_head, m->x, B, m->logits, st, &norm))) return rc;
-    argmax_kernel<<<B, 1024, 0, st>>>(m->logits, m->V, m->next);
-    return check_launch("argmax");
+    const int parts = std::min(kArgmaxParts, (m->V + 2047) / 2048);
+    const int chunk = (m->V + parts - 1) / parts;
+    argmax_part_kernel<<<dim3(parts, B), 256, 0, st>>>(m->logits, m->V, chunk, m->amax);
+    if ((rc = check_launch("argmax"))) return rc;
+    const bool tp = m->comm.tp > 1;
+    argmax_final_kernel<<<(B + 7) / 8, 256, 0, st>>>(m->amax, parts, B, m->vocab_off, m->next,
+                                                    tp ? m->comm.pairs : nullptr);
+    if ((rc = check_launch("argmax"))) return rc;
+    if (tp) return comm_pick(m->comm, 2 * m->L, 2 * m->L + 1, B, m->next, st);
+    return POX_OK;
 }
 
 }  // namespace pox
@@ -491,8 +493,16 @@ using namespace pox;
 
 extern "C" int pox_cuda_model_create(pox_cuda_ctx* ctx, const pox_llama_config* cfg, uint32_t max_batch,
                                      uint32_t kv_blocks, uint32_t max_blocks_per_seq, pox_model** out) {
+    return pox_cuda_model_create_tp(ctx, cfg, max_batch, kv_blocks, max_blocks_per_seq, 0, 1, out);
+}
+
+extern "C" int pox_cuda_model_create_tp(pox_cuda_ctx* ctx, const pox_llama_config* cfg, uint32_t max_batch,
+                                        uint32_t kv_blocks, uint32_t max_blocks_per_seq, uint32_t tp_rank,
+                                        uint32_t tp_size, pox_model** out) {
     if (!ctx || !cfg || !out) return set_error(POX_ERR_INVALID, "NULL argument");
     *out = nullptr;
+    if (tp_size == 0 || tp_size > (uint32_t)kMaxTP || tp_rank >= tp_size)
+        return set_error(POX_ERR_INVALID, "tensor-parallel rank %u of %u (at most %d ranks)", tp_rank, tp_size, kMaxTP);
     if (!cfg->hidden || !cfg->heads || !cfg->kv_heads || !cfg->layers || !cfg->vocab || !cfg->intermediate ||
         !max_batch || !kv_blocks || !max_blocks_per_seq)
         return set_error(POX_ERR_INVALID, "zero dimension in the model configuration");
@@ -503,6 +513,11 @@ extern "C" int pox_cuda_model_create(pox_cuda_ctx* ctx, const pox_llama_config* 
         return set_error(POX_ERR_UNSUPPORTED, "head_dim %u / %u query heads per kv head not supported", hd, G);
     if (cfg->hidden % 128 || cfg->intermediate % 128)
         return set_error(POX_ERR_UNSUPPORTED, "hidden and intermediate must be multiples of 128");
+    if (cfg->heads % tp_size || cfg->kv_heads % tp_size || cfg->vocab % tp_size ||
+        cfg->intermediate % (128 * tp_size))
+        return set_error(POX_ERR_UNSUPPORTED,
+                         "tensor parallel %u needs heads, kv_heads, vocab divisible by it and intermediate by 128x it",
+                         tp_size);
     std::lock_guard<std::mutex> lk(ctx->mu);
     cudaError_t e = cudaSetDevice(ctx->device);
     if (e != cudaSuccess) return cuda_error(e, "cudaSetDevice");
@@ -510,11 +525,13 @@ extern "C" int pox_cuda_model_create(pox_cuda_ctx* ctx, const pox_llama_config* 
     m->ctx = ctx;
     m->cfg = *cfg;
     m->H = (int)cfg->hidden;
-    m->I = (int)cfg->intermediate;
-    m->V = (int)cfg->vocab;
+    m->I = (int)(cfg->intermediate / tp_size);
+    m->V_full = (int)cfg->vocab;
+    m->V = (int)(cfg->vocab / tp_size);
+    m->vocab_off = (int)tp_rank * m->V;
     m->L = (int)cfg->layers;
-    m->nq = (int)cfg->heads;
-    m->nkv = (int)cfg->kv_heads;
+    m->nq = (int)(cfg->heads / tp_size);
+    m->nkv = (int)(cfg->kv_heads / tp_size);
     m->hd = (int)hd;
     m->G = (int)G;
     m->qkv_rows = (m->nq + 2 * m->nkv) * m->hd;
@@ -534,6 +551,7 @@ extern "C" int pox_cuda_model_create(pox_cuda_ctx* ctx, const pox_llama_config* 
         {(void**)&m->gu, B * 2 * m->I * 4},
         {(void**)&m->logits, B * m->V * 4},
         {(void**)&m->apart, B * m->nkv * m->max_splits * m->G * (m->hd + 2) * 4},
+        {(void**)&m->amax, B * kArgmaxParts * sizeof(float2)},
         {(void**)&m->tok, B * 4},
         {(void**)&m->pos, B * 4},
         {(void**)&m->next, B * 4},
@@ -545,6 +563,15 @@ extern "C" int pox_cuda_model_create(pox_cuda_ctx* ctx, const pox_llama_config* 
             for (auto& f : allocs) cudaFree(*f.p);
             delete m;
             return cuda_error(e, "cudaMalloc(model buffers)");
+        }
+    }
+    if (tp_size > 1) {
+        const int rc = comm_alloc(m->comm, (int)tp_rank, (int)tp_size, B, (size_t)m->H, ctx->err_dev);
+        if (rc) {
+            comm_free(m->comm);
+            for (auto& f : allocs) cudaFree(*f.p);
+            delete m;
+            return rc;
         }
     }
     cudaMemsetAsync(m->kc, 0, kv_elems * 2, ctx->stream);
@@ -583,8 +610,9 @@ static void destroy_model(pox_model* m) {
     }
     free_tensor(ctx, m->lm_head);
     void* bufs[] = {m->embed, m->final_norm, m->kc, m->vc, m->x, m->qkv, m->att, m->gu, m->logits, m->apart,
-                    m->tok, m->pos, m->next, m->btab};
+                    m->amax, m->tok, m->pos, m->next, m->btab};
     for (void* p : bufs) cudaFree(p);
+    comm_free(m->comm);
     delete m;
 }
 }  // namespace pox
@@ -600,7 +628,7 @@ extern "C" int pox_cuda_model_set_embeddings(pox_model* m, const uint16_t* embed
         cudaFree(m->embed);
         cudaFree(m->final_norm);
         m->embed = m->final_norm = nullptr;
-        int rc = upload_f16(embed, (size_t)m->V * m->H, &m->embed, st);
+        int rc = upload_f16(embed, (size_t)m->V_full * m->H, &m->embed, st);
         if (!rc) rc = upload_f16(final_norm, (size_t)m->H, &m->final_norm, st);
         if (rc) return rc;
     }
@@ -746,7 +774,8 @@ extern "C" int pox_cuda_model_decode(pox_model* m, uint32_t batch, const uint32_
     if (e == cudaSuccess)
         e = cudaMemcpyAsync(m->btab, block_tables, B * m->max_blocks_per_seq * 4, cudaMemcpyHostToDevice, st);
     if (e != cudaSuccess) return cuda_error(e, "cudaMemcpy(decode inputs)");
-    int rc = decode_step(m, (int)batch, st);
+    int rc = comm_reset(m->comm, st);
+    if (!rc) rc = decode_step(m, (int)batch, st);
     if (rc) return rc;
     if (logits) e = cudaMemcpyAsync(logits, m->logits, B * m->V * 4, cudaMemcpyDeviceToHost, st);
     if (e == cudaSuccess && next_tokens) e = cudaMemcpyAsync(next_tokens, m->next, B * 4, cudaMemcpyDeviceToHost, st);
@@ -770,6 +799,7 @@ extern "C" int pox_cuda_model_set_state(pox_model* m, uint32_t batch, const uint
     if (e == cudaSuccess) e = cudaMemcpyAsync(m->pos, positions, B * 4, cudaMemcpyHostToDevice, ctx->stream);
     if (e == cudaSuccess)
         e = cudaMemcpyAsync(m->btab, block_tables, B * m->max_blocks_per_seq * 4, cudaMemcpyHostToDevice, ctx->stream);
+    if (e == cudaSuccess && comm_reset(m->comm, ctx->stream)) return POX_ERR_CUDA;
     if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
     return e == cudaSuccess ? POX_OK : cuda_error(e, "set_state");
 }
@@ -782,5 +812,56 @@ extern "C" int pox_cuda_model_buffers(pox_model* m, uint32_t** tokens_dev, uint3
     if (block_tables_dev) *block_tables_dev = m->btab;
     if (logits_dev) *logits_dev = m->logits;
     if (next_dev) *next_dev = m->next;
+    return POX_OK;
+}
+
+extern "C" int pox_cuda_comm_unique_id(uint8_t id[128]) {
+    if (!id) return set_error(POX_ERR_INVALID, "NULL argument");
+#ifdef POX_HAVE_NCCL
+    ncclUniqueId uid;
+    const ncclResult_t r = ncclGetUniqueId(&uid);
+    if (r != ncclSuccess) return set_error(POX_ERR_NCCL, "ncclGetUniqueId: %s", ncclGetErrorString(r));
+    std::memcpy(id, &uid, 128);
+    return POX_OK;
+#else
+    return set_error(POX_ERR_UNSUPPORTED, "built without NCCL");
+#endif
+}
+
+static int tp_model(pox_model* m) {
+    if (!m) return set_error(POX_ERR_INVALID, "model is NULL");
+    if (m->comm.tp < 2) return set_error(POX_ERR_INVALID, "model is not tensor parallel");
+    const cudaError_t e = cudaSetDevice(m->ctx->device);
+    return e == cudaSuccess ? POX_OK : cuda_error(e, "cudaSetDevice");
+}
+
+extern "C" int pox_cuda_model_comm_nccl(pox_model* m, const uint8_t id[128]) {
+    int rc = tp_model(m);
+    if (rc) return rc;
+    if (!id) return set_error(POX_ERR_INVALID, "NULL id");
+    return comm_init_nccl(m->comm, id);
+}
+
+extern "C" int pox_cuda_model_comm_ipc_handle(pox_model* m, uint8_t handle[64]) {
+    int rc = tp_model(m);
+    if (rc) return rc;
+    if (!handle) return set_error(POX_ERR_INVALID, "NULL handle");
+    return comm_ipc_handle(m->comm, handle);
+}
+
+extern "C" int pox_cuda_model_comm_peer(pox_model* m, const uint8_t* handles) {
+    int rc = tp_model(m);
+    if (rc) return rc;
+    if (!handles) return set_error(POX_ERR_INVALID, "NULL handles");
+    return comm_open_peers(m->comm, handles);
+}
+
+extern "C" int pox_cuda_model_comm_mode(pox_model* m, int mode) {
+    int rc = tp_model(m);
+    if (rc) return rc;
+    if (mode == POX_COMM_NCCL && !m->comm.nccl) return set_error(POX_ERR_INVALID, "NCCL communicator not set up");
+    if (mode == POX_COMM_PEER && !m->comm.peer_ready) return set_error(POX_ERR_INVALID, "peer buffers not opened");
+    if (mode != POX_COMM_NCCL && mode != POX_COMM_PEER) return set_error(POX_ERR_INVALID, "unknown mode %d", mode);
+    m->comm.mode = mode;
     return POX_OK;
 }

@@ -30,21 +30,62 @@ def _u16(a) -> np.ndarray:
 
 
 class CudaModel:
-    """A model resident on one B200: weights uploaded once, paged fp16 KV cache in HBM."""
+    """A model resident on one B200: weights uploaded once, paged fp16 KV cache in HBM.
 
-    def __init__(self, backend, cfg: dict, max_batch: int, kv_blocks: int, max_blocks_per_seq: int):
+    With tp_size > 1 this object is rank tp_rank of a tensor-parallel model (one process per GPU):
+    it takes the rank's weight shards (tp.shard_llama), returns the rank's vocab slice of the
+    logits, and needs init_comm() on every rank before the first step."""
+
+    def __init__(self, backend, cfg: dict, max_batch: int, kv_blocks: int, max_blocks_per_seq: int,
+                 tp_rank: int = 0, tp_size: int = 1):
         self.backend = backend
         self.cfg = dict(cfg)
+        self.tp_rank, self.tp_size = tp_rank, tp_size
         c = L.LlamaConfig(cfg["hidden"], cfg["inter"], cfg["layers"], cfg["n_heads"], cfg["n_kv_heads"],
                           cfg["vocab"], np.float32(cfg.get("rms_eps", 1e-5)), np.float32(cfg.get("rope_theta", 500000.0)))
         h = C.c_void_p()
-        L.check(L.lib().pox_cuda_model_create(backend.ctx, C.byref(c), max_batch, kv_blocks, max_blocks_per_seq,
-                                              C.byref(h)))
+        L.check(L.lib().pox_cuda_model_create_tp(backend.ctx, C.byref(c), max_batch, kv_blocks, max_blocks_per_seq,
+                                                 tp_rank, tp_size, C.byref(h)))
         self.handle = h.value
         backend._children.append(weakref.ref(self))
         self.max_batch = max_batch
         self.max_blocks_per_seq = max_blocks_per_seq
         self.blocks = BlockManager(kv_blocks, DEFAULT_BLOCK_SIZE)
+
+    @property
+    def vocab_local(self) -> int:
+        return self.cfg["vocab"] // self.tp_size
+
+    def init_comm(self, modes=("peer", "nccl"), group=None) -> None:
+        """Sets up the tensor-parallel exchanges (collective over the torch.distributed group of
+        the tp_size ranks, rank order = tp_rank): "nccl" joins an NCCL communicator, "peer" maps
+        every rank's exchange buffer over CUDA IPC. The first mode listed is selected."""
+        import torch.distributed as dist
+
+        lib = L.lib()
+        for mode in modes:
+            if mode == "nccl":
+                uid = (C.c_uint8 * 128)()
+                if self.tp_rank == 0:
+                    L.check(lib.pox_cuda_comm_unique_id(uid))
+                obj = [bytes(uid)]
+                dist.broadcast_object_list(obj, src=dist.get_global_rank(group, 0) if group else 0, group=group)
+                buf = (C.c_uint8 * 128).from_buffer_copy(obj[0])
+                L.check(lib.pox_cuda_model_comm_nccl(self.handle, buf))
+            elif mode == "peer":
+                h = (C.c_uint8 * 64)()
+                L.check(lib.pox_cuda_model_comm_ipc_handle(self.handle, h))
+                hs = [None] * self.tp_size
+                dist.all_gather_object(hs, bytes(h), group=group)
+                allh = (C.c_uint8 * (64 * self.tp_size)).from_buffer_copy(b"".join(hs))
+                L.check(lib.pox_cuda_model_comm_peer(self.handle, allh))
+            else:
+                raise ValueError(f"unknown exchange {mode!r}")
+        self.set_comm_mode(modes[0])
+        dist.barrier(group=group)  # every rank's buffers exist and are mapped before the first step
+
+    def set_comm_mode(self, mode: str) -> None:
+        L.check(L.lib().pox_cuda_model_comm_mode(self.handle, {"nccl": L.POX_COMM_NCCL, "peer": L.POX_COMM_PEER}[mode]))
 
     def close(self) -> None:
         if self.handle:
@@ -97,8 +138,8 @@ class CudaModel:
 
     def decode(self, tokens: Sequence[int], seqs: Sequence[BlockTable], want_logits: bool = True):
         """One forward_token per sequence (engine.rs:411-716) at its next position; appends the
-        token to each sequence's block table. Returns (logits [batch][vocab] or None, greedy next
-        tokens [batch])."""
+        token to each sequence's block table. Returns (logits [batch][vocab / tp_size] (this rank's
+        vocab slice) or None, greedy next tokens [batch])."""
         B = len(tokens)
         assert B == len(seqs) and B > 0
         pos = np.zeros(B, np.uint32)
@@ -108,7 +149,7 @@ class CudaModel:
             s.append_token(self.blocks)
             tab[b] = s.as_array(self.max_blocks_per_seq)
         tok = np.asarray(tokens, np.uint32)
-        logits = np.zeros((B, self.cfg["vocab"]), np.float32) if want_logits else None
+        logits = np.zeros((B, self.vocab_local), np.float32) if want_logits else None
         nxt = np.zeros(B, np.uint32)
         L.check(L.lib().pox_cuda_model_decode(self.handle, B, tok.ctypes.data, pos.ctypes.data, tab.ctypes.data,
                                               None if logits is None else logits.ctypes.data, nxt.ctypes.data))

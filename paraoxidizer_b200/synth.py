@@ -70,11 +70,13 @@ def oracle_weights(weights: dict) -> dict:
 
 
 def build_llama_on_device(backend, cfg: dict, max_batch: int, kv_blocks: int, max_blocks_per_seq: int, seed: int = 0,
-                          sigma: float = 0.02):
+                          sigma: float = 0.02, tp_rank: int = 0, tp_size: int = 1):
     """A CudaModel with random-init N(0, sigma) weights generated on the GPU: projections quantized
     INT4 g128 by the GPU quantizer (bit-exact with quantize_int4_group) and uploaded from device
     memory; embedding and lm_head f16; norms 1.0. q/k/v and gate/up are drawn as stacked
-    tensors (per-row quantization makes that identical to quantizing them separately)."""
+    tensors (per-row quantization makes that identical to quantizing them separately).
+    With tp_size > 1 only rank tp_rank's shard is drawn (shapes of tp.shard_llama; the draws
+    differ from the whole model's, which a throughput benchmark does not need)."""
     import ctypes as C
 
     import torch
@@ -83,11 +85,11 @@ def build_llama_on_device(backend, cfg: dict, max_batch: int, kv_blocks: int, ma
     from .model import CudaModel
 
     gen = torch.Generator(device="cuda")
-    gen.manual_seed(seed)
-    H, I, V = cfg["hidden"], cfg["inter"], cfg["vocab"]
+    gen.manual_seed(seed * 1000 + tp_rank)
+    H, I, V = cfg["hidden"], cfg["inter"] // tp_size, cfg["vocab"] // tp_size
     hd = H // cfg["n_heads"]
-    qd, kvd = cfg["n_heads"] * hd, cfg["n_kv_heads"] * hd
-    model = CudaModel(backend, cfg, max_batch, kv_blocks, max_blocks_per_seq)
+    qd, kvd = cfg["n_heads"] * hd // tp_size, cfg["n_kv_heads"] * hd // tp_size
+    model = CudaModel(backend, cfg, max_batch, kv_blocks, max_blocks_per_seq, tp_rank=tp_rank, tp_size=tp_size)
     lib = L.lib()
 
     def tensor(rows, cols):
@@ -112,7 +114,7 @@ def build_llama_on_device(backend, cfg: dict, max_batch: int, kv_blocks: int, ma
         hs = [tensor(r, c) for r, c in shapes]
         weight_bytes += sum(r * c // 2 + r * c // 128 * 4 for r, c in shapes)
         model.set_layer_tensors(l, *hs, ones, ones)
-    embed = torch.randn(V * H, device="cuda", generator=gen).mul_(sigma).half()
+    embed = torch.randn(cfg["vocab"] * H, device="cuda", generator=gen).mul_(sigma).half()
     head = torch.randn(V * H, device="cuda", generator=gen).mul_(sigma).half()
     fn = torch.ones(H, device="cuda", dtype=torch.float16)
     torch.cuda.synchronize()

@@ -16,8 +16,8 @@ CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libpox_cuda.so")
 BUILD_DIR = os.path.join(PKG, "_build")
 
-SOURCES = ["pox_api.cu", "gemv.cu", "engine.cu", "comm.cu", "quantize.cu", "noalloc.cu"]
-HEADERS = ["common.cuh", "gemv.cuh", "api_internal.h", "model.h", "comm.cuh"]
+SOURCES = ["pox_api.cu", "gemv.cu", "gemm_tc05.cu", "engine.cu", "comm.cu", "quantize.cu", "noalloc.cu"]
+HEADERS = ["common.cuh", "gemv.cuh", "api_internal.h", "model.h", "comm.cuh", "tc05.cuh"]
 
 
 def _nvcc() -> str:

@@ -43,6 +43,10 @@ struct pox_cuda_ctx {
     size_t scratch_x_bytes = 0;
     void* scratch_y = nullptr;
     size_t scratch_y_bytes = 0;
+    void* tc_scratch = nullptr;  // small-M path: prepared x, row scales, k-split partials
+    size_t tc_scratch_bytes = 0;
+    int* tc_tickets = nullptr;   // small-M path: per row block split counters (zeroed, self-resetting)
+    size_t tc_tickets_n = 0;
     int* err_host = nullptr;  // kernel error flag (host-mapped); nonzero = a bounded wait expired
     int* err_dev = nullptr;
     std::vector<pox_model*> models;  // decode models created on this context (destroyed with it)
@@ -59,6 +63,9 @@ struct PrepOp;
 int gemv_launch(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x, size_t batch, float* y, cudaStream_t st,
                 const PrepOp* op = nullptr, const float* resid = nullptr);
 void destroy_ctx_extras(pox_cuda_ctx* ctx);
+// Small-M path scratch for a tensor of rows x cols at `batch` rows of x (grown outside stream
+// capture only; a captured graph keeps the buffers it was captured with).
+int ensure_tc_scratch(pox_cuda_ctx* ctx, size_t rows, size_t cols, size_t batch, cudaStream_t st);
 // After a synchronize: turns a raised kernel error flag into POX_ERR_TIMEOUT (and clears it).
 int take_kernel_error(pox_cuda_ctx* ctx);
 }  // namespace pox

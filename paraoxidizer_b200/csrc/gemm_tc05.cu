@@ -1,0 +1,487 @@
+// gemm_tc05.cu -- the small-M path of the weight-only quantized projection: x [B][K] times
+// W^T for B = 9 .. 128 rows of x (decode at batch 16-64, chunks of a prefill), on the
+// 5th-generation tensor cores (tcgen05.mma kind::f16, accumulator in tensor memory).
+//
+// Same results contract as quant::gemv_int4 / gemv_int8 (crates/paraoxidizer-quant/src/
+// kernels.rs:177-255) and the F16 projection (crates/paraoxidizer-runtime/src/engine.rs:235-250)
+// for every row of x, within the GEMV tolerance: the weights enter the MMA as f16 -- INT4 as
+// f16(min + q scale) per element (one rounding of the exact affine value), INT8 as the exact
+// integer q with the per-tensor scale applied in f32 after the sum, F16 as stored -- and x as f16
+// after an exact power-of-two scaling per row that puts max|x| in [2^13, 2^14). Outlier values
+// replace their weights in the f16 tile exactly as SparseOutlierTable::apply_to does
+// (outlier.rs:88-95; the CSR keeps the last of duplicate entries).
+//
+// Kernel (one CTA = 128 weight rows x one k-split, 9 warps):
+//  * warps 0-7 (producers): warp d owns row tile d (16 rows) of the CTA's 128 rows. Per 128-k
+//    block it bulk-copies that tile's packed bytes (INT4: nibbles + scale words, 1088 B; INT8 2 KiB;
+//    F16 4 KiB, already contiguous in the re-tiled layout) into a private 4-stage ring, expands
+//    them to f16 in the 128-byte-swizzled K-major layout the MMA reads, writes the row tile's
+//    outlier values over their slots and arrives on the stage's "full" barrier.
+//  * warp 8 (MMA): allocates the accumulator (128 lanes x N columns of TMEM), bulk-copies the
+//    stage's x block (pre-swizzled in global memory by the x preparation), and issues 8 MMAs of
+//    128 x N x 16 per 128-k block; tcgen05.commit frees the stage.
+//  * epilogue (warps 0-3 = TMEM lanes 0-127 = the CTA's rows): y[b][row] = scale_b * D[row][b]
+//    (+ resid). With a k-split, each CTA stores its partial and the last CTA of the row block
+//    (ticket counter) adds the partials in split order, so results are deterministic.
+//  * every wait is bounded (kWaitCycles); a timeout raises the context error flag, drains what is
+//    in flight and frees the tensor memory before the CTA exits.
+#include <algorithm>
+
+#include "common.cuh"
+#include "gemv.cuh"
+#include "tc05.cuh"
+
+namespace pox {
+
+constexpr int kTcStages = 2;     // A / B stages (one 128-k block each)
+constexpr int kTcProd = 8;       // producer warps (row tiles of 16 rows)
+constexpr int kTcThreads = (kTcProd + 1) * 32;
+constexpr int kErrWaitTc = 16;   // bit of the kernel error flag
+
+__host__ __device__ constexpr int tc_wbytes(int kind) { return kind == kKindI4 ? 1088 : kind == kKindI8 ? 2048 : 4096; }
+// weight stages per producer warp (about 32-64 KiB of rings per CTA)
+__host__ __device__ constexpr int tc_ring(int kind) { return kind == kKindI4 ? 4 : kind == kKindI8 ? 3 : 2; }
+
+struct TcSmem {  // byte offsets in dynamic shared memory (1024-aligned base)
+    int a, b, ring, bars, tmem, total;
+};
+__host__ __device__ inline TcSmem tc_smem(int kind, int N) {
+    TcSmem s;
+    s.a = 0;                                         // kTcStages x 2 atoms x 128 rows x 128 B
+    s.b = s.a + kTcStages * 32768;                   // kTcStages x 2 atoms x N rows x 128 B
+    s.ring = s.b + kTcStages * N * 256;              // kTcProd x ring x wbytes
+    s.bars = s.ring + kTcProd * tc_ring(kind) * tc_wbytes(kind);
+    // barriers: full[S], xfull[S], empty[S], done, ring[kTcProd][ring]
+    s.tmem = s.bars + 8 * (3 * kTcStages + 1 + kTcProd * tc_ring(kind));
+    s.total = s.tmem + 16;
+    return s;
+}
+
+__device__ __forceinline__ void sts128(uint32_t a, uint4 v) {
+    asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
+}
+__device__ __forceinline__ void sts16(uint32_t a, uint16_t v) {
+    asm volatile("st.shared.u16 [%0], %1;" ::"r"(a), "h"(v) : "memory");
+}
+
+// 8 INT4 nibbles of a re-tiled word (byte i = q[i] | q[4+i] << 4) -> 8 f16 weights min + q scale in k order.
+__device__ __forceinline__ uint4 i4_word_to_f16(uint32_t w, uint32_t s2, uint32_t m2) {
+    const uint32_t kMagic = 0x64006400u;  // f16 pair (1024, 1024)
+    const uint32_t t01 = prmt(w, 0u, 0x4140u), t23 = prmt(w, 0u, 0x4342u);
+    uint4 r;
+    r.x = hfma2_u32(hsub2_u32(lop3_and_or(t01, 0x000F000Fu, kMagic), kMagic), s2, m2);
+    r.y = hfma2_u32(hsub2_u32(lop3_and_or(t23, 0x000F000Fu, kMagic), kMagic), s2, m2);
+    r.z = hfma2_u32(hsub2_u32(lop3_and_or(t01 >> 4, 0x000F000Fu, kMagic), kMagic), s2, m2);
+    r.w = hfma2_u32(hsub2_u32(lop3_and_or(t23 >> 4, 0x000F000Fu, kMagic), kMagic), s2, m2);
+    return r;
+}
+
+template <int KIND, int N>
+__global__ void __launch_bounds__(kTcThreads, 1) gemm_tc05_kernel(TcArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    const TcSmem P = tc_smem(KIND, N);
+    constexpr int kTcRing = tc_ring(KIND);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int rb = blockIdx.x, split = blockIdx.y;
+    const int kb0 = (int)((long long)a.nkb * split / a.S), kb1 = (int)((long long)a.nkb * (split + 1) / a.S);
+    const int nk = kb1 - kb0;
+    const uint32_t sA = smem_u32(smem + P.a), sB = smem_u32(smem + P.b), sRing = smem_u32(smem + P.ring);
+    const uint32_t bars = smem_u32(smem + P.bars);
+    auto full = [&](int s) { return bars + 8 * s; };
+    auto xfull = [&](int s) { return bars + 8 * (kTcStages + s); };
+    auto empty = [&](int s) { return bars + 8 * (2 * kTcStages + s); };
+    const uint32_t done = bars + 8 * (3 * kTcStages);
+    auto ringbar = [&](int d, int r) { return bars + 8 * (3 * kTcStages + 1 + d * kTcRing + r); };
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + P.tmem);
+    __shared__ int s_abort;
+
+    if (tid == 0) {
+        for (int s = 0; s < kTcStages; s++) {
+            mbar_init(full(s), kTcProd);
+            mbar_init(xfull(s), 1);
+            mbar_init(empty(s), 1);
+        }
+        mbar_init(done, 1);
+        for (int d = 0; d < kTcProd; d++)
+            for (int r = 0; r < kTcRing; r++) mbar_init(ringbar(d, r), 1);
+        s_abort = 0;
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    __syncthreads();
+    pdl_launch_dependents();
+
+    const int TB = tc_wbytes(KIND);
+    if (warp < kTcProd) {
+        // ------------------------------ producer warp d ------------------------------
+        const int d = warp, T = rb * 8 + d;  // row tile
+        const bool live = T < a.nT;
+        const uint8_t* wsrc = a.w + ((size_t)T * a.nkb + kb0) * TB;
+        const uint32_t ring = sRing + d * kTcRing * TB;
+        auto issue = [&](int i) {  // lane 0: weights of k-block kb0 + i into ring stage i % kTcRing
+            const uint32_t bar = ringbar(d, i % kTcRing);
+            mbar_expect_tx(bar, TB);
+            bulk_g2s(ring + (i % kTcRing) * TB, wsrc + (size_t)i * TB, TB, bar);
+        };
+        if (live && lane == 0)
+            for (int i = 0; i < kTcRing && i < nk; i++) issue(i);
+        // outlier cursor of row 16 T + lane (lanes 0..15), first entry at or after k-block kb0
+        uint32_t e_cur = 0, e_end = 0;
+        if (KIND == kKindI4 && a.row_ptr && live && lane < 16 && T * 16 + lane < a.Nout) {
+            e_cur = __ldg(a.row_ptr + T * 16 + lane);
+            e_end = __ldg(a.row_ptr + T * 16 + lane + 1);
+            while (e_cur < e_end && (int)__ldg(&a.ent[e_cur].x) < kb0 * 128) e_cur++;
+        }
+        const int g = lane >> 2, t = lane & 3;
+        int i = 0;
+        bool ok = true;
+        for (; i < nk; i++) {
+            const int s = i % kTcStages;
+            if (!__all_sync(0xffffffffu, mbar_wait(empty(s), ((i / kTcStages) & 1) ^ 1))) { ok = false; break; }
+            const uint32_t stA = sA + s * 32768;
+            if (live) {
+                const int r = i % kTcRing;
+                if (!__all_sync(0xffffffffu, mbar_wait(ringbar(d, r), (i / kTcRing) & 1))) { ok = false; break; }
+                const uint32_t src = ring + r * TB;
+#pragma unroll
+                for (int hs = 0; hs < 2; hs++) {  // rows g (hs 0) and g + 8 (hs 1) of the tile
+                    const uint32_t row = 16 * d + g + 8 * hs;
+                    if (KIND == kKindI4) {
+                        const uint4 v = lds128(src + hs * 512 + lane * 16);
+                        const uint32_t sw = *reinterpret_cast<const uint32_t*>(smem + P.ring + d * kTcRing * TB +
+                                                                               r * TB + 1024 + 4 * (2 * g + hs));
+                        const uint32_t s2 = (sw & 0xFFFFu) * 0x10001u, m2 = (sw >> 16) * 0x10001u;
+                        const uint32_t atom = stA + (t >> 1) * 16384;
+                        const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                        for (int w = 0; w < 4; w++)
+                            sts128(atom + sw128_off(row, 4 * (t & 1) + w), i4_word_to_f16(wv[w], s2, m2));
+                    } else if (KIND == kKindI8) {
+#pragma unroll
+                        for (int u = 0; u < 2; u++) {  // 64-k tiles u = atoms u
+                            const uint4 v = lds128(src + u * 1024 + hs * 512 + lane * 16);
+                            uint4 c0, c1;
+                            i8x4_to_f16x4(v.x, c0.x, c0.y);
+                            i8x4_to_f16x4(v.y, c0.z, c0.w);
+                            i8x4_to_f16x4(v.z, c1.x, c1.y);
+                            i8x4_to_f16x4(v.w, c1.z, c1.w);
+                            sts128(stA + u * 16384 + sw128_off(row, 2 * t), c0);
+                            sts128(stA + u * 16384 + sw128_off(row, 2 * t + 1), c1);
+                        }
+                    } else {
+#pragma unroll
+                        for (int u = 0; u < 4; u++) {  // 32-k tiles u: atom u / 2, chunks 4 (u % 2) + t
+                            const uint4 v = lds128(src + u * 1024 + hs * 512 + lane * 16);
+                            sts128(stA + (u >> 1) * 16384 + sw128_off(row, 4 * (u & 1) + t), v);
+                        }
+                    }
+                }
+                if (KIND == kKindI4 && a.row_ptr) {
+                    __syncwarp();
+                    const int kend = (kb0 + i + 1) * 128;
+                    while (e_cur < e_end) {  // lanes 0..15: entries of row 16 T + lane in this k-block
+                        const int col = (int)__ldg(&a.ent[e_cur].x);
+                        if (col >= kend) break;
+                        const int kk = col - (kb0 + i) * 128;
+                        sts16(stA + (kk >> 6) * 16384 + sw128_off(16 * d + lane, (kk & 63) >> 3) + 2 * (kk & 7),
+                              __ldg(a.vals + e_cur));
+                        e_cur++;
+                    }
+                }
+                __syncwarp();
+                if (lane == 0 && i + kTcRing < nk) {
+                    fence_proxy_async_smem();  // reads of the ring stage done before its refill
+                    issue(i + kTcRing);
+                }
+            } else {
+                // rows beyond the tensor: zero weights
+#pragma unroll
+                for (int hs = 0; hs < 2; hs++)
+#pragma unroll
+                    for (int c = 0; c < 4; c++)
+                        sts128(stA + ((t * 4 + c) >> 3) * 16384 + sw128_off(16 * d + g + 8 * hs, (t * 4 + c) & 7),
+                               make_uint4(0u, 0u, 0u, 0u));
+            }
+            fence_proxy_async_smem();  // generic-proxy writes visible to the tensor core
+            __syncwarp();
+            if (lane == 0) mbar_arrive(full(s));
+        }
+        if (!ok) {
+            if (lane == 0) {
+                atomicOr(a.err, kErrWaitTc);
+                atomicExch(&s_abort, 1);
+                if (live)  // copies issued but not consumed: wait for them (bounded) before exiting
+                    for (int j = i; j < nk && j < i + kTcRing; j++) mbar_wait(ringbar(d, j % kTcRing), (j / kTcRing) & 1);
+            }
+        }
+    } else {
+        // ------------------------------ MMA warp ------------------------------
+        pdl_wait();  // x is written by the preceding kernel; TMEM is taken only after it finished
+        tmem_alloc(smem_u32(tmem_slot), N < 32 ? 32 : N);
+        tmem_relinquish();
+        tc_fence_before();
+        __syncwarp();
+        tc_fence_after();
+        const uint32_t tmem = *tmem_slot;
+        if (lane == 0) {
+            const uint32_t idesc = umma_idesc_f16(128, N);
+            const uint32_t xb = N * 256;  // x bytes per 128-k block
+            auto issue_x = [&](int i) {
+                const int s = i % kTcStages;
+                mbar_expect_tx(xfull(s), xb);
+                bulk_g2s(sB + s * xb, a.xs + (size_t)(kb0 + i) * xb, xb, xfull(s));
+            };
+            int i = 0, issued = 0;
+            bool ok = true;
+            if (nk > 0) {
+                issue_x(0);
+                issued = 1;
+            }
+            for (; i < nk; i++) {
+                const int s = i % kTcStages;
+                if (i + 1 < nk) {  // stage of k-block i+1 is free once the MMAs of i+1-kTcStages completed
+                    if (!mbar_wait(empty((i + 1) % kTcStages), (((i + 1) / kTcStages) & 1) ^ 1)) { ok = false; break; }
+                    issue_x(i + 1);
+                    issued = i + 2;
+                }
+                if (!mbar_wait(full(s), (i / kTcStages) & 1) || !mbar_wait(xfull(s), (i / kTcStages) & 1)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll
+                for (int at = 0; at < 2; at++) {
+                    const uint64_t ad = umma_desc_sw128(sA + s * 32768 + at * 16384);
+                    const uint64_t bd = umma_desc_sw128(sB + s * xb + at * N * 128);
+#pragma unroll
+                    for (int k16 = 0; k16 < 4; k16++)
+                        umma_f16(tmem, ad + 2 * k16, bd + 2 * k16, idesc, (i | at | k16) != 0);
+                }
+                umma_commit(empty(s));
+            }
+            umma_commit(done);  // arrives when every MMA issued above has completed
+            if (!ok) {
+                atomicOr(a.err, kErrWaitTc);
+                atomicExch(&s_abort, 1);
+                for (int j = i; j < issued; j++)  // x copies in flight
+                    mbar_wait(xfull(j % kTcStages), (j / kTcStages) & 1);
+            }
+        }
+        __syncwarp();
+    }
+
+    // ------------------------------ epilogue ------------------------------
+    tc_fence_before();
+    __syncthreads();  // the TMEM address and every abort decision of the main loop are visible
+    tc_fence_after();
+    if (warp < 4) {
+        pdl_wait();
+        if (!mbar_wait(done, 0)) {
+            if (lane == 0) atomicOr(a.err, kErrWaitTc);
+            atomicExch(&s_abort, 1);
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");  // one decision for the four epilogue warps
+        tc_fence_after();
+        if (!*(volatile int*)&s_abort) {
+            const uint32_t tmem = *tmem_slot;
+            const int row = rb * 128 + warp * 32 + lane;
+            float* dst = a.S > 1 ? a.ws + (size_t)split * a.Bp * a.Nout : a.y;
+#pragma unroll
+            for (int c0 = 0; c0 < N; c0 += 32) {
+                float v[32];
+                tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + c0, v);
+                if (row < a.Nout) {
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        const int b = c0 + j;
+                        if (b < a.B) {
+                            if (a.S > 1) {
+                                dst[(size_t)b * a.Nout + row] = v[j];
+                            } else {
+                                float r = v[j] * a.xscale[b] * a.wscale;
+                                if (a.resid) r += a.resid[(size_t)b * a.Nout + row];
+                                dst[(size_t)b * a.Nout + row] = r;
+                            }
+                        }
+                    }
+                }
+            }
+            if (a.S > 1) {
+                __threadfence();
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+                __shared__ int s_last;
+                if (tid == 0) {
+                    const int prev = atomicAdd(a.tickets + rb, 1);
+                    s_last = prev == a.S - 1;
+                    if (s_last) a.tickets[rb] = 0;  // ready for the next launch
+                }
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+                if (s_last && row < a.Nout) {
+                    __threadfence();
+                    for (int b = 0; b < a.B; b++) {
+                        float acc = 0.f;
+                        for (int sp = 0; sp < a.S; sp++)
+                            acc += __ldcg(a.ws + ((size_t)sp * a.Bp + b) * a.Nout + row);
+                        float r = acc * a.xscale[b] * a.wscale;
+                        if (a.resid) r += a.resid[(size_t)b * a.Nout + row];
+                        a.y[(size_t)b * a.Nout + row] = r;
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();  // every TMEM read has completed (tcgen05.wait::ld) before the deallocation
+    if (warp == kTcProd) {
+        tc_fence_after();
+        tmem_dealloc(*tmem_slot, N < 32 ? 32 : N);
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// x preparation: one CTA per row n < Bp of the padded batch. Row n < B: v = op(x_n); e such that
+// max|v| 2^-e lies in [2^13, 2^14) (e = 0 for an all-zero row); writes f16(v 2^-e) into the
+// k-block-major, 128-byte-swizzled layout [kb][atom][Bp rows][128 B] and xscale[n] = 2^e. Rows
+// B .. Bp-1 are zero.
+// ------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) xprep_tc05_kernel(const float* __restrict__ x, int B, int Bp, int K,
+                                                         PrepOp op, uint8_t* __restrict__ xs,
+                                                         float* __restrict__ xscale) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int n = blockIdx.x, tid = threadIdx.x;
+    __shared__ float red[8];
+    __shared__ float s_inv, s_scale;
+    const float* xr = x + (size_t)n * op.ld_x;
+    const float* ur = op.up ? op.up + (size_t)n * op.ld_up : nullptr;
+    auto elem = [&](int k, float inv) -> float {
+        const float v = xr[k];
+        if (op.mode == kPrepNorm) {
+            const float t = v * inv;
+            return op.norm_w ? t * half_bits_to_float(op.norm_w[k]) : t;
+        }
+        if (op.mode == kPrepSwiGLU) return v / (1.0f + expf(-v)) * ur[k];
+        return v;
+    };
+    float inv = 1.f, scale = 0.f;
+    if (n < B) {
+        if (op.mode == kPrepNorm) {  // same fixed-order sum as the GEMV's x preparation
+            if (tid < 32) {
+                const float r = row_rms_inv(xr, K, op.eps);
+                if (tid == 0) s_inv = r;
+            }
+            __syncthreads();
+            inv = s_inv;
+        }
+        float m = 0.f;
+        for (int k = tid; k < K; k += 256) m = fmaxf(m, fabsf(elem(k, inv)));
+        m = warp_max(m);
+        if ((tid & 31) == 0) red[tid >> 5] = m;
+        __syncthreads();
+        if (tid == 0) {
+            float mm = 0.f;
+            for (int w = 0; w < 8; w++) mm = fmaxf(mm, red[w]);
+            int e = 0;
+            if (mm > 0.f && isfinite(mm)) {
+                frexpf(mm, &e);  // mm in [2^(e-1), 2^e)
+                e -= 14;
+            }
+            s_scale = ldexpf(1.f, e);
+            xscale[n] = ldexpf(1.f, e);
+        }
+        __syncthreads();
+        scale = 1.f / s_scale;  // a power of two: exact
+    }
+    // writes: thread handles 8 consecutive k (one 16-byte chunk) per iteration
+    for (int c = tid; c < K / 8; c += 256) {
+        const int k = c * 8, kb = k >> 7, kk = k & 127;
+        uint32_t h[4] = {0u, 0u, 0u, 0u};
+        if (n < B) {
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const __half2 p = __floats2half2_rn(elem(k + 2 * j, inv) * scale, elem(k + 2 * j + 1, inv) * scale);
+                h[j] = *reinterpret_cast<const uint32_t*>(&p);
+            }
+        }
+        const size_t off = ((size_t)kb * 2 + (kk >> 6)) * (size_t)Bp * 128 + sw128_off(n, (kk & 63) >> 3);
+        *reinterpret_cast<uint4*>(xs + off) = make_uint4(h[0], h[1], h[2], h[3]);
+    }
+}
+
+// ------------------------------------------------------------------------------------------
+// host side
+// ------------------------------------------------------------------------------------------
+int tc05_pad(int B) { return B <= 16 ? 16 : B <= 32 ? 32 : B <= 64 ? 64 : 128; }
+
+size_t tc05_x_bytes(int K, int Bp) { return (size_t)(K / 128) * Bp * 256; }
+
+// k-split count: waves of CTAs x k-blocks per CTA, plus a fixed cost per CTA and per split reduction.
+int tc05_splits(int nrb, int nkb, int sms) {
+    int best = 1;
+    double best_t = 1e30;
+    for (int S = 1; S <= 16 && S <= nkb; S++) {
+        const int waves = (nrb * S + sms - 1) / sms;
+        const int per = (nkb + S - 1) / S;
+        const double t = waves * (per + 3.0) + (S > 1 ? 2.0 : 0.0);
+        if (t < best_t - 1e-9) {
+            best_t = t;
+            best = S;
+        }
+    }
+    return best;
+}
+
+template <int KIND, int N>
+static cudaError_t launch_tc05_t(const TcArgs& a, cudaStream_t st) {
+    const TcSmem P = tc_smem(KIND, N);
+    const int bytes = P.total + 1024;
+    const cudaError_t e =  // per device and function: set on every launch (host-side, cheap)
+        cudaFuncSetAttribute(gemm_tc05_kernel<KIND, N>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((a.Nout + 127) / 128), (unsigned)a.S, 1);
+    cfg.blockDim = dim3(kTcThreads, 1, 1);
+    cfg.dynamicSmemBytes = bytes;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gemm_tc05_kernel<KIND, N>, a);
+}
+
+template <int KIND>
+static cudaError_t launch_tc05_kind(const TcArgs& a, cudaStream_t st) {
+    switch (a.Bp) {
+        case 16: return launch_tc05_t<KIND, 16>(a, st);
+        case 32: return launch_tc05_t<KIND, 32>(a, st);
+        case 64: return launch_tc05_t<KIND, 64>(a, st);
+        case 128: return launch_tc05_t<KIND, 128>(a, st);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_tc05(int kind, const TcArgs& a, cudaStream_t st) {
+    if (kind == kKindI4) return launch_tc05_kind<kKindI4>(a, st);
+    if (kind == kKindI8) return launch_tc05_kind<kKindI8>(a, st);
+    return launch_tc05_kind<kKindF16>(a, st);
+}
+
+cudaError_t launch_xprep_tc05(const float* x, int B, int Bp, int K, const PrepOp& op_in, uint8_t* xs, float* xscale,
+                              cudaStream_t st) {
+    PrepOp op = op_in;
+    if (op.ld_x == 0) op.ld_x = K;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)Bp, 1, 1);
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, xprep_tc05_kernel, x, B, Bp, K, op, xs, xscale);
+}
+
+}  // namespace pox

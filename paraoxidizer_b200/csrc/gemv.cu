@@ -78,23 +78,6 @@ __device__ __forceinline__ float prep_elem(const PrepOp& op, const PrepRow& r, i
     }
     return v;
 }
-// Per-row RMSNorm scale, computed by a whole warp in a fixed order (every warp of the row gets the
-// same value): lane-sequential sums over k = 4 lane + 128 j, then a butterfly.
-__device__ __forceinline__ float row_rms_inv(const float* x, int K, float eps) {
-    const int lane = threadIdx.x & 31;
-    float s = 0.f;
-    for (int k = 4 * lane; k < K; k += 128) {
-        const float4 v = *reinterpret_cast<const float4*>(x + k);
-        s = fmaf(v.x, v.x, s);
-        s = fmaf(v.y, v.y, s);
-        s = fmaf(v.z, v.z, s);
-        s = fmaf(v.w, v.w, s);
-    }
-    s = warp_sum(s);
-    const float rms = sqrtf(s / (float)K + eps);
-    return 1.0f / rms;
-}
-
 // One warp per (batch row, 128-k block); lane l covers k = 4l .. 4l+3 of the block.
 __global__ void __launch_bounds__(256) xprep_int_kernel(const float* __restrict__ x, int B, int K, uint8_t* cols,
                                                         float2* meta, int Kp, int nxb, int nxbs, PrepOp op) {

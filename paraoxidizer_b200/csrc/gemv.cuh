@@ -114,4 +114,28 @@ cudaError_t launch_dequant_i8(bool tiled, const void* w, float scale, float* out
 cudaError_t launch_apply_outliers(const uint32_t* row_ptr, const uint2* entries, const uint16_t* vals, float* out,
                                   int N, int K, cudaStream_t st);
 
+
+// ---- small-M path (tcgen05): batch 9 .. 128 rows of x per launch (gemm_tc05.cu) ----
+struct TcArgs {
+    const uint8_t* w;          // tile blobs (TileLayout of the kind; K % 128 == 0)
+    const uint32_t* row_ptr;   // INT4 outlier CSR by row (nullptr if none)
+    const uint2* ent;          // (col, ...) of each entry
+    const uint16_t* vals;      // f16 outlier value of each entry
+    const uint8_t* xs;         // prepared x: [K / 128][2][Bp][128 B], swizzled
+    const float* xscale;       // [Bp] power-of-two scale of each x row
+    float wscale;              // INT8 per-tensor scale (1 otherwise)
+    float* y;                  // [B][Nout]
+    const float* resid;        // nullptr, or [B][Nout] added (may alias y)
+    float* ws;                 // k-split partials [S][Bp][Nout]
+    int* tickets;              // [row blocks] zero-initialised, self-resetting
+    int* err;
+    int Nout, K, nkb, nT, B, Bp, S;
+};
+int tc05_pad(int B);                      // padded batch (MMA N): 16, 32, 64 or 128
+size_t tc05_x_bytes(int K, int Bp);       // prepared-x bytes
+int tc05_splits(int nrb, int nkb, int sms);
+cudaError_t launch_tc05(int kind, const TcArgs& a, cudaStream_t st);
+cudaError_t launch_xprep_tc05(const float* x, int B, int Bp, int K, const PrepOp& op, uint8_t* xs, float* xscale,
+                              cudaStream_t st);
+
 }  // namespace pox

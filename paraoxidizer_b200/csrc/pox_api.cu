@@ -6,6 +6,7 @@
 #include <algorithm>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -128,6 +129,8 @@ extern "C" void pox_cuda_destroy(pox_cuda_ctx* ctx) {
         ctx->tensors.clear();
         cudaFree(ctx->scratch_x);
         cudaFree(ctx->scratch_y);
+        cudaFree(ctx->tc_scratch);
+        cudaFree(ctx->tc_tickets);
         cudaFreeHost(ctx->err_host);
         cudaStreamDestroy(ctx->stream);
     }
@@ -452,6 +455,100 @@ extern "C" int pox_cuda_tensor_info(const pox_tensor* t, size_t* rows, size_t* c
 // ------------------------------------------------------------------------------------------
 // GEMV
 // ------------------------------------------------------------------------------------------
+static size_t tc_bytes(size_t rows, size_t cols, int Bp, int S) {
+    const size_t xs = (pox::tc05_x_bytes((int)cols, Bp) + 255) & ~(size_t)255;
+    return xs + 256 * sizeof(float) + (S > 1 ? (size_t)S * Bp * rows * sizeof(float) : 0);
+}
+
+int pox::ensure_tc_scratch(pox_cuda_ctx* ctx, size_t rows, size_t cols, size_t batch, cudaStream_t st) {
+    const int Bp = tc05_pad((int)std::min<size_t>(batch, 128));
+    const int nrb = (int)((rows + 127) / 128);
+    const int S = tc05_splits(nrb, (int)(cols / 128), ctx->num_sms);
+    const size_t need = tc_bytes(rows, cols, Bp, S);
+    const bool grow = need > ctx->tc_scratch_bytes || (size_t)nrb > ctx->tc_tickets_n;
+    if (!grow) return POX_OK;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (st && cudaStreamIsCapturing(st, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone)
+        return set_error(POX_ERR_INVALID, "small-M scratch must be sized by a call before stream capture");
+    CK(cudaStreamSynchronize(st ? st : ctx->stream), "cudaStreamSynchronize");
+    if (need > ctx->tc_scratch_bytes) {
+        cudaFree(ctx->tc_scratch);
+        ctx->tc_scratch = nullptr;
+        ctx->tc_scratch_bytes = 0;
+        const size_t bytes = std::max(need, (size_t)64 << 20);
+        CK(cudaMalloc(&ctx->tc_scratch, bytes), "cudaMalloc(small-M scratch)");
+        CK(cudaMemset(ctx->tc_scratch, 0, bytes), "cudaMemset(small-M scratch)");
+        ctx->tc_scratch_bytes = bytes;
+    }
+    if ((size_t)nrb > ctx->tc_tickets_n) {
+        cudaFree(ctx->tc_tickets);
+        ctx->tc_tickets = nullptr;
+        ctx->tc_tickets_n = 0;
+        const size_t n = std::max<size_t>(nrb, 4096);
+        CK(cudaMalloc(&ctx->tc_tickets, n * sizeof(int)), "cudaMalloc(tickets)");
+        CK(cudaMemset(ctx->tc_tickets, 0, n * sizeof(int)), "cudaMemset(tickets)");
+        ctx->tc_tickets_n = n;
+    }
+    return POX_OK;
+}
+
+// Small-M path: up to 128 rows of x per launch pair (x preparation + tcgen05 GEMM).
+static int tc05_gemv(pox_cuda_ctx* ctx, const pox_tensor* t, int kind, const float* x, size_t batch, float* y,
+                     cudaStream_t st, const PrepOp& op, const float* resid) {
+    const int N = (int)t->rows, K = (int)t->cols;
+    const size_t ldx = op.ld_x ? (size_t)op.ld_x : t->cols;
+    int rc = ensure_tc_scratch(ctx, t->rows, t->cols, batch, st);
+    if (rc) return rc;
+    const int nrb = (N + 127) / 128;
+    const int S = tc05_splits(nrb, K / 128, ctx->num_sms);
+    size_t done = 0;
+    while (done < batch) {
+        const int b = (int)std::min<size_t>(batch - done, 128);
+        const int Bp = tc05_pad(b);
+        uint8_t* xs = static_cast<uint8_t*>(ctx->tc_scratch);
+        const size_t xsb = (tc05_x_bytes(K, Bp) + 255) & ~(size_t)255;
+        float* xscale = reinterpret_cast<float*>(xs + xsb);
+        float* ws = xscale + 256;
+        PrepOp opb = op;
+        if (opb.up) opb.up += done * (size_t)opb.ld_up;
+        cudaError_t e = launch_xprep_tc05(x + done * ldx, b, Bp, K, opb, xs, xscale, st);
+        if (e != cudaSuccess) return cuda_error(e, "x preparation launch");
+        TcArgs a = {};
+        a.w = (const uint8_t*)t->w;
+        a.row_ptr = kind == kKindI4 ? t->row_ptr : nullptr;
+        a.ent = t->entries;
+        a.vals = t->vals;
+        a.xs = xs;
+        a.xscale = xscale;
+        a.wscale = kind == kKindI8 ? t->i8_scale : 1.0f;
+        a.y = y + done * t->rows;
+        a.resid = resid ? resid + done * t->rows : nullptr;
+        a.ws = ws;
+        a.tickets = ctx->tc_tickets;
+        a.err = ctx->err_dev;
+        a.Nout = N;
+        a.K = K;
+        a.nkb = K / 128;
+        a.nT = (N + 15) / 16;
+        a.B = b;
+        a.Bp = Bp;
+        a.S = S;
+        e = launch_tc05(kind, a, st);
+        if (e != cudaSuccess) return cuda_error(e, "small-M GEMM launch");
+        done += b;
+    }
+    return POX_OK;
+}
+
+// Batches above this use the small-M tensor-core path (when the tensor qualifies).
+static int tc05_min_batch() {
+    static const int v = [] {
+        const char* s = getenv("POX_TC05_MIN_BATCH");
+        return s ? std::max(1, atoi(s)) : kMaxBatch + 1;
+    }();
+    return v;
+}
+
 int pox::gemv_launch(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x, size_t batch, float* y,
                      cudaStream_t st, const PrepOp* op_in, const float* resid) {
     if (t->rows == 0 || t->cols == 0 || batch == 0) return POX_OK;
@@ -461,6 +558,8 @@ int pox::gemv_launch(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x, siz
         return set_error(POX_ERR_UNSUPPORTED, "fused pre-ops need a tensor in the tiled layout");
     const int kind = t->dtype == POX_I4 ? kKindI4 : (t->dtype == POX_I8 ? kKindI8 : kKindF16);
     const int N = (int)t->rows, K = (int)t->cols;
+    if (t->tiled && K % 128 == 0 && batch >= (size_t)tc05_min_batch())
+        return tc05_gemv(ctx, t, kind, x, batch, y, st, op, resid);
     const size_t ldx = op.ld_x ? (size_t)op.ld_x : t->cols;
     size_t done = 0;
     while (done < batch) {

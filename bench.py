@@ -222,6 +222,65 @@ def run_reference(args):
     return 0
 
 
+def batched_gemv_bench(be, batches=(1, 4, 16, 64), reps=400):
+    """The batched configurations: INT8 14336x4096 (per-tensor scale, the parity path) and INT4 g128
+    4096x14336 with 3.5-sigma outliers, at B rows of x (B <= 8: the GEMV kernel; B >= 9: the
+    tcgen05 small-M kernel). Copies rotated past L2, CUDA graph of `reps` launches, CUDA events.
+    Algorithmic bytes: weights + scales (+ outlier table) + x as f16 (2 K B) + y as f32 (4 N B)."""
+    import torch
+
+    from paraoxidizer_b200 import quant as Q
+
+    out = {}
+    peak, _ = measured_peak()
+    rng = np.random.default_rng(11)
+    stream = torch.cuda.Stream()
+    cases = []
+    w8 = rng.standard_normal(14336 * 4096, dtype=np.float32) * np.float32(0.02)
+    q8, s8 = Q.quantize_int8_symmetric(w8)
+    cases.append(("int8_14336x4096", 14336, 4096, [be.upload_int8(q8, s8, 14336, 4096) for _ in range(6)],
+                  14336 * 4096 + 4))
+    del w8, q8
+    packed, scales, tab, ob, _ = make_workload(seed=3)
+    cases.append(("int4_g128_4096x14336_outliers", ROWS, COLS,
+                  [be.upload_int4(packed, scales, ROWS, COLS, GS, ob) for _ in range(8)],
+                  ROWS * COLS // 2 + ROWS * (COLS // GS) * 4 + 4 + 6 * len(tab[0])))
+    for name, N, K, ts, wbytes in cases:
+        res = {}
+        for B in batches:
+            x = torch.randn(B * K, device="cuda")
+            y = torch.zeros(B * N, device="cuda")
+            with torch.cuda.stream(stream):
+                for i in range(3 * len(ts)):
+                    ts[i % len(ts)].gemv_device(x.data_ptr(), B, y.data_ptr(), stream.cuda_stream)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(stream):
+                with torch.cuda.graph(g, stream=stream):
+                    for i in range(reps):
+                        ts[i % len(ts)].gemv_device(x.data_ptr(), B, y.data_ptr(),
+                                                    torch.cuda.current_stream().cuda_stream)
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream):
+                g.replay()
+                e0.record(stream)
+                g.replay()
+                e1.record(stream)
+            torch.cuda.synchronize()
+            sec = e0.elapsed_time(e1) * 1e-3 / reps
+            nbytes = wbytes + 2 * K * B + 4 * N * B
+            res[str(B)] = {"us": round(sec * 1e6, 2), "gbs": round(nbytes / sec / 1e9, 1),
+                           "frac_of_hbm_peak": round(nbytes / sec / 1e9 / peak, 4),
+                           "tflops": round(2.0 * N * K * B / sec / 1e12, 2),
+                           "kernel": "gemv_tc_kernel (mma.sync)" if B <= 8 else "gemm_tc05_kernel (tcgen05)"}
+            del g
+        out[name] = res
+        for t in ts:
+            t.free()
+    return out
+
+
 LLAMA_8B = {"hidden": 4096, "inter": 14336, "layers": 32, "n_heads": 32, "n_kv_heads": 8, "vocab": 128256,
             "rms_eps": 1e-5, "rope_theta": 500000.0}
 
@@ -325,10 +384,11 @@ def run_decode_only(args):
     from paraoxidizer_b200.backend import CudaBackend
 
     be = CudaBackend.create(local)
+    bg = batched_gemv_bench(be) if world == 1 else None
     d = decode_bench(be, batches=decode_batches(args), prefill=args.decode_prefill, steps=args.decode_steps,
                      world=world, rank=rank)
     if rank == 0:
-        print(json.dumps({"decode": d}), flush=True)
+        print(json.dumps({"batched_gemv": bg, "decode": d}), flush=True)
     be.close()
     if world > 1:
         torch.distributed.barrier()
@@ -435,6 +495,10 @@ def run_ours(args):
     e2e_s = float(t.item())
     e2e_gbs = bytes_per * e2e_steps * world / e2e_s / 1e9
 
+    batched = None
+    if world == 1 and not args.no_decode:
+        batched = batched_gemv_bench(be)
+
     decode = None
     if not args.no_decode:
         decode = decode_bench(be, batches=decode_batches(args), prefill=args.decode_prefill,
@@ -466,7 +530,7 @@ def run_ours(args):
                         "d2h_bytes_per_step": ROWS * 4, "steps": e2e_steps,
                         "us_per_call": e2e_s / e2e_steps * 1e6},
                 "gpu_launches": 2 * args.steps, "clocks": clocks, "check_max_rel": rel,
-                "cpu_baseline": cpu, "decode": decode}
+                "cpu_baseline": cpu, "batched_gemv": batched, "decode": decode}
         print(json.dumps(line), flush=True)
     for tt in tensors:
         tt.free()

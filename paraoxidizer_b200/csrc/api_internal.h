@@ -20,6 +20,8 @@ struct pox_tensor {
     uint32_t* row_ptr = nullptr;  // outlier CSR by row [rows+1]
     uint2* entries = nullptr;     // (col, f32 bits of v - dequant(q))
     uint16_t* vals = nullptr;     // f16 outlier values (dequantization path)
+    uint32_t* tile_ptr = nullptr; // tiled INT4: outliers ordered by (row tile, 128-k block) [nT * nkb + 1]
+    uint32_t* tile_ent = nullptr; //   (row % 16) | (col % 128) << 4 | f16 value << 16
     size_t nnz = 0;
     void* scratch = nullptr;      // prepared x of the tiled GEMV (up to 8 batch rows)
     size_t scratch_bytes = 0;
@@ -60,8 +62,22 @@ int upload_tensor_locked(pox_cuda_ctx* ctx, const pox_tensor_desc* d, pox_tensor
 struct PrepOp;
 // GEMV of a resident tensor on device pointers; op fuses RMSNorm / SwiGLU into the x preparation
 // and resid (same shape as y, may alias it) is added to the result (tiled tensors only).
+// prepared = the x preparation was already written by the caller (gemv_x_target), x itself is
+// still passed (the GEMV's outlier correction reads it).
 int gemv_launch(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x, size_t batch, float* y, cudaStream_t st,
-                const PrepOp* op = nullptr, const float* resid = nullptr);
+                const PrepOp* op = nullptr, const float* resid = nullptr, bool prepared = false);
+// Where a kernel that produces the input of an INT4 tiled tensor's GEMV can write it prepared
+// (batch <= 8: the two-limb fixed point + meta; small-M path: swizzled f16 + row scales).
+struct XTarget {
+    uint8_t* cols = nullptr;
+    float2* meta = nullptr;
+    int Kp = 0, nxbs = 0;
+    uint8_t* xs = nullptr;
+    float* xscale = nullptr;
+    int Bp = 0;
+};
+int gemv_x_target(pox_cuda_ctx* ctx, const pox_tensor* t, size_t batch, cudaStream_t st, XTarget* out);
+bool gemv_uses_small_m(const pox_tensor* t, size_t batch);
 void destroy_ctx_extras(pox_cuda_ctx* ctx);
 // Small-M path scratch for a tensor of rows x cols at `batch` rows of x (grown outside stream
 // capture only; a captured graph keeps the buffers it was captured with).

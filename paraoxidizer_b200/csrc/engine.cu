@@ -6,8 +6,9 @@
 // Per layer: 4 GEMV launches on resident re-tiled weights (QKV and gate/up are concatenated at
 // load, so every projection row is computed exactly as in the separate tensors):
 //   qkv  = W_qkv  rmsnorm(x, attn_norm)            (norm fused into the GEMV's x preparation)
-//   rope(q, k); k, v -> KV pages at pos             (rope_append_kernel)
-//   att  = paged GQA attention over 0..=pos          (attn_split_kernel + attn_combine_kernel)
+//   att  = paged GQA attention over 0..=pos          (attn_decode_kernel: RoPE on q and k, k and v
+//          appended to the KV pages, split-context partials; attn_combine_kernel: the splits
+//          combined and written as the o projection's prepared input)
 //   x   += W_o att                                   (residual fused into the GEMV epilogue)
 //   gu   = W_gu   rmsnorm(x, mlp_norm)
 //   x   += W_down silu(g) * u                        (SwiGLU fused into the x preparation)
@@ -24,6 +25,7 @@
 #include "common.cuh"
 #include "gemv.cuh"
 #include "model.h"
+#include "tc05.cuh"
 
 #ifdef POX_HAVE_NCCL
 #include <nccl.h>
@@ -35,6 +37,8 @@ namespace pox {
 // sin(tok * 0.17) * 0.1 everywhere ----
 __global__ void embed_kernel(const uint32_t* __restrict__ tokens, const uint16_t* __restrict__ embed, int V, int H,
                              float* __restrict__ x) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int b = blockIdx.x;
     const uint32_t tok = tokens[b] % (uint32_t)V;
     const uint16_t* row = embed + (size_t)tok * H;
@@ -51,165 +55,175 @@ __global__ void embed_kernel(const uint32_t* __restrict__ tokens, const uint16_t
     }
 }
 
-// ---- RoPE (engine.rs:353-408, interleaved pairs) on q and k in place, then k and v into the KV
-// page of position pos (block_table[pos / 16], slot pos % 16) ----
-__global__ void rope_append_kernel(float* __restrict__ qkv, int qkv_rows, const uint32_t* __restrict__ pos,
-                                   const int32_t* __restrict__ btab, int mbps, __half* __restrict__ kc,
-                                   __half* __restrict__ vc, int layer, int L, int nq, int nkv, int hd, float theta) {
-    const int b = blockIdx.y, h = blockIdx.x;  // h < nq: q head; nq <= h < nq + nkv: kv head
-    const int i = threadIdx.x;                 // pair index < hd / 2
-    const uint32_t p = pos[b];
-    float* row = qkv + (size_t)b * qkv_rows;
+// ---- RoPE (engine.rs:353-408, interleaved pairs): cos / sin of pair i at position p ----
+__device__ __forceinline__ void rope_cs(uint32_t p, int i, int hd, float theta, float& c, float& s) {
     const float th = fmaxf(theta, 1.0f);
     const float exponent = __fdiv_rn((float)(2 * i), (float)hd);
     const float freq = __fdiv_rn(1.0f, powf(th, exponent));
     const float angle = __fmul_rn((float)p, freq);
-    float c = 1.0f, s = 0.0f;
+    c = 1.0f;
+    s = 0.0f;
     if (isfinite(angle)) {
         c = cosf(angle);
         s = sinf(angle);
     }
-    float* v = row + (size_t)h * hd;  // q heads, then k heads (k follows q in the fused projection)
-    const float a0 = v[2 * i], a1 = v[2 * i + 1];
-    const float r0 = __fsub_rn(__fmul_rn(a0, c), __fmul_rn(a1, s));
-    const float r1 = __fadd_rn(__fmul_rn(a0, s), __fmul_rn(a1, c));
-    v[2 * i] = r0;
-    v[2 * i + 1] = r1;
-    if (h >= nq) {
-        const int hk = h - nq;
-        const int blk = btab[(size_t)b * mbps + p / kPage];
-        const size_t off = ((((size_t)blk * L + layer) * nkv + hk) * kPage + p % kPage) * hd;
-        kc[off + 2 * i] = __float2half_rn(r0);
-        kc[off + 2 * i + 1] = __float2half_rn(r1);
-        const float* vv = row + (size_t)(nq + nkv + hk) * hd;
-        vc[off + 2 * i] = __float2half_rn(vv[2 * i]);
-        vc[off + 2 * i + 1] = __float2half_rn(vv[2 * i + 1]);
-    }
+}
+__device__ __forceinline__ float2 rope_pair(float a0, float a1, float c, float s) {
+    return make_float2(__fsub_rn(__fmul_rn(a0, c), __fmul_rn(a1, s)), __fadd_rn(__fmul_rn(a0, s), __fmul_rn(a1, c)));
 }
 
-// ---- paged GQA decode attention (engine.rs:580-641), split over the context ----
-// CTA (split, kv head, batch row): tokens [split * 128, min(ctx, +128)) for the G query heads of
-// this kv head. Scores: one token per lane (its K row read from the page), dot products against
-// q in shared memory; softmax partial over the split; V accumulation: one token at a time, dims
-// spread over lanes. Writes (max, sum, acc[hd]) per query head for the combine kernel.
+// ---- paged GQA decode attention (engine.rs:580-641), split over the context, RoPE and the KV
+// append fused in ----
+// CTA (split, kv head, batch row) takes tokens [64 split, min(ctx, 64 split + 64)) for the G query
+// heads of its kv head. q is roped into shared memory; the CTA whose split holds the new position
+// ropes k and writes k and v into the page (block_table[pos / 16], slot pos % 16) first. Warp w
+// takes the 16 tokens of one page: two lanes per token read its K row (one half each) and the
+// warp reads the 16 V rows, all issued before any use; scores, the split's softmax partial and
+// sum_t p_t v_t follow. Writes (max, sum, acc[hd]) per query head for the combine kernel.
 template <int HD>
-__global__ void __launch_bounds__(128) attn_split_kernel(const float* __restrict__ qkv, int qkv_rows,
-                                                         const uint32_t* __restrict__ pos,
-                                                         const int32_t* __restrict__ btab, int mbps,
-                                                         const __half* __restrict__ kc, const __half* __restrict__ vc,
-                                                         int layer, int L, int nq, int nkv, int G, int max_splits,
-                                                         float* __restrict__ apart) {
-    constexpr int DPL = HD / 32;  // dims per lane
+__global__ void __launch_bounds__(128) attn_decode_kernel(const float* __restrict__ qkv, int qkv_rows,
+                                                          const uint32_t* __restrict__ pos,
+                                                          const int32_t* __restrict__ btab, int mbps,
+                                                          __half* __restrict__ kc, __half* __restrict__ vc, int layer,
+                                                          int L, int nq, int nkv, int G, int max_splits, float theta,
+                                                          float* __restrict__ apart) {
+    constexpr int DH = HD / 2;   // K dims per lane (two lanes per token)
+    constexpr int DPL = HD / 32; // V dims per lane
+    pdl_launch_dependents();
+    pdl_wait();
     const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-    const int ctx = (int)pos[b] + 1;
+    const uint32_t p = pos[b];
+    const int ctx = (int)p + 1;
     const int t0 = split * kSplitTok;
-    if (t0 >= ctx) return;  // the combine kernel reads only ceil(ctx / 128) splits
-    const int t1 = min(ctx, t0 + kSplitTok);
-    const int nt = t1 - t0;
+    if (t0 >= ctx) return;  // the combine kernel reads only ceil(ctx / 64) splits
+    const int nt = min(ctx - t0, kSplitTok);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     __shared__ float qs[8][HD];
     __shared__ float ps[8][kSplitTok];
-    __shared__ float red[4][8];
+    __shared__ float red_m[4][8], red_l[4][8];
     __shared__ float acc_s[4][8][HD];
-    const float scale = 1.0f / sqrtf(fmaxf((float)HD, 1.0f));
-    const float* qrow = qkv + (size_t)b * qkv_rows + (size_t)h * G * HD;
-    for (int i = tid; i < G * HD; i += 128) qs[i / HD][i % HD] = qrow[i];
+    const float* row = qkv + (size_t)b * qkv_rows;
+    for (int j = tid; j < G * DH; j += 128) {
+        const int g = j / DH, i = j % DH;
+        float c, sn;
+        rope_cs(p, i, HD, theta, c, sn);
+        const float* q = row + (size_t)(h * G + g) * HD;
+        const float2 r = rope_pair(q[2 * i], q[2 * i + 1], c, sn);
+        qs[g][2 * i] = r.x;
+        qs[g][2 * i + 1] = r.y;
+    }
+    if ((int)p < t0 + kSplitTok) {  // this split holds the new position: append k, v
+        const int blk = btab[(size_t)b * mbps + p / kPage];
+        const size_t off = ((((size_t)blk * L + layer) * nkv + h) * kPage + p % kPage) * HD;
+        const float* k = row + (size_t)(nq + h) * HD;
+        const float* v = row + (size_t)(nq + nkv + h) * HD;
+        for (int i = tid; i < DH; i += 128) {
+            float c, sn;
+            rope_cs(p, i, HD, theta, c, sn);
+            const float2 r = rope_pair(k[2 * i], k[2 * i + 1], c, sn);
+            *reinterpret_cast<__half2*>(kc + off + 2 * i) = __floats2half2_rn(r.x, r.y);
+            *reinterpret_cast<__half2*>(vc + off + 2 * i) = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+        }
+    }
     __syncthreads();
 
-    // scores: token t0 + tid (128 threads = 128 tokens)
+    // this warp's page: tokens t0 + 16 warp .. + 15 (t0 is a multiple of 64, pages hold 16)
+    const int jt = 16 * warp + (lane & 15), hh = lane >> 4;
+    const int nw = max(0, min(16, nt - 16 * warp));  // valid tokens of this warp
+    uint4 kr[DH / 8];
+    uint2 vr[16];
+    if (nw > 0) {
+        const int blk = btab[(size_t)b * mbps + (t0 + 16 * warp) / kPage];
+        const size_t page = (((size_t)blk * L + layer) * nkv + h) * kPage * HD;
+        if ((lane & 15) < nw) {
+            const __half* kp = kc + page + (size_t)(lane & 15) * HD + hh * DH;
+#pragma unroll
+            for (int i = 0; i < DH / 8; i++) kr[i] = __ldcg(reinterpret_cast<const uint4*>(kp) + i);
+        }
+#pragma unroll
+        for (int u = 0; u < 16; u++) {
+            vr[u] = make_uint2(0u, 0u);
+            if (u < nw) {
+                const __half* vp = vc + page + (size_t)u * HD + DPL * lane;
+                if constexpr (DPL == 4) vr[u] = __ldcg(reinterpret_cast<const uint2*>(vp));
+                else if constexpr (DPL == 2) vr[u].x = __ldcg(reinterpret_cast<const unsigned int*>(vp));
+                else vr[u].x = __ldcg(reinterpret_cast<const unsigned short*>(vp));
+            }
+        }
+    }
+    const float scale = 1.0f / sqrtf(fmaxf((float)HD, 1.0f));
     float sc[8];
 #pragma unroll
-    for (int g = 0; g < 8; g++) sc[g] = -INFINITY;
-    if (tid < nt) {
-        const int t = t0 + tid;
-        const int blk = btab[(size_t)b * mbps + t / kPage];
-        const __half* kr = kc + ((((size_t)blk * L + layer) * nkv + h) * kPage + t % kPage) * HD;
-        float dot[8];
+    for (int g = 0; g < 8; g++) {
+        float dot = 0.f;
+        if (g < G && (lane & 15) < nw) {
 #pragma unroll
-        for (int g = 0; g < 8; g++) dot[g] = 0.f;
-#pragma unroll 4
-        for (int d0 = 0; d0 < HD; d0 += 8) {
-            const uint4 raw = *reinterpret_cast<const uint4*>(kr + d0);
-            const __half2* hp = reinterpret_cast<const __half2*>(&raw);
-            float kf[8];
+            for (int i = 0; i < DH / 8; i++) {
+                const __half2* hp = reinterpret_cast<const __half2*>(&kr[i]);
 #pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const float2 f = __half22float2(hp[j]);
-                kf[2 * j] = f.x;
-                kf[2 * j + 1] = f.y;
-            }
-#pragma unroll
-            for (int g = 0; g < 8; g++) {
-                if (g < G) {
-#pragma unroll
-                    for (int j = 0; j < 8; j++) dot[g] = fmaf(qs[g][d0 + j], kf[j], dot[g]);
+                for (int j = 0; j < 4; j++) {
+                    const float2 f = __half22float2(hp[j]);
+                    dot = fmaf(qs[g][hh * DH + 8 * i + 2 * j], f.x, dot);
+                    dot = fmaf(qs[g][hh * DH + 8 * i + 2 * j + 1], f.y, dot);
                 }
             }
         }
+        dot += __shfl_xor_sync(0xffffffffu, dot, 16);
+        sc[g] = (g < G && (lane & 15) < nw) ? dot * scale : -INFINITY;
+        float m = sc[g];
 #pragma unroll
-        for (int g = 0; g < 8; g++) sc[g] = dot[g] * scale;
+        for (int o = 8; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        if (lane == 0) red_m[warp][g] = m;
     }
-    // softmax partial: max and exp over the split
+    __syncthreads();
     float mx[8];
 #pragma unroll
     for (int g = 0; g < 8; g++) {
-        float m = sc[g];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        if (lane == 0) red[warp][g] = m;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int g = 0; g < 8; g++) {
-        mx[g] = fmaxf(fmaxf(red[0][g], red[1][g]), fmaxf(red[2][g], red[3][g]));
+        mx[g] = fmaxf(fmaxf(red_m[0][g], red_m[1][g]), fmaxf(red_m[2][g], red_m[3][g]));
         if (!isfinite(mx[g])) mx[g] = 0.f;
-    }
-    __syncthreads();
-    float l[8];
-#pragma unroll
-    for (int g = 0; g < 8; g++) {
-        float p = 0.f;
-        if (tid < nt && g < G) {
-            p = expf(sc[g] - mx[g]);
-            if (!isfinite(p)) p = 0.f;
-            ps[g][tid] = p;
+        float pv = 0.f;
+        if (g < G && (lane & 15) < nw) {
+            pv = expf(sc[g] - mx[g]);
+            if (!isfinite(pv)) pv = 0.f;
+            if (hh == 0) ps[g][jt] = pv;
         }
-        l[g] = warp_sum(p);
-        if (lane == 0) red[warp][g] = l[g];
+        float l = hh == 0 ? pv : 0.f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+        if (lane == 0) red_l[warp][g] = l;
     }
     __syncthreads();
-    // V accumulation: warp w takes tokens w, w + 4, ...; lane holds dims DPL * lane .. + DPL
+    // sum_t p_t v_t over this warp's tokens; lane holds dims DPL lane .. + DPL
     float acc[8][DPL];
 #pragma unroll
     for (int g = 0; g < 8; g++)
 #pragma unroll
-        for (int j = 0; j < DPL; j++) acc[g][j] = 0.f;
-    for (int j = warp; j < nt; j += 4) {
-        const int t = t0 + j;
-        const int blk = btab[(size_t)b * mbps + t / kPage];
-        const __half* vr = vc + ((((size_t)blk * L + layer) * nkv + h) * kPage + t % kPage) * HD + DPL * lane;
-        float vf[DPL];
-        if constexpr (DPL == 4) {
-            const uint2 raw = *reinterpret_cast<const uint2*>(vr);
-            const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
-            const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
-            vf[0] = f0.x;
-            vf[1] = f0.y;
-            vf[2] = f1.x;
-            vf[3] = f1.y;
-        } else if constexpr (DPL == 2) {
-            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(vr));
-            vf[0] = f.x;
-            vf[1] = f.y;
-        } else {
-            vf[0] = __half2float(vr[0]);
-        }
+        for (int q = 0; q < DPL; q++) acc[g][q] = 0.f;
 #pragma unroll
-        for (int g = 0; g < 8; g++) {
-            if (g < G) {
-                const float p = ps[g][j];
+    for (int u = 0; u < 16; u++) {
+        if (u < nw) {
+            float vf[DPL];
+            if constexpr (DPL == 4) {
+                const float2 f0 = __half22float2(*reinterpret_cast<const __half2*>(&vr[u].x));
+                const float2 f1 = __half22float2(*reinterpret_cast<const __half2*>(&vr[u].y));
+                vf[0] = f0.x;
+                vf[1] = f0.y;
+                vf[2] = f1.x;
+                vf[3] = f1.y;
+            } else if constexpr (DPL == 2) {
+                const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&vr[u].x));
+                vf[0] = f.x;
+                vf[1] = f.y;
+            } else {
+                vf[0] = __half2float(__ushort_as_half((unsigned short)vr[u].x));
+            }
 #pragma unroll
-                for (int q = 0; q < DPL; q++) acc[g][q] = fmaf(p, vf[q], acc[g][q]);
+            for (int g = 0; g < 8; g++) {
+                if (g < G) {
+                    const float pw = ps[g][16 * warp + u];
+#pragma unroll
+                    for (int q = 0; q < DPL; q++) acc[g][q] = fmaf(pw, vf[q], acc[g][q]);
+                }
             }
         }
     }
@@ -226,15 +240,34 @@ __global__ void __launch_bounds__(128) attn_split_kernel(const float* __restrict
     }
     if (tid < G) {
         out[(size_t)tid * (HD + 2)] = mx[tid];
-        out[(size_t)tid * (HD + 2) + 1] = (red[0][tid] + red[1][tid]) + (red[2][tid] + red[3][tid]);
+        out[(size_t)tid * (HD + 2) + 1] = (red_l[0][tid] + red_l[1][tid]) + (red_l[2][tid] + red_l[3][tid]);
     }
 }
 
-// Combines the splits of one (batch row, query head): out = sum_s e^(m_s - M) acc_s / sum_s e^(m_s - M) l_s
-// (the reference's 1 / sum_exp, 0 when the sum is <= 1e-9).
-__global__ void attn_combine_kernel(const uint32_t* __restrict__ pos, int nq, int nkv, int G, int hd, int max_splits,
-                                    const float* __restrict__ apart, float* __restrict__ att) {
-    const int hq = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+// Combines the splits of the attention output and prepares it as the o projection's input:
+// att = sum_s e^(m_s - M) acc_s / sum_s e^(m_s - M) l_s (the reference's 1 / sum_exp, 0 when the
+// sum is <= 1e-9). CTA (128-element block blk of the row, batch row b); thread d = element
+// 128 blk + d. Writes att (f32) and, for the GEMV that follows:
+//  * cols / meta (batch <= 8): the 15-bit two-limb fixed point of the block and (max/16383, sum),
+//    as xprep_int_kernel computes them;
+//  * xs (small-M path): f16(att) in the 128-byte-swizzled k-block-major layout, row scale 1 (|att|
+//    <= max|v| <= 65504, the f16 range, so no scaling is needed).
+struct OPrep {
+    uint8_t* cols = nullptr;
+    float2* meta = nullptr;
+    int Kp = 0, nxbs = 0;
+    uint8_t* xs = nullptr;
+    float* xscale = nullptr;
+    int Bp = 0;
+};
+__global__ void __launch_bounds__(128) attn_combine_kernel(const uint32_t* __restrict__ pos, int nq, int nkv, int G,
+                                                           int hd, int max_splits, const float* __restrict__ apart,
+                                                           float* __restrict__ att, OPrep op) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int blk = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+    const int e = blk * 128 + d, hq = e / hd, dd = e % hd;
+    if (e >= nq * hd) return;  // only when nq hd % 128 != 0, where nothing is prepared (no barrier below)
     const int ns = ((int)pos[b] + 1 + kSplitTok - 1) / kSplitTok;
     const int h = hq / G, g = hq % G;
     const float* base = apart + (((size_t)b * nkv + h) * max_splits * G + g) * (hd + 2);
@@ -243,13 +276,39 @@ __global__ void attn_combine_kernel(const uint32_t* __restrict__ pos, int nq, in
     for (int s = 0; s < ns; s++) M = fmaxf(M, base[s * sstride]);
     float num = 0.f, den = 0.f;
     for (int s = 0; s < ns; s++) {
-        const float* ps = base + s * sstride;
-        const float w = expf(ps[0] - M);
-        den = fmaf(w, ps[1], den);
-        if (d < hd) num = fmaf(w, ps[2 + d], num);
+        const float* pp = base + s * sstride;
+        const float w = expf(pp[0] - M);
+        den = fmaf(w, pp[1], den);
+        num = fmaf(w, pp[2 + dd], num);
     }
     const float inv = den > 1e-9f ? 1.0f / den : 0.f;
-    if (d < hd) att[((size_t)b * nq + hq) * hd + d] = num * inv;
+    const float v = num * inv;
+    const int K = nq * hd;
+    att[(size_t)b * K + e] = v;
+    if (op.cols) {
+        __shared__ float red[4];
+        const int warp = d >> 5, lane = d & 31;
+        float m = warp_max(fabsf(v));
+        if (lane == 0) red[warp] = m;
+        __syncthreads();
+        m = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+        __syncthreads();
+        const float qi = m > 0.f ? (float)kXLimbMax / m : 0.f;
+        const int X = max(-kXLimbMax, min(kXLimbMax, __float2int_rn(v * qi)));
+        op.cols[(size_t)(2 * b) * op.Kp + e] = (uint8_t)((uint32_t)(X >> 7) & 0xFFu);
+        op.cols[(size_t)(2 * b + 1) * op.Kp + e] = (uint8_t)((uint32_t)X & 0x7Fu);
+        const float sw = warp_sum(v);
+        if (lane == 0) red[warp] = sw;
+        __syncthreads();
+        if (d == 0)
+            op.meta[(size_t)b * op.nxbs + blk] =
+                make_float2(m > 0.f ? m / (float)kXLimbMax : 0.f, (red[0] + red[1]) + (red[2] + red[3]));
+    } else if (op.xs) {
+        const int kb = e >> 7, kk = e & 127;
+        const size_t off = ((size_t)kb * 2 + (kk >> 6)) * (size_t)op.Bp * 128 + sw128_off(b, (kk & 63) >> 3) + 2 * (kk & 7);
+        *reinterpret_cast<__half*>(op.xs + off) = __float2half_rn(v);
+        if (blk == 0 && d == 0) op.xscale[b] = 1.0f;
+    }
 }
 
 // Non-finite logits -> 0 (engine.rs:709-713), then greedy argmax: the first index of the maximum
@@ -264,6 +323,8 @@ __device__ __forceinline__ void first_max(float& v, int& i, float ov, int oi) {
 
 __global__ void __launch_bounds__(256) argmax_part_kernel(float* __restrict__ logits, int V, int chunk,
                                                           float2* __restrict__ part) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int p = blockIdx.x, b = blockIdx.y;
     float* lr = logits + (size_t)b * V;
     const int i1 = min(V, (p + 1) * chunk);
@@ -301,6 +362,8 @@ __global__ void __launch_bounds__(256) argmax_part_kernel(float* __restrict__ lo
 // (logit, token index in the whole vocabulary) for the pick across ranks.
 __global__ void argmax_final_kernel(const float2* __restrict__ part, int parts, int B, int vocab_off,
                                     uint32_t* __restrict__ next, float2* __restrict__ pairs) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int b = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
     if (b >= B) return;
     float bv = -INFINITY;
@@ -419,10 +482,10 @@ static void free_tensor(pox_cuda_ctx* ctx, pox_tensor*& t) {
 // the GEMV epilogue. Tensor parallel: each rank's GEMV writes its partial (rank 0's carrying the
 // residual) where exchange `call` expects it, and the exchange leaves the sum over ranks in x.
 static int row_split_gemv(pox_model* m, const pox_tensor* t, const float* xin, int B, int call, const PrepOp* op,
-                          cudaStream_t st) {
-    if (m->comm.tp == 1) return gemv_launch(m->ctx, t, xin, B, m->x, st, op, m->x);
+                          cudaStream_t st, bool prepared = false) {
+    if (m->comm.tp == 1) return gemv_launch(m->ctx, t, xin, B, m->x, st, op, m->x, prepared);
     float* y = comm_partial(m->comm, call, m->x);
-    int rc = gemv_launch(m->ctx, t, xin, B, y, st, op, m->comm.rank == 0 ? m->x : nullptr);
+    int rc = gemv_launch(m->ctx, t, xin, B, y, st, op, m->comm.rank == 0 ? m->x : nullptr, prepared);
     if (rc) return rc;
     return comm_allreduce(m->comm, call, 2 * m->L + 1, m->x, (size_t)B * m->H, st);
 }
@@ -432,8 +495,9 @@ static int decode_step(pox_model* m, int B, cudaStream_t st) {
     pox_cuda_ctx* ctx = m->ctx;
     int rc;
     if (m->comm.tp > 1 && !m->comm.mode) return set_error(POX_ERR_INVALID, "tensor-parallel exchange not set up");
-    embed_kernel<<<B, 256, 0, st>>>(m->tok, m->embed, m->V_full, m->H, m->x);
-    if ((rc = check_launch("embed"))) return rc;
+    cudaError_t le = launch_pdl(embed_kernel, dim3(B), dim3(256), 0, st, (const uint32_t*)m->tok,
+                                (const uint16_t*)m->embed, m->V_full, m->H, m->x);
+    if (le != cudaSuccess) return cuda_error(le, "embed launch");
     PrepOp norm;
     norm.mode = kPrepNorm;
     norm.eps = m->cfg.rms_eps;
@@ -442,28 +506,41 @@ static int decode_step(pox_model* m, int B, cudaStream_t st) {
         if (!w.qkv) return set_error(POX_ERR_INVALID, "layer %d has no weights", l);
         norm.norm_w = w.attn_norm;
         if ((rc = gemv_launch(ctx, w.qkv, m->x, B, m->qkv, st, &norm))) return rc;
-        rope_append_kernel<<<dim3(m->nq + m->nkv, B), m->hd / 2, 0, st>>>(
-            m->qkv, m->qkv_rows, m->pos, m->btab, (int)m->max_blocks_per_seq, m->kc, m->vc, l, m->L, m->nq, m->nkv,
-            m->hd, m->cfg.rope_theta);
-        if ((rc = check_launch("rope_append"))) return rc;
         const dim3 ag(m->max_splits, m->nkv, B);
+        cudaError_t e;
         if (m->hd == 128)
-            attn_split_kernel<128><<<ag, 128, 0, st>>>(m->qkv, m->qkv_rows, m->pos, m->btab, (int)m->max_blocks_per_seq,
-                                                      m->kc, m->vc, l, m->L, m->nq, m->nkv, m->G, m->max_splits,
-                                                      m->apart);
+            e = launch_pdl(attn_decode_kernel<128>, ag, dim3(128), 0, st, (const float*)m->qkv, m->qkv_rows,
+                           (const uint32_t*)m->pos, (const int32_t*)m->btab, (int)m->max_blocks_per_seq, m->kc, m->vc,
+                           l, m->L, m->nq, m->nkv, m->G, m->max_splits, m->cfg.rope_theta, m->apart);
         else if (m->hd == 64)
-            attn_split_kernel<64><<<ag, 128, 0, st>>>(m->qkv, m->qkv_rows, m->pos, m->btab, (int)m->max_blocks_per_seq,
-                                                     m->kc, m->vc, l, m->L, m->nq, m->nkv, m->G, m->max_splits,
-                                                     m->apart);
+            e = launch_pdl(attn_decode_kernel<64>, ag, dim3(128), 0, st, (const float*)m->qkv, m->qkv_rows,
+                           (const uint32_t*)m->pos, (const int32_t*)m->btab, (int)m->max_blocks_per_seq, m->kc, m->vc,
+                           l, m->L, m->nq, m->nkv, m->G, m->max_splits, m->cfg.rope_theta, m->apart);
         else
-            attn_split_kernel<32><<<ag, 128, 0, st>>>(m->qkv, m->qkv_rows, m->pos, m->btab, (int)m->max_blocks_per_seq,
-                                                     m->kc, m->vc, l, m->L, m->nq, m->nkv, m->G, m->max_splits,
-                                                     m->apart);
-        if ((rc = check_launch("attn_split"))) return rc;
-        attn_combine_kernel<<<dim3(m->nq, B), std::max(32, m->hd), 0, st>>>(m->pos, m->nq, m->nkv, m->G, m->hd,
-                                                                           m->max_splits, m->apart, m->att);
-        if ((rc = check_launch("attn_combine"))) return rc;
-        if ((rc = row_split_gemv(m, w.o, m->att, B, 2 * l, nullptr, st))) return rc;
+            e = launch_pdl(attn_decode_kernel<32>, ag, dim3(128), 0, st, (const float*)m->qkv, m->qkv_rows,
+                           (const uint32_t*)m->pos, (const int32_t*)m->btab, (int)m->max_blocks_per_seq, m->kc, m->vc,
+                           l, m->L, m->nq, m->nkv, m->G, m->max_splits, m->cfg.rope_theta, m->apart);
+        if (e != cudaSuccess) return cuda_error(e, "attention launch");
+        // the combine writes the o projection's prepared input when that tensor takes one
+        OPrep op;
+        XTarget xt;
+        const bool fuse = (m->nq * m->hd) % 128 == 0 && w.o->tiled && w.o->dtype == POX_I4 &&
+                          (size_t)B <= (gemv_uses_small_m(w.o, B) ? 128u : 8u) &&
+                          gemv_x_target(ctx, w.o, B, st, &xt) == POX_OK;
+        if (fuse) {
+            op.cols = xt.cols;
+            op.meta = xt.meta;
+            op.Kp = xt.Kp;
+            op.nxbs = xt.nxbs;
+            op.xs = xt.xs;
+            op.xscale = xt.xscale;
+            op.Bp = xt.Bp;
+        }
+        e = launch_pdl(attn_combine_kernel, dim3((m->nq * m->hd + 127) / 128, B), dim3(128), 0, st,
+                       (const uint32_t*)m->pos, m->nq, m->nkv, m->G, m->hd, m->max_splits, (const float*)m->apart,
+                       m->att, op);
+        if (e != cudaSuccess) return cuda_error(e, "attention combine launch");
+        if ((rc = row_split_gemv(m, w.o, m->att, B, 2 * l, nullptr, st, fuse))) return rc;
         norm.norm_w = w.mlp_norm;
         if ((rc = gemv_launch(ctx, w.gu, m->x, B, m->gu, st, &norm))) return rc;
         PrepOp sw;
@@ -477,12 +554,12 @@ static int decode_step(pox_model* m, int B, cudaStream_t st) {
     if ((rc = gemv_launch(ctx, m->lm_head, m->x, B, m->logits, st, &norm))) return rc;
     const int parts = std::min(kArgmaxParts, (m->V + 2047) / 2048);
     const int chunk = (m->V + parts - 1) / parts;
-    argmax_part_kernel<<<dim3(parts, B), 256, 0, st>>>(m->logits, m->V, chunk, m->amax);
-    if ((rc = check_launch("argmax"))) return rc;
+    le = launch_pdl(argmax_part_kernel, dim3(parts, B), dim3(256), 0, st, m->logits, m->V, chunk, m->amax);
+    if (le != cudaSuccess) return cuda_error(le, "argmax launch");
     const bool tp = m->comm.tp > 1;
-    argmax_final_kernel<<<(B + 7) / 8, 256, 0, st>>>(m->amax, parts, B, m->vocab_off, m->next,
-                                                    tp ? m->comm.pairs : nullptr);
-    if ((rc = check_launch("argmax"))) return rc;
+    le = launch_pdl(argmax_final_kernel, dim3((B + 7) / 8), dim3(256), 0, st, (const float2*)m->amax, parts, B,
+                    m->vocab_off, m->next, tp ? m->comm.pairs : (float2*)nullptr);
+    if (le != cudaSuccess) return cuda_error(le, "argmax launch");
     if (tp) return comm_pick(m->comm, 2 * m->L, 2 * m->L + 1, B, m->next, st);
     return POX_OK;
 }

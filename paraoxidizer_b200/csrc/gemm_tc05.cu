@@ -33,32 +33,47 @@
 
 namespace pox {
 
-constexpr int kTcStages = 2;     // A / B stages (one 128-k block each)
 constexpr int kTcProd = 8;       // producer warps (row tiles of 16 rows)
-constexpr int kTcThreads = (kTcProd + 1) * 32;
+constexpr int kTcThreads = (kTcProd + 2) * 32;  // + MMA warp + x loader warp
 constexpr int kErrWaitTc = 16;   // bit of the kernel error flag
 
 __host__ __device__ constexpr int tc_wbytes(int kind) { return kind == kKindI4 ? 1088 : kind == kKindI8 ? 2048 : 4096; }
-// weight stages per producer warp (about 32-64 KiB of rings per CTA)
+// Pipeline depths:
+//  A stages: dequantized 128-k weight blocks waiting for / read by the MMAs (32 KiB each); the
+//    producers run this many blocks ahead of the MMA completions;
+//  weight ring: bulk copies in flight per producer warp (HBM latency);
+//  x stages: x blocks in flight (L2 latency).
 __host__ __device__ constexpr int tc_ring(int kind) { return kind == kKindI4 ? 4 : kind == kKindI8 ? 3 : 2; }
+__host__ __device__ constexpr int tc_xstages(int N) { return N == 128 ? 2 : 3; }
+__host__ __device__ constexpr int tc_smem_bytes(int kind, int N, int A) {
+    return A * 32768 + tc_xstages(N) * N * 256 + kTcProd * tc_ring(kind) * tc_wbytes(kind) + 1024;
+}
+__host__ __device__ constexpr int tc_astages(int kind, int N) {  // the most that fit (at most 4)
+    return tc_smem_bytes(kind, N, 4) + 3072 <= 232448 ? 4 : tc_smem_bytes(kind, N, 3) + 3072 <= 232448 ? 3 : 2;
+}
 
 struct TcSmem {  // byte offsets in dynamic shared memory (1024-aligned base)
     int a, b, ring, bars, tmem, total;
 };
 __host__ __device__ inline TcSmem tc_smem(int kind, int N) {
     TcSmem s;
-    s.a = 0;                                         // kTcStages x 2 atoms x 128 rows x 128 B
-    s.b = s.a + kTcStages * 32768;                   // kTcStages x 2 atoms x N rows x 128 B
-    s.ring = s.b + kTcStages * N * 256;              // kTcProd x ring x wbytes
+    s.a = 0;                                         // A stages x 2 atoms x 128 rows x 128 B
+    s.b = s.a + tc_astages(kind, N) * 32768;         // x stages x 2 atoms x N rows x 128 B
+    s.ring = s.b + tc_xstages(N) * N * 256;          // kTcProd x ring x wbytes
     s.bars = s.ring + kTcProd * tc_ring(kind) * tc_wbytes(kind);
-    // barriers: full[S], xfull[S], empty[S], done, ring[kTcProd][ring]
-    s.tmem = s.bars + 8 * (3 * kTcStages + 1 + kTcProd * tc_ring(kind));
+    // barriers: full[A], empty[A], xfull[X], xempty[X], done, ring[kTcProd][ring]
+    s.tmem = s.bars + 8 * (2 * tc_astages(kind, N) + 2 * tc_xstages(N) + 1 + kTcProd * tc_ring(kind));
     s.total = s.tmem + 16;
     return s;
 }
 
 __device__ __forceinline__ void sts128(uint32_t a, uint4 v) {
     asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w) : "memory");
+}
+__device__ __forceinline__ uint32_t lds32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
 }
 __device__ __forceinline__ void sts16(uint32_t a, uint16_t v) {
     asm volatile("st.shared.u16 [%0], %1;" ::"r"(a), "h"(v) : "memory");
@@ -82,25 +97,31 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc05_kernel(TcArgs a) {
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     const TcSmem P = tc_smem(KIND, N);
     constexpr int kTcRing = tc_ring(KIND);
+    constexpr int kTcStages = tc_astages(KIND, N);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int rb = blockIdx.x, split = blockIdx.y;
     const int kb0 = (int)((long long)a.nkb * split / a.S), kb1 = (int)((long long)a.nkb * (split + 1) / a.S);
     const int nk = kb1 - kb0;
     const uint32_t sA = smem_u32(smem + P.a), sB = smem_u32(smem + P.b), sRing = smem_u32(smem + P.ring);
     const uint32_t bars = smem_u32(smem + P.bars);
+    constexpr int XS = tc_xstages(N);
     auto full = [&](int s) { return bars + 8 * s; };
-    auto xfull = [&](int s) { return bars + 8 * (kTcStages + s); };
-    auto empty = [&](int s) { return bars + 8 * (2 * kTcStages + s); };
-    const uint32_t done = bars + 8 * (3 * kTcStages);
-    auto ringbar = [&](int d, int r) { return bars + 8 * (3 * kTcStages + 1 + d * kTcRing + r); };
+    auto empty = [&](int s) { return bars + 8 * (kTcStages + s); };
+    auto xfull = [&](int s) { return bars + 8 * (2 * kTcStages + s); };
+    auto xempty = [&](int s) { return bars + 8 * (2 * kTcStages + XS + s); };
+    const uint32_t done = bars + 8 * (2 * kTcStages + 2 * XS);
+    auto ringbar = [&](int d, int r) { return bars + 8 * (2 * kTcStages + 2 * XS + 1 + d * kTcRing + r); };
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + P.tmem);
     __shared__ int s_abort;
 
     if (tid == 0) {
         for (int s = 0; s < kTcStages; s++) {
             mbar_init(full(s), kTcProd);
-            mbar_init(xfull(s), 1);
             mbar_init(empty(s), 1);
+        }
+        for (int s = 0; s < XS; s++) {
+            mbar_init(xfull(s), 1);
+            mbar_init(xempty(s), 1);
         }
         mbar_init(done, 1);
         for (int d = 0; d < kTcProd; d++)
@@ -125,12 +146,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc05_kernel(TcArgs a) {
         };
         if (live && lane == 0)
             for (int i = 0; i < kTcRing && i < nk; i++) issue(i);
-        // outlier cursor of row 16 T + lane (lanes 0..15), first entry at or after k-block kb0
-        uint32_t e_cur = 0, e_end = 0;
-        if (KIND == kKindI4 && a.row_ptr && live && lane < 16 && T * 16 + lane < a.Nout) {
-            e_cur = __ldg(a.row_ptr + T * 16 + lane);
-            e_end = __ldg(a.row_ptr + T * 16 + lane + 1);
-            while (e_cur < e_end && (int)__ldg(&a.ent[e_cur].x) < kb0 * 128) e_cur++;
+        // outliers of (row tile, k-block) kb0 + i: entries [tp[i], tp[i + 1]) of the tile-ordered
+        // table, each (row % 16) | (col % 128) << 4 | f16 value << 16; lane j holds entry j of the
+        // next k-block, loaded one k-block ahead
+        const bool has_out = KIND == kKindI4 && a.tile_ptr != nullptr && live;
+        const uint32_t* tp = has_out ? a.tile_ptr + (size_t)T * a.nkb + kb0 : nullptr;
+        uint32_t e0 = 0, e1 = 0, ent = 0;
+        if (has_out) {
+            e0 = __ldg(tp);
+            e1 = __ldg(tp + 1);
+            ent = e0 + lane < a.nnz ? __ldg(a.tile_ent + e0 + lane) : 0u;
         }
         const int g = lane >> 2, t = lane & 3;
         int i = 0;
@@ -148,14 +173,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc05_kernel(TcArgs a) {
                     const uint32_t row = 16 * d + g + 8 * hs;
                     if (KIND == kKindI4) {
                         const uint4 v = lds128(src + hs * 512 + lane * 16);
-                        const uint32_t sw = *reinterpret_cast<const uint32_t*>(smem + P.ring + d * kTcRing * TB +
-                                                                               r * TB + 1024 + 4 * (2 * g + hs));
+                        const uint32_t sw = lds32(src + 1024 + 4 * (2 * g + hs));
                         const uint32_t s2 = (sw & 0xFFFFu) * 0x10001u, m2 = (sw >> 16) * 0x10001u;
                         const uint32_t atom = stA + (t >> 1) * 16384;
                         const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+                        // lanes t and t + 2 of a quarter warp share a bank group for equal w: they
+                        // take the words in the order w ^ 2, so each quarter-warp store is one wavefront
+                        const int rot = t & 2;
 #pragma unroll
-                        for (int w = 0; w < 4; w++)
-                            sts128(atom + sw128_off(row, 4 * (t & 1) + w), i4_word_to_f16(wv[w], s2, m2));
+                        for (int w = 0; w < 4; w++) {
+                            const int ww = w ^ rot;
+                            const uint32_t wd = rot ? wv[w ^ 2] : wv[w];
+                            sts128(atom + sw128_off(row, 4 * (t & 1) + ww), i4_word_to_f16(wd, s2, m2));
+                        }
                     } else if (KIND == kKindI8) {
 #pragma unroll
                         for (int u = 0; u < 2; u++) {  // 64-k tiles u = atoms u
@@ -170,23 +200,31 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc05_kernel(TcArgs a) {
                         }
                     } else {
 #pragma unroll
-                        for (int u = 0; u < 4; u++) {  // 32-k tiles u: atom u / 2, chunks 4 (u % 2) + t
+                        for (int u0 = 0; u0 < 4; u0++) {  // 32-k tiles u: atom u / 2, chunks 4 (u % 2) + t
+                            const int u = u0 ^ (g & 1);   // rows g, g ^ 1 of a quarter warp: other half of the atom
                             const uint4 v = lds128(src + u * 1024 + hs * 512 + lane * 16);
                             sts128(stA + (u >> 1) * 16384 + sw128_off(row, 4 * (u & 1) + t), v);
                         }
                     }
                 }
-                if (KIND == kKindI4 && a.row_ptr) {
-                    __syncwarp();
-                    const int kend = (kb0 + i + 1) * 128;
-                    while (e_cur < e_end) {  // lanes 0..15: entries of row 16 T + lane in this k-block
-                        const int col = (int)__ldg(&a.ent[e_cur].x);
-                        if (col >= kend) break;
-                        const int kk = col - (kb0 + i) * 128;
-                        sts16(stA + (kk >> 6) * 16384 + sw128_off(16 * d + lane, (kk & 63) >> 3) + 2 * (kk & 7),
-                              __ldg(a.vals + e_cur));
-                        e_cur++;
+                if (has_out) {
+                    __syncwarp();  // the dequantized tile is written before values replace slots in it
+                    uint32_t n1 = 0, nent = 0;
+                    if (i + 1 < nk) {  // next k-block's range and first entries, in flight meanwhile
+                        n1 = __ldg(tp + i + 2);
+                        nent = e1 + lane < a.nnz ? __ldg(a.tile_ent + e1 + lane) : 0u;
                     }
+                    for (uint32_t base = e0; base < e1; base += 32) {
+                        const uint32_t v = base == e0 ? ent : (base + lane < e1 ? __ldg(a.tile_ent + base + lane) : 0u);
+                        if (base + lane < e1) {
+                            const uint32_t r = v & 15u, kk = (v >> 4) & 127u;
+                            sts16(stA + (kk >> 6) * 16384 + sw128_off(16 * d + r, (kk & 63) >> 3) + 2 * (kk & 7),
+                                  (uint16_t)(v >> 16));
+                        }
+                    }
+                    e0 = e1;
+                    e1 = n1;
+                    ent = nent;
                 }
                 __syncwarp();
                 if (lane == 0 && i + kTcRing < nk) {
@@ -214,6 +252,29 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc05_kernel(TcArgs a) {
                     for (int j = i; j < nk && j < i + kTcRing; j++) mbar_wait(ringbar(d, j % kTcRing), (j / kTcRing) & 1);
             }
         }
+    } else if (warp == kTcProd + 1) {
+        // ------------------------------ x loader ------------------------------
+        pdl_wait();  // x is written by the preceding kernel
+        if (lane == 0) {
+            const uint32_t xb = N * 256;
+            int i = 0;
+            bool ok = true;
+            for (; i < nk; i++) {
+                const int s = i % XS;
+                if (!mbar_wait(xempty(s), ((i / XS) & 1) ^ 1)) {  // MMAs of k-block i - XS done
+                    ok = false;
+                    break;
+                }
+                mbar_expect_tx(xfull(s), xb);
+                bulk_g2s(sB + s * xb, a.xs + (size_t)(kb0 + i) * xb, xb, xfull(s));
+            }
+            if (!ok) {
+                atomicOr(a.err, kErrWaitTc);
+                atomicExch(&s_abort, 1);
+                for (int j = max(0, i - XS); j < i; j++) mbar_wait(xfull(j % XS), (j / XS) & 1);  // in flight
+            }
+        }
+        __syncwarp();
     } else {
         // ------------------------------ MMA warp ------------------------------
         pdl_wait();  // x is written by the preceding kernel; TMEM is taken only after it finished
@@ -226,25 +287,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc05_kernel(TcArgs a) {
         if (lane == 0) {
             const uint32_t idesc = umma_idesc_f16(128, N);
             const uint32_t xb = N * 256;  // x bytes per 128-k block
-            auto issue_x = [&](int i) {
-                const int s = i % kTcStages;
-                mbar_expect_tx(xfull(s), xb);
-                bulk_g2s(sB + s * xb, a.xs + (size_t)(kb0 + i) * xb, xb, xfull(s));
-            };
-            int i = 0, issued = 0;
+            int i = 0;
             bool ok = true;
-            if (nk > 0) {
-                issue_x(0);
-                issued = 1;
-            }
-            for (; i < nk; i++) {
-                const int s = i % kTcStages;
-                if (i + 1 < nk) {  // stage of k-block i+1 is free once the MMAs of i+1-kTcStages completed
-                    if (!mbar_wait(empty((i + 1) % kTcStages), (((i + 1) / kTcStages) & 1) ^ 1)) { ok = false; break; }
-                    issue_x(i + 1);
-                    issued = i + 2;
-                }
-                if (!mbar_wait(full(s), (i / kTcStages) & 1) || !mbar_wait(xfull(s), (i / kTcStages) & 1)) {
+            for (; i < nk; i++) {  // never waits on an MMA completion: the loaders do
+                const int s = i % kTcStages, xs_ = i % XS;
+                if (!mbar_wait(full(s), (i / kTcStages) & 1) || !mbar_wait(xfull(xs_), (i / XS) & 1)) {
                     ok = false;
                     break;
                 }
@@ -252,19 +299,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc05_kernel(TcArgs a) {
 #pragma unroll
                 for (int at = 0; at < 2; at++) {
                     const uint64_t ad = umma_desc_sw128(sA + s * 32768 + at * 16384);
-                    const uint64_t bd = umma_desc_sw128(sB + s * xb + at * N * 128);
+                    const uint64_t bd = umma_desc_sw128(sB + xs_ * xb + at * N * 128);
 #pragma unroll
                     for (int k16 = 0; k16 < 4; k16++)
                         umma_f16(tmem, ad + 2 * k16, bd + 2 * k16, idesc, (i | at | k16) != 0);
                 }
                 umma_commit(empty(s));
+                umma_commit(xempty(xs_));
             }
             umma_commit(done);  // arrives when every MMA issued above has completed
             if (!ok) {
                 atomicOr(a.err, kErrWaitTc);
                 atomicExch(&s_abort, 1);
-                for (int j = i; j < issued; j++)  // x copies in flight
-                    mbar_wait(xfull(j % kTcStages), (j / kTcStages) & 1);
             }
         }
         __syncwarp();
@@ -280,52 +326,87 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc05_kernel(TcArgs a) {
             if (lane == 0) atomicOr(a.err, kErrWaitTc);
             atomicExch(&s_abort, 1);
         }
-        asm volatile("bar.sync 1, 128;" ::: "memory");  // one decision for the four epilogue warps
+    }
+    __syncthreads();  // one decision for the whole CTA
+    const bool go = !*(volatile int*)&s_abort;
+    if (go && warp < 4) {
         tc_fence_after();
-        if (!*(volatile int*)&s_abort) {
-            const uint32_t tmem = *tmem_slot;
-            const int row = rb * 128 + warp * 32 + lane;
-            float* dst = a.S > 1 ? a.ws + (size_t)split * a.Bp * a.Nout : a.y;
+        const uint32_t tmem = *tmem_slot;
+        const int row = rb * 128 + warp * 32 + lane;
+        float* dst = a.S > 1 ? a.ws + (size_t)split * a.Bp * a.Nout : a.y;
 #pragma unroll
-            for (int c0 = 0; c0 < N; c0 += 32) {
-                float v[32];
-                tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + c0, v);
-                if (row < a.Nout) {
+        for (int c0 = 0; c0 < N; c0 += 32) {
+            float v[32];
+            tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + c0, v);
+            if (row < a.Nout) {
 #pragma unroll
-                    for (int j = 0; j < 32; j++) {
-                        const int b = c0 + j;
-                        if (b < a.B) {
-                            if (a.S > 1) {
-                                dst[(size_t)b * a.Nout + row] = v[j];
-                            } else {
-                                float r = v[j] * a.xscale[b] * a.wscale;
-                                if (a.resid) r += a.resid[(size_t)b * a.Nout + row];
-                                dst[(size_t)b * a.Nout + row] = r;
-                            }
+                for (int j = 0; j < 32; j++) {
+                    const int b = c0 + j;
+                    if (b < a.B) {
+                        if (a.S > 1) {
+                            dst[(size_t)b * a.Nout + row] = v[j];
+                        } else {
+                            float r = v[j] * a.xscale[b] * a.wscale;
+                            if (a.resid) r += a.resid[(size_t)b * a.Nout + row];
+                            dst[(size_t)b * a.Nout + row] = r;
                         }
                     }
                 }
             }
-            if (a.S > 1) {
-                __threadfence();
-                asm volatile("bar.sync 1, 128;" ::: "memory");
-                __shared__ int s_last;
-                if (tid == 0) {
-                    const int prev = atomicAdd(a.tickets + rb, 1);
-                    s_last = prev == a.S - 1;
-                    if (s_last) a.tickets[rb] = 0;  // ready for the next launch
-                }
-                asm volatile("bar.sync 1, 128;" ::: "memory");
-                if (s_last && row < a.Nout) {
-                    __threadfence();
-                    for (int b = 0; b < a.B; b++) {
-                        float acc = 0.f;
-                        for (int sp = 0; sp < a.S; sp++)
-                            acc += __ldcg(a.ws + ((size_t)sp * a.Bp + b) * a.Nout + row);
-                        float r = acc * a.xscale[b] * a.wscale;
-                        if (a.resid) r += a.resid[(size_t)b * a.Nout + row];
-                        a.y[(size_t)b * a.Nout + row] = r;
+        }
+    }
+    if (go && a.S > 1) {
+        // the last CTA of the row block adds the S partials in split order (all 320 threads, two
+        // items of 4 rows per thread in flight, S loads each)
+        __shared__ int s_last;
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) {
+            const int prev = atomicAdd(a.tickets + rb, 1);
+            s_last = prev == a.S - 1;
+            if (s_last) a.tickets[rb] = 0;  // ready for the next launch
+        }
+        __syncthreads();
+        if (s_last) {
+            __threadfence();
+            const int r0 = rb * 128, nrow = min(128, a.Nout - r0);
+            const bool vec = (a.Nout & 3) == 0;
+            const int per_b = vec ? (nrow + 3) / 4 : nrow;  // items per batch row
+            const int items = a.B * per_b;
+            for (int it = tid; it < items; it += kTcThreads) {
+                const int b = it / per_b, q = it % per_b;
+                const float sc = a.xscale[b] * a.wscale;
+                if (vec) {
+                    const size_t o = (size_t)b * a.Nout + r0 + 4 * q;
+                    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                    float4 part[16];
+#pragma unroll
+                    for (int sp = 0; sp < 16; sp++)
+                        if (sp < a.S) part[sp] = __ldcg(reinterpret_cast<const float4*>(a.ws + (size_t)sp * a.Bp * a.Nout + o));
+#pragma unroll
+                    for (int sp = 0; sp < 16; sp++)
+                        if (sp < a.S) {
+                            acc.x += part[sp].x;
+                            acc.y += part[sp].y;
+                            acc.z += part[sp].z;
+                            acc.w += part[sp].w;
+                        }
+                    float4 r = make_float4(acc.x * sc, acc.y * sc, acc.z * sc, acc.w * sc);
+                    if (a.resid) {
+                        const float4 rr = *reinterpret_cast<const float4*>(a.resid + o);
+                        r.x += rr.x;
+                        r.y += rr.y;
+                        r.z += rr.z;
+                        r.w += rr.w;
                     }
+                    *reinterpret_cast<float4*>(a.y + o) = r;
+                } else {
+                    const size_t o = (size_t)b * a.Nout + r0 + q;
+                    float acc = 0.f;
+                    for (int sp = 0; sp < a.S; sp++) acc += __ldcg(a.ws + (size_t)sp * a.Bp * a.Nout + o);
+                    float r = acc * sc;
+                    if (a.resid) r += a.resid[o];
+                    a.y[o] = r;
                 }
             }
         }
@@ -419,7 +500,7 @@ size_t tc05_x_bytes(int K, int Bp) { return (size_t)(K / 128) * Bp * 256; }
 int tc05_splits(int nrb, int nkb, int sms) {
     int best = 1;
     double best_t = 1e30;
-    for (int S = 1; S <= 16 && S <= nkb; S++) {
+    for (int S = 1; S <= 16 && S <= nkb; S++) {  // at most 16: the reduction holds 16 partials
         const int waves = (nrb * S + sms - 1) / sms;
         const int per = (nkb + S - 1) / S;
         const double t = waves * (per + 3.0) + (S > 1 ? 2.0 : 0.0);

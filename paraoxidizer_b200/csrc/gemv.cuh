@@ -118,9 +118,9 @@ cudaError_t launch_apply_outliers(const uint32_t* row_ptr, const uint2* entries,
 // ---- small-M path (tcgen05): batch 9 .. 128 rows of x per launch (gemm_tc05.cu) ----
 struct TcArgs {
     const uint8_t* w;          // tile blobs (TileLayout of the kind; K % 128 == 0)
-    const uint32_t* row_ptr;   // INT4 outlier CSR by row (nullptr if none)
-    const uint2* ent;          // (col, ...) of each entry
-    const uint16_t* vals;      // f16 outlier value of each entry
+    const uint32_t* tile_ptr;  // INT4 outliers by (row tile, 128-k block): [nT * nkb + 1] (nullptr if none)
+    const uint32_t* tile_ent;  // (row % 16) | (col % 128) << 4 | f16 value << 16, in tile_ptr order
+    uint32_t nnz;
     const uint8_t* xs;         // prepared x: [K / 128][2][Bp][128 B], swizzled
     const float* xscale;       // [Bp] power-of-two scale of each x row
     float wscale;              // INT8 per-tensor scale (1 otherwise)

@@ -14,7 +14,7 @@
 namespace pox {
 
 constexpr int kPage = 16;       // tokens per KV page (paged_cache.rs DEFAULT_BLOCK_SIZE)
-constexpr int kSplitTok = 128;  // context tokens per attention CTA
+constexpr int kSplitTok = 64;   // context tokens per attention CTA (4 pages)
 constexpr int kArgmaxParts = 64;  // max blocks per row of the argmax's first pass
 
 struct LayerW {

@@ -107,12 +107,16 @@ static void free_tensor_mem(pox_tensor* t) {
     cudaFree(t->row_ptr);
     cudaFree(t->entries);
     cudaFree(t->vals);
+    cudaFree(t->tile_ptr);
+    cudaFree(t->tile_ent);
     cudaFree(t->scratch);
     t->scratch = nullptr;
     t->w = t->scales_dev = nullptr;
     t->row_ptr = nullptr;
     t->entries = nullptr;
     t->vals = nullptr;
+    t->tile_ptr = nullptr;
+    t->tile_ent = nullptr;
 }
 
 extern "C" void pox_cuda_destroy(pox_cuda_ctx* ctx) {
@@ -369,6 +373,22 @@ int pox::upload_tensor_locked(pox_cuda_ctx* ctx, const pox_tensor_desc* d, pox_t
             ent.push_back(make_uint2(0u, 0u));  // padding: the GEMV copies entries in 16-byte pairs
             ent.push_back(make_uint2(0u, 0u));
             if ((rc = upload_vec(ent, (void**)&t->entries, &t->bytes, st))) return fail(rc);
+            std::vector<uint32_t> tptr, tent;
+            if (t->tiled) {  // the same entries by (row tile, 128-k block), for the small-M path
+                const size_t nT = div_ceil(N, 16), nkb = K / 128;
+                tptr.assign(nT * nkb + 1, 0);
+                for (size_t r = 0; r < (size_t)N; r++)
+                    for (uint32_t e = rp[r]; e < rp[r + 1]; e++) tptr[(r / 16) * nkb + cols[e] / 128 + 1]++;
+                for (size_t i = 0; i + 1 < tptr.size(); i++) tptr[i + 1] += tptr[i];
+                tent.resize(cols.size());
+                std::vector<uint32_t> fill(tptr.begin(), tptr.end() - 1);
+                for (size_t r = 0; r < (size_t)N; r++)
+                    for (uint32_t e = rp[r]; e < rp[r + 1]; e++)
+                        tent[fill[(r / 16) * nkb + cols[e] / 128]++] =
+                            (uint32_t)(r & 15) | ((cols[e] & 127u) << 4) | ((uint32_t)vals[e] << 16);
+                if ((rc = upload_vec(tptr, (void**)&t->tile_ptr, &t->bytes, st))) return fail(rc);
+                if ((rc = upload_vec(tent, (void**)&t->tile_ent, &t->bytes, st))) return fail(rc);
+            }
             // the host vectors must outlive the async copies
             CKF(cudaStreamSynchronize(st), "cudaStreamSynchronize(upload)");
         }
@@ -494,7 +514,7 @@ int pox::ensure_tc_scratch(pox_cuda_ctx* ctx, size_t rows, size_t cols, size_t b
 
 // Small-M path: up to 128 rows of x per launch pair (x preparation + tcgen05 GEMM).
 static int tc05_gemv(pox_cuda_ctx* ctx, const pox_tensor* t, int kind, const float* x, size_t batch, float* y,
-                     cudaStream_t st, const PrepOp& op, const float* resid) {
+                     cudaStream_t st, const PrepOp& op, const float* resid, bool prepared) {
     const int N = (int)t->rows, K = (int)t->cols;
     const size_t ldx = op.ld_x ? (size_t)op.ld_x : t->cols;
     int rc = ensure_tc_scratch(ctx, t->rows, t->cols, batch, st);
@@ -511,13 +531,16 @@ static int tc05_gemv(pox_cuda_ctx* ctx, const pox_tensor* t, int kind, const flo
         float* ws = xscale + 256;
         PrepOp opb = op;
         if (opb.up) opb.up += done * (size_t)opb.ld_up;
-        cudaError_t e = launch_xprep_tc05(x + done * ldx, b, Bp, K, opb, xs, xscale, st);
-        if (e != cudaSuccess) return cuda_error(e, "x preparation launch");
+        cudaError_t e = cudaSuccess;
+        if (!prepared) {
+            e = launch_xprep_tc05(x + done * ldx, b, Bp, K, opb, xs, xscale, st);
+            if (e != cudaSuccess) return cuda_error(e, "x preparation launch");
+        }
         TcArgs a = {};
         a.w = (const uint8_t*)t->w;
-        a.row_ptr = kind == kKindI4 ? t->row_ptr : nullptr;
-        a.ent = t->entries;
-        a.vals = t->vals;
+        a.tile_ptr = kind == kKindI4 ? t->tile_ptr : nullptr;
+        a.tile_ent = t->tile_ent;
+        a.nnz = (uint32_t)t->nnz;
         a.xs = xs;
         a.xscale = xscale;
         a.wscale = kind == kKindI8 ? t->i8_scale : 1.0f;
@@ -549,8 +572,33 @@ static int tc05_min_batch() {
     return v;
 }
 
+bool pox::gemv_uses_small_m(const pox_tensor* t, size_t batch) {
+    return t->tiled && t->cols % 128 == 0 && batch >= (size_t)tc05_min_batch();
+}
+
+int pox::gemv_x_target(pox_cuda_ctx* ctx, const pox_tensor* t, size_t batch, cudaStream_t st, XTarget* out) {
+    *out = XTarget();
+    if (!t->tiled || t->dtype != POX_I4 || t->cols % 128 != 0) return set_error(POX_ERR_UNSUPPORTED, "no prepared-x path");
+    if (gemv_uses_small_m(t, batch)) {
+        if (batch > 128) return set_error(POX_ERR_UNSUPPORTED, "prepared x holds up to 128 rows");
+        int rc = ensure_tc_scratch(ctx, t->rows, t->cols, batch, st);
+        if (rc) return rc;
+        out->Bp = tc05_pad((int)batch);
+        out->xs = static_cast<uint8_t*>(ctx->tc_scratch);
+        out->xscale = reinterpret_cast<float*>(out->xs + ((tc05_x_bytes((int)t->cols, out->Bp) + 255) & ~(size_t)255));
+        return POX_OK;
+    }
+    if (batch > (size_t)kMaxBatch) return set_error(POX_ERR_UNSUPPORTED, "prepared x holds up to 8 rows");
+    const XPrep xp = xprep_view(t->scratch, kKindI4, (int)t->cols);
+    out->cols = static_cast<uint8_t*>(xp.cols);
+    out->meta = xp.meta;
+    out->Kp = xp.Kp;
+    out->nxbs = xp.nxbs;
+    return POX_OK;
+}
+
 int pox::gemv_launch(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x, size_t batch, float* y,
-                     cudaStream_t st, const PrepOp* op_in, const float* resid) {
+                     cudaStream_t st, const PrepOp* op_in, const float* resid, bool prepared) {
     if (t->rows == 0 || t->cols == 0 || batch == 0) return POX_OK;
     if (((uintptr_t)x & 15) != 0) return set_error(POX_ERR_INVALID, "x must be 16-byte aligned");
     const PrepOp op = op_in ? *op_in : PrepOp();
@@ -558,8 +606,9 @@ int pox::gemv_launch(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x, siz
         return set_error(POX_ERR_UNSUPPORTED, "fused pre-ops need a tensor in the tiled layout");
     const int kind = t->dtype == POX_I4 ? kKindI4 : (t->dtype == POX_I8 ? kKindI8 : kKindF16);
     const int N = (int)t->rows, K = (int)t->cols;
-    if (t->tiled && K % 128 == 0 && batch >= (size_t)tc05_min_batch())
-        return tc05_gemv(ctx, t, kind, x, batch, y, st, op, resid);
+    if (prepared && (op.mode != kPrepNone || batch > (gemv_uses_small_m(t, batch) ? 128u : (size_t)kMaxBatch)))
+        return set_error(POX_ERR_INVALID, "prepared x: no pre-op, at most one launch of rows");
+    if (gemv_uses_small_m(t, batch)) return tc05_gemv(ctx, t, kind, x, batch, y, st, op, resid, prepared);
     const size_t ldx = op.ld_x ? (size_t)op.ld_x : t->cols;
     size_t done = 0;
     while (done < batch) {
@@ -572,8 +621,10 @@ int pox::gemv_launch(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x, siz
         if (t->tiled) {
             const TileLayout TL(kind, N, K);
             const XPrep xp = xprep_view(t->scratch, kind, K);
-            e = launch_xprep(kind, xb, (int)b, K, xp, opb, true, st);
-            if (e != cudaSuccess) return cuda_error(e, "x preparation launch");
+            if (!prepared) {
+                e = launch_xprep(kind, xb, (int)b, K, xp, opb, true, st);
+                if (e != cudaSuccess) return cuda_error(e, "x preparation launch");
+            }
             GemvArgs a = {};
             a.w = (const uint8_t*)t->w;
             a.i8_scale = t->i8_scale;

@@ -38,17 +38,21 @@ def be():
     b.close()
 
 
-@pytest.mark.parametrize("name,outliers", [("hd128", None), ("hd128", "automatic"), ("fixture", None),
-                                           ("hd64", "aggressive")])
-def test_decode_matches_forward_token(be, name, outliers):
+@pytest.mark.parametrize("name,outliers,nseq", [("hd128", None, 3), ("hd128", "automatic", 3), ("fixture", None, 3),
+                                                ("hd64", "aggressive", 3), ("hd128", "automatic", 11),
+                                                ("hd64", None, 10)])
+def test_decode_matches_forward_token(be, name, outliers, nseq):
+    """nseq 3: the batch <= 8 GEMV path; nseq 10-11: the small-M tensor-core path (batch >= 9
+    while every sequence is active)."""
     cfg = CONFIGS[name]
     w = make_llama(cfg, seed=11, outlier_policy=outliers, norm_jitter=0.1)
-    model = CudaModel(be, cfg, max_batch=3, kv_blocks=48, max_blocks_per_seq=16)
+    model = CudaModel(be, cfg, max_batch=nseq, kv_blocks=16 * nseq, max_blocks_per_seq=16)
     load_into(model, w)
     ow = oracle_weights(w)
     rng = np.random.default_rng(5)
-    # three sequences; one runs past 128 positions so attention uses two context splits
-    prompts = [list(rng.integers(0, cfg["vocab"], n)) for n in (6, 150, 21)]
+    # sequences of different lengths; one runs past 128 positions so attention uses several splits
+    lens = (6, 150, 21) if nseq == 3 else tuple(int(v) for v in rng.integers(12, 40, nseq - 1)) + (140,)
+    prompts = [list(rng.integers(0, cfg["vocab"], n)) for n in lens]
     steps = 12
     oracles = [O.OracleModel(cfg, ow, max_seq=256, kv_f16=True) for _ in prompts]
     seqs = [model.new_sequence() for _ in prompts]

@@ -384,7 +384,7 @@ def run_decode_only(args):
     from paraoxidizer_b200.backend import CudaBackend
 
     be = CudaBackend.create(local)
-    bg = batched_gemv_bench(be) if world == 1 else None
+    bg = batched_gemv_bench(be) if world == 1 and args.with_batched else None
     d = decode_bench(be, batches=decode_batches(args), prefill=args.decode_prefill, steps=args.decode_steps,
                      world=world, rank=rank)
     if rank == 0:
@@ -551,6 +551,7 @@ def main():
     ap.add_argument("--no-decode", action="store_true", help="skip the Llama-8B-architecture decode benchmark")
     ap.add_argument("--decode-only", action="store_true",
                     help="run only the decode benchmark (one JSON object; for launch lists and captures)")
+    ap.add_argument("--with-batched", action="store_true", help="--decode-only: also run the batched GEMV bench")
     ap.add_argument("--decode-batches", default="1,8,32")
     ap.add_argument("--decode-prefill", type=int, default=512)
     ap.add_argument("--decode-steps", type=int, default=256)

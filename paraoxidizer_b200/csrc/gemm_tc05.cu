@@ -420,69 +420,82 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc05_kernel(TcArgs a) {
 }
 
 // ------------------------------------------------------------------------------------------
-// x preparation: one CTA per row n < Bp of the padded batch. Row n < B: v = op(x_n); e such that
+// x preparation: one CTA of 1024 threads per row n < Bp of the padded batch. Row n < B:
+// v = op(x_n) is computed once into shared memory together with the row's sum of squares and
+// max|v| (RMSNorm: the scale 1/rms is common to the row, so max|x w| gives max|v|); e such that
 // max|v| 2^-e lies in [2^13, 2^14) (e = 0 for an all-zero row); writes f16(v 2^-e) into the
 // k-block-major, 128-byte-swizzled layout [kb][atom][Bp rows][128 B] and xscale[n] = 2^e. Rows
 // B .. Bp-1 are zero.
 // ------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) xprep_tc05_kernel(const float* __restrict__ x, int B, int Bp, int K,
-                                                         PrepOp op, uint8_t* __restrict__ xs,
-                                                         float* __restrict__ xscale) {
+constexpr int kXpThreads = 1024;
+__global__ void __launch_bounds__(kXpThreads) xprep_tc05_kernel(const float* __restrict__ x, int B, int Bp, int K,
+                                                                PrepOp op, uint8_t* __restrict__ xs,
+                                                                float* __restrict__ xscale) {
+    extern __shared__ float vs[];  // [K]
     pdl_launch_dependents();
     pdl_wait();
-    const int n = blockIdx.x, tid = threadIdx.x;
-    __shared__ float red[8];
-    __shared__ float s_inv, s_scale;
-    const float* xr = x + (size_t)n * op.ld_x;
-    const float* ur = op.up ? op.up + (size_t)n * op.ld_up : nullptr;
-    auto elem = [&](int k, float inv) -> float {
-        const float v = xr[k];
-        if (op.mode == kPrepNorm) {
-            const float t = v * inv;
-            return op.norm_w ? t * half_bits_to_float(op.norm_w[k]) : t;
-        }
-        if (op.mode == kPrepSwiGLU) return v / (1.0f + expf(-v)) * ur[k];
-        return v;
-    };
-    float inv = 1.f, scale = 0.f;
+    const int n = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    __shared__ float red_s[32], red_m[32];
+    __shared__ float s_mul;
     if (n < B) {
-        if (op.mode == kPrepNorm) {  // same fixed-order sum as the GEMV's x preparation
-            if (tid < 32) {
-                const float r = row_rms_inv(xr, K, op.eps);
-                if (tid == 0) s_inv = r;
+        const float* xr = x + (size_t)n * op.ld_x;
+        const float* ur = op.up ? op.up + (size_t)n * op.ld_up : nullptr;
+        float ss = 0.f, m = 0.f;
+        for (int k = 4 * tid; k < K; k += 4 * kXpThreads) {  // K % 128 == 0
+            float4 v = *reinterpret_cast<const float4*>(xr + k);
+            float e[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                if (op.mode == kPrepNorm) {
+                    ss = fmaf(e[j], e[j], ss);
+                    if (op.norm_w) e[j] *= half_bits_to_float(op.norm_w[k + j]);  // x w; 1/rms applied below
+                } else if (op.mode == kPrepSwiGLU) {
+                    e[j] = e[j] / (1.0f + expf(-e[j])) * ur[k + j];
+                }
+                m = fmaxf(m, fabsf(e[j]));
             }
-            __syncthreads();
-            inv = s_inv;
+            *reinterpret_cast<float4*>(vs + k) = make_float4(e[0], e[1], e[2], e[3]);
         }
-        float m = 0.f;
-        for (int k = tid; k < K; k += 256) m = fmaxf(m, fabsf(elem(k, inv)));
+        ss = warp_sum(ss);
         m = warp_max(m);
-        if ((tid & 31) == 0) red[tid >> 5] = m;
+        if (lane == 0) {
+            red_s[warp] = ss;
+            red_m[warp] = m;
+        }
         __syncthreads();
         if (tid == 0) {
-            float mm = 0.f;
-            for (int w = 0; w < 8; w++) mm = fmaxf(mm, red[w]);
+            float sst = 0.f, mm = 0.f;
+            for (int w = 0; w < kXpThreads / 32; w++) {
+                sst += red_s[w];
+                mm = fmaxf(mm, red_m[w]);
+            }
+            float inv = 1.f;
+            if (op.mode == kPrepNorm) {
+                inv = 1.0f / sqrtf(sst / (float)K + op.eps);
+                mm *= inv;
+            }
             int e = 0;
             if (mm > 0.f && isfinite(mm)) {
                 frexpf(mm, &e);  // mm in [2^(e-1), 2^e)
                 e -= 14;
             }
-            s_scale = ldexpf(1.f, e);
             xscale[n] = ldexpf(1.f, e);
+            s_mul = inv * ldexpf(1.f, -e);  // 1/rms (or 1) times the power-of-two scale
         }
         __syncthreads();
-        scale = 1.f / s_scale;  // a power of two: exact
     }
-    // writes: thread handles 8 consecutive k (one 16-byte chunk) per iteration
-    for (int c = tid; c < K / 8; c += 256) {
+    const float mul = n < B ? s_mul : 0.f;
+    for (int c = tid; c < K / 8; c += kXpThreads) {  // one 16-byte chunk of 8 consecutive k
         const int k = c * 8, kb = k >> 7, kk = k & 127;
         uint32_t h[4] = {0u, 0u, 0u, 0u};
         if (n < B) {
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const __half2 p = __floats2half2_rn(elem(k + 2 * j, inv) * scale, elem(k + 2 * j + 1, inv) * scale);
-                h[j] = *reinterpret_cast<const uint32_t*>(&p);
-            }
+            const float4 a0 = *reinterpret_cast<const float4*>(vs + k), a1 = *reinterpret_cast<const float4*>(vs + k + 4);
+            const __half2 p0 = __floats2half2_rn(a0.x * mul, a0.y * mul), p1 = __floats2half2_rn(a0.z * mul, a0.w * mul);
+            const __half2 p2 = __floats2half2_rn(a1.x * mul, a1.y * mul), p3 = __floats2half2_rn(a1.z * mul, a1.w * mul);
+            h[0] = *reinterpret_cast<const uint32_t*>(&p0);
+            h[1] = *reinterpret_cast<const uint32_t*>(&p1);
+            h[2] = *reinterpret_cast<const uint32_t*>(&p2);
+            h[3] = *reinterpret_cast<const uint32_t*>(&p3);
         }
         const size_t off = ((size_t)kb * 2 + (kk >> 6)) * (size_t)Bp * 128 + sw128_off(n, (kk & 63) >> 3);
         *reinterpret_cast<uint4*>(xs + off) = make_uint4(h[0], h[1], h[2], h[3]);
@@ -553,9 +566,16 @@ cudaError_t launch_xprep_tc05(const float* x, int B, int Bp, int K, const PrepOp
                               cudaStream_t st) {
     PrepOp op = op_in;
     if (op.ld_x == 0) op.ld_x = K;
+    const size_t smem = (size_t)K * sizeof(float);
+    if (smem > 48 * 1024) {
+        const cudaError_t e = cudaFuncSetAttribute(xprep_tc05_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   (int)smem);
+        if (e != cudaSuccess) return e;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)Bp, 1, 1);
-    cfg.blockDim = dim3(256, 1, 1);
+    cfg.blockDim = dim3(kXpThreads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

@@ -573,7 +573,8 @@ static int tc05_min_batch() {
 }
 
 bool pox::gemv_uses_small_m(const pox_tensor* t, size_t batch) {
-    return t->tiled && t->cols % 128 == 0 && batch >= (size_t)tc05_min_batch();
+    // the x preparation stages one row (cols floats) in shared memory
+    return t->tiled && t->cols % 128 == 0 && t->cols <= 53248 && batch >= (size_t)tc05_min_batch();
 }
 
 int pox::gemv_x_target(pox_cuda_ctx* ctx, const pox_tensor* t, size_t batch, cudaStream_t st, XTarget* out) {
@@ -606,6 +607,7 @@ int pox::gemv_launch(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x, siz
         return set_error(POX_ERR_UNSUPPORTED, "fused pre-ops need a tensor in the tiled layout");
     const int kind = t->dtype == POX_I4 ? kKindI4 : (t->dtype == POX_I8 ? kKindI8 : kKindF16);
     const int N = (int)t->rows, K = (int)t->cols;
+    (void)K;
     if (prepared && (op.mode != kPrepNone || batch > (gemv_uses_small_m(t, batch) ? 128u : (size_t)kMaxBatch)))
         return set_error(POX_ERR_INVALID, "prepared x: no pre-op, at most one launch of rows");
     if (gemv_uses_small_m(t, batch)) return tc05_gemv(ctx, t, kind, x, batch, y, st, op, resid, prepared);

@@ -38,15 +38,18 @@ constexpr int kTcThreads = (kTcProd + 2) * 32;  // + MMA warp + x loader warp
 constexpr int kErrWaitTc = 16;   // bit of the kernel error flag
 
 __host__ __device__ constexpr int tc_wbytes(int kind) { return kind == kKindI4 ? 1088 : kind == kKindI8 ? 2048 : 4096; }
+// 128-k blocks per weight copy: a copy costs its warp a fixed overhead whatever its size, so a
+// producer moves about 4 KiB at a time (consecutive k-blocks of its row tile are contiguous).
+__host__ __device__ constexpr int tc_group(int kind) { return kind == kKindI4 ? 4 : kind == kKindI8 ? 2 : 1; }
 // Pipeline depths:
 //  A stages: dequantized 128-k weight blocks waiting for / read by the MMAs (32 KiB each); the
 //    producers run this many blocks ahead of the MMA completions;
-//  weight ring: bulk copies in flight per producer warp (HBM latency);
+//  weight ring: copies (of tc_group k-blocks) in flight per producer warp (HBM latency);
 //  x stages: x blocks in flight (L2 latency).
-__host__ __device__ constexpr int tc_ring(int kind) { return kind == kKindI4 ? 4 : kind == kKindI8 ? 3 : 2; }
+__host__ __device__ constexpr int tc_ring(int) { return 2; }
 __host__ __device__ constexpr int tc_xstages(int N) { return N == 128 ? 2 : 3; }
 __host__ __device__ constexpr int tc_smem_bytes(int kind, int N, int A) {
-    return A * 32768 + tc_xstages(N) * N * 256 + kTcProd * tc_ring(kind) * tc_wbytes(kind) + 1024;
+    return A * 32768 + tc_xstages(N) * N * 256 + kTcProd * tc_ring(kind) * tc_group(kind) * tc_wbytes(kind) + 1024;
 }
 __host__ __device__ constexpr int tc_astages(int kind, int N) {  // the most that fit (at most 4)
     return tc_smem_bytes(kind, N, 4) + 3072 <= 232448 ? 4 : tc_smem_bytes(kind, N, 3) + 3072 <= 232448 ? 3 : 2;
@@ -59,8 +62,8 @@ __host__ __device__ inline TcSmem tc_smem(int kind, int N) {
     TcSmem s;
     s.a = 0;                                         // A stages x 2 atoms x 128 rows x 128 B
     s.b = s.a + tc_astages(kind, N) * 32768;         // x stages x 2 atoms x N rows x 128 B
-    s.ring = s.b + tc_xstages(N) * N * 256;          // kTcProd x ring x wbytes
-    s.bars = s.ring + kTcProd * tc_ring(kind) * tc_wbytes(kind);
+    s.ring = s.b + tc_xstages(N) * N * 256;          // kTcProd x ring x group x wbytes
+    s.bars = s.ring + kTcProd * tc_ring(kind) * tc_group(kind) * tc_wbytes(kind);
     // barriers: full[A], empty[A], xfull[X], xempty[X], done, ring[kTcProd][ring]
     s.tmem = s.bars + 8 * (2 * tc_astages(kind, N) + 2 * tc_xstages(N) + 1 + kTcProd * tc_ring(kind));
     s.total = s.tmem + 16;
@@ -133,19 +136,22 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc05_kernel(TcArgs a) {
     pdl_launch_dependents();
 
     const int TB = tc_wbytes(KIND);
+    constexpr int GK = tc_group(KIND);
+    const int SBy = GK * TB;  // bytes per ring stage
     if (warp < kTcProd) {
         // ------------------------------ producer warp d ------------------------------
         const int d = warp, T = rb * 8 + d;  // row tile
         const bool live = T < a.nT;
         const uint8_t* wsrc = a.w + ((size_t)T * a.nkb + kb0) * TB;
-        const uint32_t ring = sRing + d * kTcRing * TB;
-        auto issue = [&](int i) {  // lane 0: weights of k-block kb0 + i into ring stage i % kTcRing
-            const uint32_t bar = ringbar(d, i % kTcRing);
-            mbar_expect_tx(bar, TB);
-            bulk_g2s(ring + (i % kTcRing) * TB, wsrc + (size_t)i * TB, TB, bar);
+        const uint32_t ring = sRing + d * kTcRing * SBy;
+        auto issue = [&](int gi) {  // lane 0: k-blocks kb0 + GK gi .. (one copy) into ring stage gi % kTcRing
+            const uint32_t bar = ringbar(d, gi % kTcRing);
+            const uint32_t bytes = (uint32_t)min(GK, nk - gi * GK) * TB;
+            mbar_expect_tx(bar, bytes);
+            bulk_g2s(ring + (gi % kTcRing) * SBy, wsrc + (size_t)gi * GK * TB, bytes, bar);
         };
         if (live && lane == 0)
-            for (int i = 0; i < kTcRing && i < nk; i++) issue(i);
+            for (int gi = 0; gi < kTcRing && gi * GK < nk; gi++) issue(gi);
         // outliers of (row tile, k-block) kb0 + i: entries [tp[i], tp[i + 1]) of the tile-ordered
         // table, each (row % 16) | (col % 128) << 4 | f16 value << 16; lane j holds entry j of the
         // next k-block, loaded one k-block ahead
@@ -165,9 +171,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc05_kernel(TcArgs a) {
             if (!__all_sync(0xffffffffu, mbar_wait(empty(s), ((i / kTcStages) & 1) ^ 1))) { ok = false; break; }
             const uint32_t stA = sA + s * 32768;
             if (live) {
-                const int r = i % kTcRing;
-                if (!__all_sync(0xffffffffu, mbar_wait(ringbar(d, r), (i / kTcRing) & 1))) { ok = false; break; }
-                const uint32_t src = ring + r * TB;
+                const int gi = i / GK, r = gi % kTcRing;
+                if (i % GK == 0 &&
+                    !__all_sync(0xffffffffu, mbar_wait(ringbar(d, r), (gi / kTcRing) & 1))) { ok = false; break; }
+                const uint32_t src = ring + r * SBy + (i % GK) * TB;
 #pragma unroll
                 for (int hs = 0; hs < 2; hs++) {  // rows g (hs 0) and g + 8 (hs 1) of the tile
                     const uint32_t row = 16 * d + g + 8 * hs;
@@ -227,9 +234,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc05_kernel(TcArgs a) {
                     ent = nent;
                 }
                 __syncwarp();
-                if (lane == 0 && i + kTcRing < nk) {
+                if (lane == 0 && (i % GK == GK - 1 || i + 1 == nk) && (gi + kTcRing) * GK < nk) {
                     fence_proxy_async_smem();  // reads of the ring stage done before its refill
-                    issue(i + kTcRing);
+                    issue(gi + kTcRing);
                 }
             } else {
                 // rows beyond the tensor: zero weights
@@ -249,7 +256,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc05_kernel(TcArgs a) {
                 atomicOr(a.err, kErrWaitTc);
                 atomicExch(&s_abort, 1);
                 if (live)  // copies issued but not consumed: wait for them (bounded) before exiting
-                    for (int j = i; j < nk && j < i + kTcRing; j++) mbar_wait(ringbar(d, j % kTcRing), (j / kTcRing) & 1);
+                    for (int gj = i / GK; gj * GK < nk && gj < i / GK + kTcRing; gj++)
+                        mbar_wait(ringbar(d, gj % kTcRing), (gj / kTcRing) & 1);
             }
         }
     } else if (warp == kTcProd + 1) {

@@ -142,24 +142,6 @@ __device__ __forceinline__ float warp_max(float v) {
     return v;
 }
 
-// Per-row RMSNorm scale, computed by a whole warp in a fixed order (every warp of the row gets the
-// same value): lane-sequential sums over k = 4 lane + 128 j, then a butterfly.
-__device__ __forceinline__ float row_rms_inv(const float* x, int K, float eps) {
-    const int lane = threadIdx.x & 31;
-    float s = 0.f;
-    for (int k = 4 * lane; k < K; k += 128) {
-        const float4 v = *reinterpret_cast<const float4*>(x + k);
-        s = fmaf(v.x, v.x, s);
-        s = fmaf(v.y, v.y, s);
-        s = fmaf(v.z, v.z, s);
-        s = fmaf(v.w, v.w, s);
-    }
-    s = warp_sum(s);
-    const float rms = sqrtf(s / (float)K + eps);
-    return 1.0f / rms;
-}
-
-
 __device__ __forceinline__ float half_bits_to_float(uint32_t bits16) {
     return __half2float(__ushort_as_half(static_cast<unsigned short>(bits16 & 0xFFFFu)));
 }

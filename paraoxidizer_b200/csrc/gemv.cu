@@ -78,20 +78,62 @@ __device__ __forceinline__ float prep_elem(const PrepOp& op, const PrepRow& r, i
     }
     return v;
 }
+// RMSNorm scale 1 / sqrt(sum x^2 / K + eps) of rows b0 .. b1, computed by the whole block (every
+// thread must call it): each thread sums squares of k = 4 t + 4 nthreads j in order (its loads of
+// four j issued together), then warps in a butterfly and the block in warp order.
+__device__ __forceinline__ void block_rms_inv(const float* x, int ldx, int K, float eps, int b0, int b1,
+                                              float* s_inv) {
+    __shared__ float red[32];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    const int step = 4 * blockDim.x;
+    for (int b = b0; b <= b1; b++) {
+        const float* xr = x + (size_t)b * ldx;
+        float s = 0.f;
+        for (int k0 = 4 * tid; k0 < K; k0 += 4 * step) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                v[u] = k0 + u * step < K ? *reinterpret_cast<const float4*>(xr + k0 + u * step)
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                s = fmaf(v[u].x, v[u].x, s);
+                s = fmaf(v[u].y, v[u].y, s);
+                s = fmaf(v[u].z, v[u].z, s);
+                s = fmaf(v[u].w, v[u].w, s);
+            }
+        }
+        s = warp_sum(s);
+        if (lane == 0) red[warp] = s;
+        __syncthreads();
+        if (tid == 0) {
+            float t = 0.f;
+            for (int w = 0; w < nw; w++) t += red[w];
+            s_inv[b - b0] = 1.0f / sqrtf(t / (float)K + eps);
+        }
+        __syncthreads();
+    }
+}
+
 // One warp per (batch row, 128-k block); lane l covers k = 4l .. 4l+3 of the block.
 __global__ void __launch_bounds__(256) xprep_int_kernel(const float* __restrict__ x, int B, int K, uint8_t* cols,
                                                         float2* meta, int Kp, int nxb, int nxbs, PrepOp op) {
     pdl_launch_dependents();
     pdl_wait();
-    const int wid = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int nwb = blockDim.x >> 5, wid0 = blockIdx.x * nwb;
+    const int wid = wid0 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
+    __shared__ float s_inv[8];  // RMSNorm scales of the rows this block's warps cover (at most 8)
+    const int b0 = wid0 / nxb;
+    if (op.mode == kPrepNorm && wid0 < B * nxb)
+        block_rms_inv(x, op.ld_x, K, op.eps, b0, min(B * nxb - 1, wid0 + nwb - 1) / nxb, s_inv);
     if (wid >= B * nxb) return;
     const int b = wid / nxb, blk = wid % nxb;
     const int k = blk * kXBlock + lane * 4;
     PrepRow r;
     r.x = x + (size_t)b * op.ld_x;
     r.up = op.up ? op.up + (size_t)b * op.ld_up : nullptr;
-    r.inv = op.mode == kPrepNorm ? row_rms_inv(r.x, K, op.eps) : 1.f;
+    r.inv = op.mode == kPrepNorm ? s_inv[b - b0] : 1.f;
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
     if (k < K) {
         v = *reinterpret_cast<const float4*>(r.x + k);  // K % 4 == 0 on this path
@@ -125,14 +167,19 @@ __global__ void __launch_bounds__(256) xprep_f16_kernel(const float* __restrict_
     pdl_launch_dependents();
     pdl_wait();
     const int per = Kp / 64;  // warps per row
-    const int wid = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int nwb = blockDim.x >> 5, wid0 = blockIdx.x * nwb;
+    const int wid = wid0 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
+    __shared__ float s_inv[8];
+    const int b0 = wid0 / per;
+    if (op.mode == kPrepNorm && wid0 < B * per)
+        block_rms_inv(x, op.ld_x, K, op.eps, b0, min(B * per - 1, wid0 + nwb - 1) / per, s_inv);
     if (wid >= B * per) return;
     const int b = wid / per, k = (wid % per) * 64 + 2 * lane;
     PrepRow r;
     r.x = x + (size_t)b * op.ld_x;
     r.up = op.up ? op.up + (size_t)b * op.ld_up : nullptr;
-    r.inv = op.mode == kPrepNorm ? row_rms_inv(r.x, K, op.eps) : 1.f;
+    r.inv = op.mode == kPrepNorm ? s_inv[b - b0] : 1.f;
     float2 v = make_float2(0.f, 0.f);
     if (k < K) {
         v = *reinterpret_cast<const float2*>(r.x + k);  // K % 32 == 0 on this path

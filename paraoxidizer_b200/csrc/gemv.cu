@@ -59,62 +59,6 @@ XPrep xprep_view(void* scratch, int kind, int K) {
 }
 
 
-// Element k of batch row b of the GEMV input, after the fused pre-op: x itself, RMSNorm
-// (crates/paraoxidizer-runtime/src/engine.rs:294-350: x * (1 / sqrt(sum x^2 / n + eps)) then * w),
-// or SwiGLU (engine.rs:671-677: g / (1 + exp(-g)) * u).
-struct PrepRow {
-    const float* x;
-    const float* up;
-    float inv;  // RMSNorm scale of this row
-};
-__device__ __forceinline__ float prep_elem(const PrepOp& op, const PrepRow& r, int k, float v) {
-    if (op.mode == kPrepNorm) {
-        const float t = v * r.inv;
-        return op.norm_w ? t * half_bits_to_float(op.norm_w[k]) : t;
-    }
-    if (op.mode == kPrepSwiGLU) {
-        const float u = r.up[k];
-        return v / (1.0f + expf(-v)) * u;
-    }
-    return v;
-}
-// RMSNorm scale 1 / sqrt(sum x^2 / K + eps) of rows b0 .. b1, computed by the whole block (every
-// thread must call it): each thread sums squares of k = 4 t + 4 nthreads j in order (its loads of
-// four j issued together), then warps in a butterfly and the block in warp order.
-__device__ __forceinline__ void block_rms_inv(const float* x, int ldx, int K, float eps, int b0, int b1,
-                                              float* s_inv) {
-    __shared__ float red[32];
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
-    const int step = 4 * blockDim.x;
-    for (int b = b0; b <= b1; b++) {
-        const float* xr = x + (size_t)b * ldx;
-        float s = 0.f;
-        for (int k0 = 4 * tid; k0 < K; k0 += 4 * step) {
-            float4 v[4];
-#pragma unroll
-            for (int u = 0; u < 4; u++)
-                v[u] = k0 + u * step < K ? *reinterpret_cast<const float4*>(xr + k0 + u * step)
-                                         : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                s = fmaf(v[u].x, v[u].x, s);
-                s = fmaf(v[u].y, v[u].y, s);
-                s = fmaf(v[u].z, v[u].z, s);
-                s = fmaf(v[u].w, v[u].w, s);
-            }
-        }
-        s = warp_sum(s);
-        if (lane == 0) red[warp] = s;
-        __syncthreads();
-        if (tid == 0) {
-            float t = 0.f;
-            for (int w = 0; w < nw; w++) t += red[w];
-            s_inv[b - b0] = 1.0f / sqrtf(t / (float)K + eps);
-        }
-        __syncthreads();
-    }
-}
-
 // One warp per (batch row, 128-k block); lane l covers k = 4l .. 4l+3 of the block.
 __global__ void __launch_bounds__(256) xprep_int_kernel(const float* __restrict__ x, int B, int K, uint8_t* cols,
                                                         float2* meta, int Kp, int nxb, int nxbs, PrepOp op) {

@@ -2,8 +2,11 @@
 // preparation, re-tiling and dequantization kernels (gemv.cu).
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+
+#include "common.cuh"
 
 namespace pox {
 
@@ -67,6 +70,65 @@ struct PrepOp {
     const float* up = nullptr;         // kPrepSwiGLU: up rows (x holds the gate rows)
     int ld_x = 0, ld_up = 0;           // row strides in elements (0: K)
 };
+
+#ifdef __CUDACC__
+// Element k of batch row b of the GEMV input, after the fused pre-op: x itself, RMSNorm
+// (crates/paraoxidizer-runtime/src/engine.rs:294-350: x * (1 / sqrt(sum x^2 / n + eps)) then * w),
+// or SwiGLU (engine.rs:671-677: g / (1 + exp(-g)) * u).
+struct PrepRow {
+    const float* x;
+    const float* up;
+    float inv;  // RMSNorm scale of this row
+};
+__device__ __forceinline__ float prep_elem(const PrepOp& op, const PrepRow& r, int k, float v) {
+    if (op.mode == kPrepNorm) {
+        const float t = v * r.inv;
+        return op.norm_w ? t * half_bits_to_float(op.norm_w[k]) : t;
+    }
+    if (op.mode == kPrepSwiGLU) {
+        const float u = r.up[k];
+        return v / (1.0f + expf(-v)) * u;
+    }
+    return v;
+}
+// RMSNorm scale 1 / sqrt(sum x^2 / K + eps) of rows b0 .. b1, computed by the whole block (every
+// thread must call it): each thread sums squares of k = 4 t + 4 nthreads j in order (its loads of
+// four j issued together), then warps in a butterfly and the block in warp order.
+__device__ __forceinline__ void block_rms_inv(const float* x, int ldx, int K, float eps, int b0, int b1,
+                                              float* s_inv) {
+    __shared__ float red[32];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    const int step = 4 * blockDim.x;
+    for (int b = b0; b <= b1; b++) {
+        const float* xr = x + (size_t)b * ldx;
+        float s = 0.f;
+        for (int k0 = 4 * tid; k0 < K; k0 += 4 * step) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                v[u] = k0 + u * step < K ? *reinterpret_cast<const float4*>(xr + k0 + u * step)
+                                         : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                s = fmaf(v[u].x, v[u].x, s);
+                s = fmaf(v[u].y, v[u].y, s);
+                s = fmaf(v[u].z, v[u].z, s);
+                s = fmaf(v[u].w, v[u].w, s);
+            }
+        }
+        s = warp_sum(s);
+        if (lane == 0) red[warp] = s;
+        __syncthreads();
+        if (tid == 0) {
+            float t = 0.f;
+            for (int w = 0; w < nw; w++) t += red[w];
+            s_inv[b - b0] = 1.0f / sqrtf(t / (float)K + eps);
+        }
+        __syncthreads();
+    }
+}
+
+#endif
 
 struct GemvArgs {
     const uint8_t* w;        // tile blobs (TileLayout)
@@ -137,5 +199,25 @@ int tc05_splits(int nrb, int nkb, int sms);
 cudaError_t launch_tc05(int kind, const TcArgs& a, cudaStream_t st);
 cudaError_t launch_xprep_tc05(const float* x, int B, int Bp, int K, const PrepOp& op, uint8_t* xs, float* xscale,
                               cudaStream_t st);
+
+// ---- small-M path on the integer tensor cores (tcgen05 kind::i8): INT4 without outliers and
+// INT8, padded batch 16 .. 64 (gemm_tcq.cu) ----
+struct TqArgs {
+    const uint8_t* w;     // tile blobs (TileLayout of the kind; K % 128 == 0)
+    const uint8_t* xl;    // x limbs [K / 128][2 Bp][128 B], 128-byte swizzled (row 2b: hi, 2b + 1: lo)
+    const float2* xm;     // [K / 128][Bp]: (max|x| / 16383, sum x) of each 128-k block of each x row
+    float wscale;         // INT8 per-tensor scale (1 otherwise)
+    float* y;             // [B][Nout]
+    const float* resid;   // nullptr, or [B][Nout] added (may alias y)
+    float* ws;            // k-split partials [S][Bp][Nout]
+    int* tickets;         // [row blocks] zero-initialised, self-resetting
+    int* err;
+    int Nout, K, nkb, nT, B, Bp, S;  // nkb: 128-k blocks
+};
+bool tq_supported(int kind, bool outliers, int Bp);
+size_t tq_x_bytes(int K, int Bp);  // limbs, then (256-byte aligned) the block meta
+cudaError_t launch_xprep_tq(const float* x, int B, int Bp, int K, const PrepOp& op, uint8_t* xl, float2* xm,
+                            cudaStream_t st);
+cudaError_t launch_tq(int kind, const TqArgs& a, cudaStream_t st);
 
 }  // namespace pox

@@ -475,9 +475,13 @@ extern "C" int pox_cuda_tensor_info(const pox_tensor* t, size_t* rows, size_t* c
 // ------------------------------------------------------------------------------------------
 // GEMV
 // ------------------------------------------------------------------------------------------
+// Small-M scratch: prepared x (the f16 layout or the integer path's limbs and block meta, whichever
+// is larger), 256 row scales, then the k-split partials.
+static size_t tc_x_region(size_t cols, int Bp) {
+    return (std::max(pox::tc05_x_bytes((int)cols, Bp), pox::tq_x_bytes((int)cols, Bp)) + 255) & ~(size_t)255;
+}
 static size_t tc_bytes(size_t rows, size_t cols, int Bp, int S) {
-    const size_t xs = (pox::tc05_x_bytes((int)cols, Bp) + 255) & ~(size_t)255;
-    return xs + 256 * sizeof(float) + (S > 1 ? (size_t)S * Bp * rows * sizeof(float) : 0);
+    return tc_x_region(cols, Bp) + 256 * sizeof(float) + (S > 1 ? (size_t)S * Bp * rows * sizeof(float) : 0);
 }
 
 int pox::ensure_tc_scratch(pox_cuda_ctx* ctx, size_t rows, size_t cols, size_t batch, cudaStream_t st) {
@@ -526,12 +530,41 @@ static int tc05_gemv(pox_cuda_ctx* ctx, const pox_tensor* t, int kind, const flo
         const int b = (int)std::min<size_t>(batch - done, 128);
         const int Bp = tc05_pad(b);
         uint8_t* xs = static_cast<uint8_t*>(ctx->tc_scratch);
-        const size_t xsb = (tc05_x_bytes(K, Bp) + 255) & ~(size_t)255;
+        const size_t xsb = tc_x_region(K, Bp);
         float* xscale = reinterpret_cast<float*>(xs + xsb);
         float* ws = xscale + 256;
         PrepOp opb = op;
         if (opb.up) opb.up += done * (size_t)opb.ld_up;
         cudaError_t e = cudaSuccess;
+        if (tq_supported(kind, t->nnz > 0, Bp)) {
+            // integer tensor cores: x as exact int8 limbs of 128-k blocks (the caller's prepared
+            // f16 x does not apply: gemv_x_target declines these tensors)
+            if (prepared) return set_error(POX_ERR_INVALID, "prepared x: the integer small-M path prepares its own");
+            float2* xm = reinterpret_cast<float2*>(xs + (((size_t)(K / 128) * 2 * Bp * 128 + 255) & ~(size_t)255));
+            e = launch_xprep_tq(x + done * ldx, b, Bp, K, opb, xs, xm, st);
+            if (e != cudaSuccess) return cuda_error(e, "x preparation launch");
+            TqArgs q = {};
+            q.w = (const uint8_t*)t->w;
+            q.xl = xs;
+            q.xm = xm;
+            q.wscale = kind == kKindI8 ? t->i8_scale : 1.0f;
+            q.y = y + done * t->rows;
+            q.resid = resid ? resid + done * t->rows : nullptr;
+            q.ws = ws;
+            q.tickets = ctx->tc_tickets;
+            q.err = ctx->err_dev;
+            q.Nout = N;
+            q.K = K;
+            q.nkb = K / 128;
+            q.nT = (N + 15) / 16;
+            q.B = b;
+            q.Bp = Bp;
+            q.S = S;
+            e = launch_tq(kind, q, st);
+            if (e != cudaSuccess) return cuda_error(e, "small-M GEMM launch");
+            done += b;
+            continue;
+        }
         if (!prepared) {
             e = launch_xprep_tc05(x + done * ldx, b, Bp, K, opb, xs, xscale, st);
             if (e != cudaSuccess) return cuda_error(e, "x preparation launch");
@@ -582,11 +615,13 @@ int pox::gemv_x_target(pox_cuda_ctx* ctx, const pox_tensor* t, size_t batch, cud
     if (!t->tiled || t->dtype != POX_I4 || t->cols % 128 != 0) return set_error(POX_ERR_UNSUPPORTED, "no prepared-x path");
     if (gemv_uses_small_m(t, batch)) {
         if (batch > 128) return set_error(POX_ERR_UNSUPPORTED, "prepared x holds up to 128 rows");
+        if (tq_supported(kKindI4, t->nnz > 0, tc05_pad((int)batch)))  // the integer path prepares x itself
+            return set_error(POX_ERR_UNSUPPORTED, "no prepared-x path on the integer small-M path");
         int rc = ensure_tc_scratch(ctx, t->rows, t->cols, batch, st);
         if (rc) return rc;
         out->Bp = tc05_pad((int)batch);
         out->xs = static_cast<uint8_t*>(ctx->tc_scratch);
-        out->xscale = reinterpret_cast<float*>(out->xs + ((tc05_x_bytes((int)t->cols, out->Bp) + 255) & ~(size_t)255));
+        out->xscale = reinterpret_cast<float*>(out->xs + tc_x_region(t->cols, out->Bp));  // as tc05_gemv places them
         return POX_OK;
     }
     if (batch > (size_t)kMaxBatch) return set_error(POX_ERR_UNSUPPORTED, "prepared x holds up to 8 rows");

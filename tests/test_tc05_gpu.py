@@ -71,13 +71,14 @@ class Op(L.GemvOp):
     pass
 
 
+@pytest.mark.parametrize("kind", ["i4_outliers", "i4"])  # f16 tiles / integer tensor cores
 @pytest.mark.parametrize("batch", [12, 40])
-def test_small_m_rmsnorm_residual(be, batch):
+def test_small_m_rmsnorm_residual(be, batch, kind):
     import torch
 
     rng = np.random.default_rng(5 + batch)
     rows, cols = 1536, 2048
-    t, gemv = make(be, "i4_outliers", rows, cols, 9)
+    t, gemv = make(be, kind, rows, cols, 9)
     x = rng.standard_normal(batch * cols, dtype=np.float32) * np.float32(3.0)
     nw = (1.0 + 0.2 * rng.standard_normal(cols, dtype=np.float32)).astype(np.float16).view(np.uint16)
     resid = rng.standard_normal(batch * rows, dtype=np.float32)

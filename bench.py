@@ -224,8 +224,8 @@ def run_reference(args):
 
 def batched_gemv_bench(be, batches=(1, 4, 16, 64), reps=400):
     """The batched configurations: INT8 14336x4096 (per-tensor scale, the parity path) and INT4 g128
-    4096x14336 with 3.5-sigma outliers, at B rows of x (B <= 8: the GEMV kernel; B >= 9: the
-    tcgen05 small-M kernel). Copies rotated past L2, CUDA graph of `reps` launches, CUDA events.
+    4096x14336 without and with 3.5-sigma outliers, at B rows of x (B <= 8: the mma.sync GEMV
+    kernel; B >= 9: a tcgen05 small-M kernel; each line names the kernel the library chose). Copies rotated past L2, CUDA graph of `reps` launches, CUDA events.
     Algorithmic bytes: weights + scales (+ outlier table) + x as f16 (2 K B) + y as f32 (4 N B)."""
     import torch
 
@@ -242,6 +242,9 @@ def batched_gemv_bench(be, batches=(1, 4, 16, 64), reps=400):
                   14336 * 4096 + 4))
     del w8, q8
     packed, scales, tab, ob, _ = make_workload(seed=3)
+    cases.append(("int4_g128_4096x14336", ROWS, COLS,  # the decode weights' format: no outlier table
+                  [be.upload_int4(packed, scales, ROWS, COLS, GS) for _ in range(8)],
+                  ROWS * COLS // 2 + ROWS * (COLS // GS) * 4))
     cases.append(("int4_g128_4096x14336_outliers", ROWS, COLS,
                   [be.upload_int4(packed, scales, ROWS, COLS, GS, ob) for _ in range(8)],
                   ROWS * COLS // 2 + ROWS * (COLS // GS) * 4 + 4 + 6 * len(tab[0])))
@@ -273,7 +276,7 @@ def batched_gemv_bench(be, batches=(1, 4, 16, 64), reps=400):
             res[str(B)] = {"us": round(sec * 1e6, 2), "gbs": round(nbytes / sec / 1e9, 1),
                            "frac_of_hbm_peak": round(nbytes / sec / 1e9 / peak, 4),
                            "tflops": round(2.0 * N * K * B / sec / 1e12, 2),
-                           "kernel": "gemv_tc_kernel (mma.sync)" if B <= 8 else "gemm_tc05_kernel (tcgen05)"}
+                           "kernel": ts[0].gemv_kernel(B)}
             del g
         out[name] = res
         for t in ts:

@@ -129,6 +129,12 @@ int pox_cuda_tensor_free(pox_cuda_ctx* ctx, pox_tensor* t);
 /* Shape and footprint of a resident tensor; any out pointer may be NULL. */
 int pox_cuda_tensor_info(const pox_tensor* t, size_t* rows, size_t* cols, size_t* outlier_count,
                          size_t* device_bytes);
+/* Name of the kernel a GEMV of this tensor at `batch` rows of x runs (per launch of up to 8 rows
+ * for the batch <= 8 kernel): "gemv_tc_kernel" (mma.sync, batch <= 8), "gemm_tq_kernel"
+ * (tcgen05 kind::i8), "gemm_tc05_kernel" (tcgen05 kind::f16) or "gemv_generic" (raw .pox layout).
+ * NULL if t is NULL. No counterpart in the reference (it has one CPU loop per dtype); it lets a
+ * caller or a benchmark report which path served a call. */
+const char* pox_cuda_tensor_gemv_kernel(const pox_tensor* t, size_t batch);
 
 /* y[b][r] = sum_c W[r][c] * x[b][c] for b < batch, on device pointers, asynchronously on
  * `stream` (a cudaStream_t; NULL = the context's stream). x: [batch][cols] f32, y:

@@ -91,6 +91,7 @@ def _declare(L):
         "pox_cuda_tensor_upload": (i32, [vp, C.POINTER(TensorDesc), C.POINTER(vp)]),
         "pox_cuda_tensor_free": (i32, [vp, vp]),
         "pox_cuda_tensor_info": (i32, [vp, C.POINTER(sz), C.POINTER(sz), C.POINTER(sz), C.POINTER(sz)]),
+        "pox_cuda_tensor_gemv_kernel": (C.c_char_p, [vp, sz]),
         "pox_cuda_tensor_gemv": (i32, [vp, vp, vp, sz, vp, vp]),
         "pox_cuda_tensor_gemv_host": (i32, [vp, vp, vp, sz, vp]),
         "pox_cuda_tensor_gemv_noalloc": (i32, [vp, vp, vp, sz, vp, vp]),

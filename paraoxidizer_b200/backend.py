@@ -67,6 +67,10 @@ class ResidentTensor:
         """Asynchronous GEMV on device pointers (x [batch][cols], y [batch][rows], f32)."""
         L.check(L.lib().pox_cuda_tensor_gemv(self.backend.ctx, self.handle, x_ptr, batch, y_ptr, stream or None))
 
+    def gemv_kernel(self, batch: int) -> str:
+        """Name of the kernel that serves a GEMV of this tensor at `batch` rows of x."""
+        return L.lib().pox_cuda_tensor_gemv_kernel(self.handle, batch).decode()
+
     def dequant_host(self) -> np.ndarray:
         out = np.zeros(self.rows * self.cols, np.float32)
         L.check(L.lib().pox_cuda_tensor_dequant_host(self.backend.ctx, self.handle, _ptr(out)))

@@ -472,6 +472,15 @@ extern "C" int pox_cuda_tensor_info(const pox_tensor* t, size_t* rows, size_t* c
     return POX_OK;
 }
 
+extern "C" const char* pox_cuda_tensor_gemv_kernel(const pox_tensor* t, size_t batch) {
+    if (!t) return nullptr;
+    if (!t->tiled) return "gemv_generic";
+    if (batch == 0 || !gemv_uses_small_m(t, batch)) return "gemv_tc_kernel";
+    const int kind = t->dtype == POX_I4 ? kKindI4 : (t->dtype == POX_I8 ? kKindI8 : kKindF16);
+    return tq_supported(kind, t->nnz > 0, tc05_pad((int)std::min<size_t>(batch, 128))) ? "gemm_tq_kernel"
+                                                                                       : "gemm_tc05_kernel";
+}
+
 // ------------------------------------------------------------------------------------------
 // GEMV
 // ------------------------------------------------------------------------------------------

@@ -135,3 +135,19 @@ def test_small_m_agrees_with_gemv_path(be):
     for b in range(9):
         assert rel(y9[b], ref[b]) <= TOL
     t.free()
+
+
+def test_kernel_choice_by_batch(be):
+    """Which kernel serves a call: mma.sync GEMV up to batch 8, the integer tensor-core path for
+    INT8 (padded batch <= 64) and INT4 without outliers (padded batch 16), the f16 tiles otherwise."""
+    t4, _ = make(be, "i4", 256, 1024, 1)
+    t4o, _ = make(be, "i4_outliers", 256, 2048, 2)
+    t8, _ = make(be, "i8", 256, 1024, 3)
+    assert t4.gemv_kernel(8) == "gemv_tc_kernel"
+    assert t4.gemv_kernel(16) == "gemm_tq_kernel"
+    assert t4.gemv_kernel(33) == "gemm_tc05_kernel"
+    assert t4o.gemv_kernel(16) == "gemm_tc05_kernel"
+    assert t8.gemv_kernel(64) == "gemm_tq_kernel"
+    assert t8.gemv_kernel(65) == "gemm_tc05_kernel"
+    for t in (t4, t4o, t8):
+        t.free()

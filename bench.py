@@ -376,6 +376,8 @@ def decode_bench(be, cfg=LLAMA_8B, batches=(1, 8, 32), prefill=512, steps=256, w
 
 
 def decode_batches(args):
+    if args.decode_batches in ("", "none"):
+        return ()
     return tuple(int(b) for b in args.decode_batches.split(","))
 
 
@@ -387,9 +389,13 @@ def run_decode_only(args):
     from paraoxidizer_b200.backend import CudaBackend
 
     be = CudaBackend.create(local)
-    bg = batched_gemv_bench(be) if world == 1 and args.with_batched else None
-    d = decode_bench(be, batches=decode_batches(args), prefill=args.decode_prefill, steps=args.decode_steps,
-                     world=world, rank=rank)
+    bg = None
+    if world == 1 and args.with_batched:
+        bg = batched_gemv_bench(be, batches=tuple(int(b) for b in args.batched_sizes.split(",")))
+    d = None
+    if decode_batches(args):
+        d = decode_bench(be, batches=decode_batches(args), prefill=args.decode_prefill, steps=args.decode_steps,
+                         world=world, rank=rank)
     if rank == 0:
         print(json.dumps({"batched_gemv": bg, "decode": d}), flush=True)
     be.close()
@@ -555,7 +561,8 @@ def main():
     ap.add_argument("--decode-only", action="store_true",
                     help="run only the decode benchmark (one JSON object; for launch lists and captures)")
     ap.add_argument("--with-batched", action="store_true", help="--decode-only: also run the batched GEMV bench")
-    ap.add_argument("--decode-batches", default="1,8,32")
+    ap.add_argument("--batched-sizes", default="1,4,16,64", help="--with-batched: rows of x per call")
+    ap.add_argument("--decode-batches", default="1,8,32", help="comma list, or 'none'")
     ap.add_argument("--decode-prefill", type=int, default=512)
     ap.add_argument("--decode-steps", type=int, default=256)
     args = ap.parse_args()

@@ -378,7 +378,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc05_kernel(TcArgs a) {
         if (s_last) {
             __threadfence();
             const int r0 = rb * 128, nrow = min(128, a.Nout - r0);
-            const bool vec = (a.Nout & 3) == 0;
+            const bool vec = (a.Nout & 3) == 0 && ((uintptr_t)a.y & 15) == 0 && ((uintptr_t)a.resid & 15) == 0;
             const int per_b = vec ? (nrow + 3) / 4 : nrow;  // items per batch row
             const int items = a.B * per_b;
             for (int it = tid; it < items; it += kTcThreads) {

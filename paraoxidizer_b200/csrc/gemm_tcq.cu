@@ -360,14 +360,49 @@ __global__ void __launch_bounds__(tq_threads(NP), 1) gemm_tq_kernel(TqArgs a) {
         __syncthreads();
         if (s_last) {
             __threadfence();
+            // all splits' loads of an item are issued before the sum (one L2 round trip per item),
+            // four rows per item when y, resid and the rows are 16-byte aligned
             const int r0 = rb * 128, nrow = min(128, a.Nout - r0);
-            for (int it = tid; it < a.B * nrow; it += blockDim.x) {
-                const int b = it / nrow, rr2 = it % nrow;
-                const size_t o = (size_t)b * a.Nout + r0 + rr2;
-                float acc = 0.f;
-                for (int sp = 0; sp < a.S; sp++) acc += __ldcg(a.ws + (size_t)sp * a.Bp * a.Nout + o);
-                if (a.resid) acc += a.resid[o];
-                a.y[o] = acc;
+            const bool vec = (a.Nout & 3) == 0 && ((uintptr_t)a.y & 15) == 0 && ((uintptr_t)a.resid & 15) == 0;
+            const int per_b = vec ? (nrow + 3) / 4 : nrow;
+            for (int it = tid; it < a.B * per_b; it += blockDim.x) {
+                const int b = it / per_b, qq = it % per_b;
+                if (vec) {
+                    const size_t o = (size_t)b * a.Nout + r0 + 4 * qq;
+                    float4 part[16];
+#pragma unroll
+                    for (int sp = 0; sp < 16; sp++)
+                        if (sp < a.S) part[sp] = __ldcg(reinterpret_cast<const float4*>(a.ws + (size_t)sp * a.Bp * a.Nout + o));
+                    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                    for (int sp = 0; sp < 16; sp++)
+                        if (sp < a.S) {
+                            acc.x += part[sp].x;
+                            acc.y += part[sp].y;
+                            acc.z += part[sp].z;
+                            acc.w += part[sp].w;
+                        }
+                    if (a.resid) {
+                        const float4 rv = *reinterpret_cast<const float4*>(a.resid + o);
+                        acc.x += rv.x;
+                        acc.y += rv.y;
+                        acc.z += rv.z;
+                        acc.w += rv.w;
+                    }
+                    *reinterpret_cast<float4*>(a.y + o) = acc;
+                } else {
+                    const size_t o = (size_t)b * a.Nout + r0 + qq;
+                    float part[16];
+#pragma unroll
+                    for (int sp = 0; sp < 16; sp++)
+                        if (sp < a.S) part[sp] = __ldcg(a.ws + (size_t)sp * a.Bp * a.Nout + o);
+                    float acc = 0.f;
+#pragma unroll
+                    for (int sp = 0; sp < 16; sp++)
+                        if (sp < a.S) acc += part[sp];
+                    if (a.resid) acc += a.resid[o];
+                    a.y[o] = acc;
+                }
             }
         }
     }

@@ -48,7 +48,8 @@ def make(be, kind, rows, cols, seed):
 
 
 @pytest.mark.parametrize("kind,rows,cols", [("i4", 768, 1024), ("i4_outliers", 640, 2048), ("i8", 1000, 1024),
-                                            ("f16", 512, 1024), ("i4", 4096, 4096), ("i4", 200, 14336)])
+                                            ("f16", 512, 1024), ("i4", 4096, 4096), ("i4", 200, 14336),
+                                            ("i8", 3000, 4096)])
 @pytest.mark.parametrize("batch", [9, 16, 33, 64, 128, 200])
 def test_small_m_matches_oracle(be, kind, rows, cols, batch):
     if rows * cols > 4096 * 4096 // 2 and batch not in (16, 64):

@@ -21,6 +21,7 @@ from paraoxidizer_b200.synth import make_llama, oracle_weights
 
 CFG = {"hidden": 256, "inter": 512, "layers": 2, "n_heads": 8, "n_kv_heads": 2, "vocab": 1000,
        "rms_eps": 1e-5, "rope_theta": 500000.0}
+CFGS = {2: CFG, 4: dict(CFG, hidden=512, n_kv_heads=4)}  # 4 ranks: one kv head and 128 columns of o/down each
 
 
 def _dequant(t):
@@ -108,20 +109,21 @@ def _tp_forward(w, cfg, tp, rank, tok, pos, kc, vc):
 
 
 def _rank_main(rank, world, port, outdir):
+    cfg = CFGS[world]
     import torch.distributed as dist
 
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
     try:
-        w = make_llama(CFG, seed=4, outlier_policy="automatic", norm_jitter=0.1)
-        shard = TP.shard_llama(oracle_weights(w), CFG, world, rank)
-        hd = CFG["hidden"] // CFG["n_heads"]
+        w = make_llama(cfg, seed=4, outlier_policy="automatic", norm_jitter=0.1)
+        shard = TP.shard_llama(oracle_weights(w), cfg, world, rank)
+        hd = cfg["hidden"] // cfg["n_heads"]
         steps = 5
-        kc = np.zeros((CFG["layers"], steps, CFG["n_kv_heads"] // world, hd), np.float32)
+        kc = np.zeros((cfg["layers"], steps, cfg["n_kv_heads"] // world, hd), np.float32)
         vc = np.zeros_like(kc)
         tok = 17
         out_logits, out_next = [], []
         for pos in range(steps):
-            logits, nxt = _tp_forward(shard, CFG, world, rank, tok, pos, kc, vc)
+            logits, nxt = _tp_forward(shard, cfg, world, rank, tok, pos, kc, vc)
             out_logits.append(logits)
             out_next.append(nxt)
             tok = nxt
@@ -136,17 +138,19 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def test_tp2_gloo_matches_oracle(tmp_path):
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_gloo_matches_oracle(tmp_path, world):
     import torch.multiprocessing as mp
 
-    world = 2
+    cfg = CFGS[world]
     mp.start_processes(_rank_main, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True,
                        start_method="spawn")
     res = [np.load(tmp_path / f"rank{r}.npz") for r in range(world)]
-    assert np.array_equal(res[0]["next"], res[1]["next"])  # every rank picks the same tokens
-    w = make_llama(CFG, seed=4, outlier_policy="automatic", norm_jitter=0.1)
-    ref = O.OracleModel(CFG, oracle_weights(w), max_seq=8)
-    Vl = CFG["vocab"] // world
+    for r in range(1, world):
+        assert np.array_equal(res[0]["next"], res[r]["next"])  # every rank picks the same tokens
+    w = make_llama(cfg, seed=4, outlier_policy="automatic", norm_jitter=0.1)
+    ref = O.OracleModel(cfg, oracle_weights(w), max_seq=8)
+    Vl = cfg["vocab"] // world
     tok = 17
     for pos in range(len(res[0]["next"])):
         full = ref.forward_token(tok, pos)

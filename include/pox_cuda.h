@@ -279,6 +279,14 @@ int pox_cuda_model_comm_peer(pox_model* m, const uint8_t* handles);
  * rank must select the same mode. */
 int pox_cuda_model_comm_mode(pox_model* m, int mode);
 
+/* Failure-detection check of the peer exchange on this context's GPU: runs one allreduce of a
+ * two-rank group whose second rank never arrives (its arrival flags are a local buffer that
+ * nothing writes). Returns POX_OK when the arrival wait ran out within its limit, was reported
+ * as a kernel error (POX_ERR_TIMEOUT internally, then cleared) and set the sticky abort word;
+ * *wait_seconds (may be NULL) = the kernel's duration. The context stays usable. No counterpart
+ * in the reference (one process, no exchanges). */
+int pox_cuda_comm_check_missing_rank(pox_cuda_ctx* ctx, double* wait_seconds);
+
 #ifdef __cplusplus
 }
 #endif

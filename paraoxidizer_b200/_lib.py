@@ -103,6 +103,7 @@ def _declare(L):
         "pox_cuda_model_comm_ipc_handle": (i32, [vp, vp]),
         "pox_cuda_model_comm_peer": (i32, [vp, vp]),
         "pox_cuda_model_comm_mode": (i32, [vp, i32]),
+        "pox_cuda_comm_check_missing_rank": (i32, [vp, C.POINTER(C.c_double)]),
         "pox_cuda_model_destroy": (None, [vp]),
         "pox_cuda_model_set_layer_tensors": (i32, [vp, u32, vp, vp, vp, vp, vp, vp]),
         "pox_cuda_quantize_int4": (i32, [vp, vp, sz, sz, vp, vp, vp]),

@@ -109,6 +109,13 @@ class CudaBackend:
         L.check(L.lib().pox_cuda_create(device, C.byref(ctx)))
         return CudaBackend(ctx.value, device)
 
+    def check_missing_rank(self) -> float:
+        """Failure-detection check of the peer exchange on this GPU (a two-rank exchange whose
+        second rank never arrives must end with the bounded wait's error); returns the wait in s."""
+        t = C.c_double(0.0)
+        L.check(L.lib().pox_cuda_comm_check_missing_rank(self.ctx, C.byref(t)))
+        return t.value
+
     def close(self) -> None:
         if self.ctx:
             for ref in self._children:  # pox_cuda_destroy frees the models still on the context

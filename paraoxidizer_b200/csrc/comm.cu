@@ -261,3 +261,55 @@ int comm_pick(TpComm& c, int call, int cps, int B, uint32_t* next, cudaStream_t 
 }
 
 }  // namespace pox
+
+extern "C" int pox_cuda_comm_check_missing_rank(pox_cuda_ctx* ctx, double* wait_seconds) {
+    using namespace pox;
+    if (!ctx) return set_error(POX_ERR_INVALID, "ctx is NULL");
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    if (cudaSetDevice(ctx->device) != cudaSuccess) return set_error(POX_ERR_CUDA, "cudaSetDevice");
+    if (cudaStreamSynchronize(ctx->stream) != cudaSuccess) return set_error(POX_ERR_CUDA, "cudaStreamSynchronize");
+    int rc = take_kernel_error(ctx);  // an earlier call's error is reported first
+    if (rc) return rc;
+    TpComm c;
+    rc = comm_alloc(c, 0, 2, 1, 128, ctx->err_dev);
+    char* absent = nullptr;  // exchange buffer of the rank that never arrives: same layout, never written
+    float* out = nullptr;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    const size_t bytes = 256 + 2 * c.slot_bytes + c.pair_bytes;
+    cudaError_t e = rc ? cudaErrorUnknown : cudaMalloc(&absent, bytes);
+    if (e == cudaSuccess) e = cudaMemset(absent, 0, bytes);
+    if (e == cudaSuccess) e = cudaMalloc(&out, 128 * sizeof(float));
+    if (e == cudaSuccess) e = cudaEventCreate(&e0);
+    if (e == cudaSuccess) e = cudaEventCreate(&e1);
+    int abort_word = 0;
+    float ms = 0.f;
+    if (e == cudaSuccess) {
+        char* base[2] = {c.buf, absent};
+        for (int p = 0; p < 2; p++) {
+            c.view.flags[p] = reinterpret_cast<unsigned long long*>(base[p]);
+            for (int s = 0; s < 3; s++) c.view.slot[p][s] = reinterpret_cast<float*>(base[p] + 256 + s * c.slot_bytes);
+        }
+        cudaEventRecord(e0, ctx->stream);
+        peer_allreduce_kernel<<<1, 256, 0, ctx->stream>>>(c.view, 0, 3, 0, 32, out);
+        e = cudaGetLastError();
+        cudaEventRecord(e1, ctx->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+        if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, e0, e1);
+        if (e == cudaSuccess) e = cudaMemcpy(&abort_word, c.buf + 128, sizeof(int), cudaMemcpyDeviceToHost);
+    }
+    const int flag = *(volatile int*)ctx->err_host;
+    *(volatile int*)ctx->err_host = 0;
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    cudaFree(out);
+    cudaFree(absent);
+    comm_free(c);
+    if (rc) return rc;
+    if (e != cudaSuccess) return cuda_error(e, "missing-rank check");
+    if (wait_seconds) *wait_seconds = ms * 1e-3;
+    if (!(flag & kErrWaitPeer) || abort_word != 1)
+        return set_error(POX_ERR_CUDA, "the exchange did not report the missing rank (flag 0x%x, abort %d)", flag,
+                         abort_word);
+    return POX_OK;
+}
+

@@ -224,8 +224,8 @@ def run_reference(args):
 
 def batched_gemv_bench(be, batches=(1, 4, 16, 64), reps=400):
     """The batched configurations: INT8 14336x4096 (per-tensor scale, the parity path) and INT4 g128
-    4096x14336 without and with 3.5-sigma outliers, at B rows of x (B <= 8: the mma.sync GEMV
-    kernel; B >= 9: a tcgen05 small-M kernel; each line names the kernel the library chose). Copies rotated past L2, CUDA graph of `reps` launches, CUDA events.
+    4096x14336 without and with 3.5-sigma outliers, at B rows of x (each line names the kernel the
+    library chose: the mma.sync GEMV at small B, a tcgen05 small-M kernel above). Copies rotated past L2, CUDA graph of `reps` launches, CUDA events.
     Algorithmic bytes: weights + scales (+ outlier table) + x as f16 (2 K B) + y as f32 (4 N B)."""
     import torch
 

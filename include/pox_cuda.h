@@ -131,7 +131,9 @@ int pox_cuda_tensor_info(const pox_tensor* t, size_t* rows, size_t* cols, size_t
                          size_t* device_bytes);
 /* Name of the kernel a GEMV of this tensor at `batch` rows of x runs (per launch of up to 8 rows
  * for the batch <= 8 kernel): "gemv_tc_kernel" (mma.sync, batch <= 8), "gemm_tq_kernel"
- * (tcgen05 kind::i8), "gemm_tc05_kernel" (tcgen05 kind::f16) or "gemv_generic" (raw .pox layout).
+ * (tcgen05 kind::i8; also below batch 9 where it was measured faster: INT4 without outliers with
+ * cols >= 8192 from batch 6, INT8 with >= 16 M weights from batch 2), "gemm_tc05_kernel"
+ * (tcgen05 kind::f16) or "gemv_generic" (raw .pox layout).
  * NULL if t is NULL. No counterpart in the reference (it has one CPU loop per dtype); it lets a
  * caller or a benchmark report which path served a call. */
 const char* pox_cuda_tensor_gemv_kernel(const pox_tensor* t, size_t batch);

@@ -614,9 +614,25 @@ static int tc05_min_batch() {
     return v;
 }
 
+// Batches <= 8 that the integer small-M kernel (padded to 16 rows) serves faster than the batch
+// <= 8 GEMV, measured on B200 (us per call, GEMV vs integer kernel):
+//  * INT4 without outliers, K >= 8192, batch >= 6: the GEMV stages 2 K bytes of x per row in shared
+//    memory and loses occupancy (4096 x 14336: 27.2 vs 20.8 at batch 6, 26.8 vs 20.9 at 8). With
+//    K = 4096 the GEMV keeps up or wins (6144 x 4096 at batch 6: 8.4 vs 13.1).
+//  * INT8 with at least 16 M weights, batch >= 2 (14336 x 4096: 20.0 vs 17.9 at batch 2, 30.0 vs
+//    18.0 at 8).
+static bool tq_below_9(const pox_tensor* t, int kind, size_t batch) {
+    if (!tq_supported(kind, t->nnz > 0, 16)) return false;
+    if (kind == kKindI4) return batch >= 6 && t->cols >= 8192;
+    return batch >= 2 && t->rows * t->cols >= ((size_t)16 << 20);
+}
+
 bool pox::gemv_uses_small_m(const pox_tensor* t, size_t batch) {
     // the x preparation stages one row (cols floats) in shared memory
-    return t->tiled && t->cols % 128 == 0 && t->cols <= 53248 && batch >= (size_t)tc05_min_batch();
+    if (!(t->tiled && t->cols % 128 == 0 && t->cols <= 53248)) return false;
+    if (batch >= (size_t)tc05_min_batch()) return true;
+    const int kind = t->dtype == POX_I4 ? kKindI4 : (t->dtype == POX_I8 ? kKindI8 : kKindF16);
+    return kind != kKindF16 && tq_below_9(t, kind, batch);
 }
 
 int pox::gemv_x_target(pox_cuda_ctx* ctx, const pox_tensor* t, size_t batch, cudaStream_t st, XTarget* out) {

@@ -140,15 +140,36 @@ def test_small_m_agrees_with_gemv_path(be):
 
 def test_kernel_choice_by_batch(be):
     """Which kernel serves a call: mma.sync GEMV up to batch 8, the integer tensor-core path for
-    INT8 (padded batch <= 64) and INT4 without outliers (padded batch 16), the f16 tiles otherwise."""
+    INT8 (padded batch <= 64) and INT4 without outliers (padded batch 16), the f16 tiles otherwise;
+    below batch 9 the integer path takes over where it was measured faster (INT4 with K >= 8192 from
+    batch 6, INT8 with >= 16 M weights from batch 2)."""
     t4, _ = make(be, "i4", 256, 1024, 1)
     t4o, _ = make(be, "i4_outliers", 256, 2048, 2)
     t8, _ = make(be, "i8", 256, 1024, 3)
+    t4k, _ = make(be, "i4", 128, 8192, 4)
+    t8big, _ = make(be, "i8", 4096, 4096, 5)
     assert t4.gemv_kernel(8) == "gemv_tc_kernel"
     assert t4.gemv_kernel(16) == "gemm_tq_kernel"
     assert t4.gemv_kernel(33) == "gemm_tc05_kernel"
     assert t4o.gemv_kernel(16) == "gemm_tc05_kernel"
+    assert t8.gemv_kernel(4) == "gemv_tc_kernel"
     assert t8.gemv_kernel(64) == "gemm_tq_kernel"
     assert t8.gemv_kernel(65) == "gemm_tc05_kernel"
-    for t in (t4, t4o, t8):
+    assert [t4k.gemv_kernel(b) for b in (5, 6, 8)] == ["gemv_tc_kernel", "gemm_tq_kernel", "gemm_tq_kernel"]
+    assert [t8big.gemv_kernel(b) for b in (1, 2)] == ["gemv_tc_kernel", "gemm_tq_kernel"]
+    for t in (t4, t4o, t8, t4k, t8big):
         t.free()
+
+
+@pytest.mark.parametrize("kind,rows,cols,batch", [("i4", 1000, 8192, 6), ("i4", 300, 14336, 8), ("i8", 4096, 4096, 2),
+                                                  ("i8", 4100, 4096, 5)])
+def test_integer_path_below_batch_9_matches_oracle(be, kind, rows, cols, batch):
+    """Batches <= 8 routed to the integer tensor-core kernel keep the GEMV tolerance."""
+    t, gemv = make(be, kind, rows, cols, 40 + batch)
+    assert t.gemv_kernel(batch) == "gemm_tq_kernel"
+    rng = np.random.default_rng(batch)
+    x = (rng.standard_normal(batch * cols, dtype=np.float32) * np.float32(1.5)).reshape(batch, cols)
+    y = t.gemv_host(x, batch).reshape(batch, rows)
+    for b in range(batch):
+        assert rel(y[b], gemv(x[b])) <= TOL, (kind, rows, cols, batch, b)
+    t.free()

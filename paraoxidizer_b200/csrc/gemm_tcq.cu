@@ -1,6 +1,6 @@
 // gemm_tcq.cu -- the small-M projection on the integer tensor cores: x [B][K] times W^T for
-// B = 9 .. 64 rows of x, tcgen05.mma kind::i8, for INT8 weights (padded batch 16-64) and INT4
-// weights without outliers (padded batch 16; tq_supported).
+// up to 64 rows of x, tcgen05.mma kind::i8, for INT8 weights and INT4 weights without outliers
+// (padded batch 16-64; tq_supported).
 //
 // Same results contract as quant::gemv_int4 / gemv_int8 (crates/paraoxidizer-quant/src/
 // kernels.rs:177-255) within the GEMV tolerance, computed the way the batch <= 8 GEMV does:
@@ -54,12 +54,13 @@ __host__ __device__ constexpr int tq_astages(int kind, int NP) {  // 16 KiB A st
 }
 __host__ __device__ constexpr int tq_smem(int kind, int NP) { return tq_astages(kind, NP) * 16384 + tq_fixed(kind, NP); }
 
-// Where this path beats the f16 tiles of gemm_tc05.cu (measured on 4096 x 14336 and 14336 x 4096):
-// INT8 up to a padded batch of 64, INT4 at 16. Past that, the per-block readout of every batch
-// column and the shared-memory traffic of unpacking (about six times the weight bytes) outweigh
-// the cheaper unpacking.
+// Where this path beats the f16 tiles of gemm_tc05.cu (us per call with its x preparation, B200,
+// f16 tiles vs this kernel): INT8 up to a padded batch of 64; INT4 without outliers up to 64 too
+// (4096 x 14336: 28.9 vs 26.6 at batch 32, 34.5 vs 32.0 at 64; 28672 x 4096: 51.9 vs 41.8 and
+// 58.3 vs 51.6; 6144 x 4096 and 4096 x 4096 within 6 % either way). At a padded batch of 128 the
+// per-block readout of every batch column outweighs the cheaper unpacking.
 bool tq_supported(int kind, bool outliers, int Bp) {
-    return (kind == kKindI4 && !outliers && Bp == 16) || (kind == kKindI8 && Bp <= 64);
+    return (kind == kKindI4 && !outliers && Bp <= 64) || (kind == kKindI8 && Bp <= 64);
 }
 size_t tq_x_bytes(int K, int Bp) {
     const size_t limbs = (size_t)(K / 128) * 2 * Bp * 128;

@@ -140,7 +140,7 @@ def test_small_m_agrees_with_gemv_path(be):
 
 def test_kernel_choice_by_batch(be):
     """Which kernel serves a call: mma.sync GEMV up to batch 8, the integer tensor-core path for
-    INT8 (padded batch <= 64) and INT4 without outliers (padded batch 16), the f16 tiles otherwise;
+    INT8 and INT4 without outliers (padded batch <= 64), the f16 tiles otherwise;
     below batch 9 the integer path takes over where it was measured faster (INT4 with K >= 8192 from
     batch 6, INT8 with >= 16 M weights from batch 2)."""
     t4, _ = make(be, "i4", 256, 1024, 1)
@@ -150,7 +150,8 @@ def test_kernel_choice_by_batch(be):
     t8big, _ = make(be, "i8", 4096, 4096, 5)
     assert t4.gemv_kernel(8) == "gemv_tc_kernel"
     assert t4.gemv_kernel(16) == "gemm_tq_kernel"
-    assert t4.gemv_kernel(33) == "gemm_tc05_kernel"
+    assert t4.gemv_kernel(64) == "gemm_tq_kernel"
+    assert t4.gemv_kernel(65) == "gemm_tc05_kernel"
     assert t4o.gemv_kernel(16) == "gemm_tc05_kernel"
     assert t8.gemv_kernel(4) == "gemv_tc_kernel"
     assert t8.gemv_kernel(64) == "gemm_tq_kernel"

@@ -38,7 +38,7 @@ namespace pox {
 constexpr int kTqProd = 8;     // producer warps (row tiles of 16 rows)
 constexpr int kTqErr = 32;     // bit of the kernel error flag
 constexpr int kTqPf = 4;       // INT4 scale words read this many blocks ahead
-__host__ __device__ constexpr int tq_epi(int NP) { return NP == 128 ? 8 : 4; }             // epilogue warps
+__host__ __device__ constexpr int tq_epi(int NP) { return NP >= 64 ? 8 : 4; }              // epilogue warps
 __host__ __device__ constexpr int tq_threads(int NP) { return (kTqProd + 2 + tq_epi(NP)) * 32; }
 __host__ __device__ constexpr int tq_slots(int NP) { return NP == 128 ? 4 : 8; }            // TMEM slots
 __host__ __device__ constexpr int tq_tmem_cols(int NP) { return tq_slots(NP) * NP < 32 ? 32 : tq_slots(NP) * NP; }

@@ -74,6 +74,8 @@ struct XTarget {
     int Kp = 0, nxbs = 0;
     uint8_t* xs = nullptr;
     float* xscale = nullptr;
+    uint8_t* xl = nullptr;   // integer small-M path: limbs [K/128][2 Bp][128 B] (swizzled), then
+    float2* xm = nullptr;    // (max|x|/16383, sum x) [K/128][Bp]
     int Bp = 0;
 };
 int gemv_x_target(pox_cuda_ctx* ctx, const pox_tensor* t, size_t batch, cudaStream_t st, XTarget* out);

@@ -250,14 +250,18 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const float* __restric
 // 128 blk + d. Writes att (f32) and, for the GEMV that follows:
 //  * cols / meta (batch <= 8): the 15-bit two-limb fixed point of the block and (max/16383, sum),
 //    as xprep_int_kernel computes them;
-//  * xs (small-M path): f16(att) in the 128-byte-swizzled k-block-major layout, row scale 1 (|att|
-//    <= max|v| <= 65504, the f16 range, so no scaling is needed).
+//  * xl / xm (integer small-M path): the same limbs as rows 2b / 2b + 1 of each block's
+//    128-byte-swizzled [2 Bp][128 B] tile, and the block's (max/16383, sum) at [block][b];
+//  * xs (f16 small-M path): f16(att) in the 128-byte-swizzled k-block-major layout, row scale 1
+//    (|att| <= max|v| <= 65504, the f16 range, so no scaling is needed).
 struct OPrep {
     uint8_t* cols = nullptr;
     float2* meta = nullptr;
     int Kp = 0, nxbs = 0;
     uint8_t* xs = nullptr;
     float* xscale = nullptr;
+    uint8_t* xl = nullptr;
+    float2* xm = nullptr;
     int Bp = 0;
 };
 __global__ void __launch_bounds__(128) attn_combine_kernel(const uint32_t* __restrict__ pos, int nq, int nkv, int G,
@@ -285,7 +289,7 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const uint32_t* __res
     const float v = num * inv;
     const int K = nq * hd;
     att[(size_t)b * K + e] = v;
-    if (op.cols) {
+    if (op.cols || op.xl) {
         __shared__ float red[4];
         const int warp = d >> 5, lane = d & 31;
         float m = warp_max(fabsf(v));
@@ -295,14 +299,23 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const uint32_t* __res
         __syncthreads();
         const float qi = m > 0.f ? (float)kXLimbMax / m : 0.f;
         const int X = max(-kXLimbMax, min(kXLimbMax, __float2int_rn(v * qi)));
-        op.cols[(size_t)(2 * b) * op.Kp + e] = (uint8_t)((uint32_t)(X >> 7) & 0xFFu);
-        op.cols[(size_t)(2 * b + 1) * op.Kp + e] = (uint8_t)((uint32_t)X & 0x7Fu);
+        const uint8_t hi = (uint8_t)((uint32_t)(X >> 7) & 0xFFu), lo = (uint8_t)((uint32_t)X & 0x7Fu);
+        if (op.cols) {
+            op.cols[(size_t)(2 * b) * op.Kp + e] = hi;
+            op.cols[(size_t)(2 * b + 1) * op.Kp + e] = lo;
+        } else {
+            uint8_t* tile = op.xl + (size_t)blk * (2 * op.Bp) * 128;  // blk = e / 128
+            tile[sw128_off(2 * b, d >> 4) + (d & 15)] = hi;
+            tile[sw128_off(2 * b + 1, d >> 4) + (d & 15)] = lo;
+        }
         const float sw = warp_sum(v);
         if (lane == 0) red[warp] = sw;
         __syncthreads();
-        if (d == 0)
-            op.meta[(size_t)b * op.nxbs + blk] =
-                make_float2(m > 0.f ? m / (float)kXLimbMax : 0.f, (red[0] + red[1]) + (red[2] + red[3]));
+        const float2 mt = make_float2(m > 0.f ? m / (float)kXLimbMax : 0.f, (red[0] + red[1]) + (red[2] + red[3]));
+        if (d == 0) {
+            if (op.cols) op.meta[(size_t)b * op.nxbs + blk] = mt;
+            else op.xm[(size_t)blk * op.Bp + b] = mt;
+        }
     } else if (op.xs) {
         const int kb = e >> 7, kk = e & 127;
         const size_t off = ((size_t)kb * 2 + (kk >> 6)) * (size_t)op.Bp * 128 + sw128_off(b, (kk & 63) >> 3) + 2 * (kk & 7);
@@ -534,6 +547,8 @@ static int decode_step(pox_model* m, int B, cudaStream_t st) {
             op.nxbs = xt.nxbs;
             op.xs = xt.xs;
             op.xscale = xt.xscale;
+            op.xl = xt.xl;
+            op.xm = xt.xm;
             op.Bp = xt.Bp;
         }
         e = launch_pdl(attn_combine_kernel, dim3((m->nq * m->hd + 127) / 128, B), dim3(128), 0, st,

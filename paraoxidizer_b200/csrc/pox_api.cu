@@ -546,12 +546,13 @@ static int tc05_gemv(pox_cuda_ctx* ctx, const pox_tensor* t, int kind, const flo
         if (opb.up) opb.up += done * (size_t)opb.ld_up;
         cudaError_t e = cudaSuccess;
         if (tq_supported(kind, t->nnz > 0, Bp)) {
-            // integer tensor cores: x as exact int8 limbs of 128-k blocks (the caller's prepared
-            // f16 x does not apply: gemv_x_target declines these tensors)
-            if (prepared) return set_error(POX_ERR_INVALID, "prepared x: the integer small-M path prepares its own");
+            // integer tensor cores: x as exact int8 limbs of 128-k blocks, prepared here or by the
+            // caller at gemv_x_target's xl / xm
             float2* xm = reinterpret_cast<float2*>(xs + (((size_t)(K / 128) * 2 * Bp * 128 + 255) & ~(size_t)255));
-            e = launch_xprep_tq(x + done * ldx, b, Bp, K, opb, xs, xm, st);
-            if (e != cudaSuccess) return cuda_error(e, "x preparation launch");
+            if (!prepared) {
+                e = launch_xprep_tq(x + done * ldx, b, Bp, K, opb, xs, xm, st);
+                if (e != cudaSuccess) return cuda_error(e, "x preparation launch");
+            }
             TqArgs q = {};
             q.w = (const uint8_t*)t->w;
             q.xl = xs;
@@ -640,11 +641,14 @@ int pox::gemv_x_target(pox_cuda_ctx* ctx, const pox_tensor* t, size_t batch, cud
     if (!t->tiled || t->dtype != POX_I4 || t->cols % 128 != 0) return set_error(POX_ERR_UNSUPPORTED, "no prepared-x path");
     if (gemv_uses_small_m(t, batch)) {
         if (batch > 128) return set_error(POX_ERR_UNSUPPORTED, "prepared x holds up to 128 rows");
-        if (tq_supported(kKindI4, t->nnz > 0, tc05_pad((int)batch)))  // the integer path prepares x itself
-            return set_error(POX_ERR_UNSUPPORTED, "no prepared-x path on the integer small-M path");
         int rc = ensure_tc_scratch(ctx, t->rows, t->cols, batch, st);
         if (rc) return rc;
         out->Bp = tc05_pad((int)batch);
+        if (tq_supported(kKindI4, t->nnz > 0, out->Bp)) {  // as tc05_gemv's integer branch places them
+            out->xl = static_cast<uint8_t*>(ctx->tc_scratch);
+            out->xm = reinterpret_cast<float2*>(out->xl + (((t->cols / 128) * 2 * (size_t)out->Bp * 128 + 255) & ~(size_t)255));
+            return POX_OK;
+        }
         out->xs = static_cast<uint8_t*>(ctx->tc_scratch);
         out->xscale = reinterpret_cast<float*>(out->xs + tc_x_region(t->cols, out->Bp));  // as tc05_gemv places them
         return POX_OK;

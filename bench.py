@@ -286,10 +286,20 @@ def batched_gemv_bench(be, batches=(1, 4, 16, 64), reps=400):
 
 LLAMA_8B = {"hidden": 4096, "inter": 14336, "layers": 32, "n_heads": 32, "n_kv_heads": 8, "vocab": 128256,
             "rms_eps": 1e-5, "rope_theta": 500000.0}
+LLAMA_70B = {"hidden": 8192, "inter": 28672, "layers": 80, "n_heads": 64, "n_kv_heads": 8, "vocab": 128256,
+             "rms_eps": 1e-5, "rope_theta": 500000.0}
+# decode workloads: (config, default batches, context before the timed steps, how it is reached,
+# outlier sigma of the projections)
+DECODE_MODELS = {
+    "llama8b": (LLAMA_8B, "1,8,32", 512, "tokens", None),
+    # context 4096 reached by reserving the pages (token-by-token prefill of 4096 x 80 layers would
+    # dominate the run); the pages hold whatever the allocation held, which only changes values
+    "llama70b": (LLAMA_70B, "1,16,64", 4096, "reserve", 3.5),
+}
 
 
 def decode_bench(be, cfg=LLAMA_8B, batches=(1, 8, 32), prefill=512, steps=256, warm=3, seed=0, world=1, rank=0,
-                 modes=("peer", "nccl")):
+                 modes=("peer", "nccl"), prefill_mode="tokens", outlier_sigma=None, name="llama-3-8b"):
     """Llama-3-8B-architecture INT4 g128 decode (random-init weights): prefill of `prefill` random
     token ids fed token by token (the reference prefills through forward_token, engine.rs:760-762),
     then `steps` greedy decode steps timed as CUDA-graph replays of one step on the device. With
@@ -303,7 +313,8 @@ def decode_bench(be, cfg=LLAMA_8B, batches=(1, 8, 32), prefill=512, steps=256, w
     runs = len(modes) if world > 1 else 1
     bps = (prefill + steps * runs + warm + 15) // 16
     t0 = time.perf_counter()
-    model = build_llama_on_device(be, cfg, max_b, max_b * bps, bps, seed=seed, tp_rank=rank, tp_size=world)
+    model = build_llama_on_device(be, cfg, max_b, max_b * bps, bps, seed=seed, tp_rank=rank, tp_size=world,
+                                  outlier_sigma=outlier_sigma)
     if world > 1:
         model.init_comm(modes=modes)
     build_s = time.perf_counter() - t0
@@ -317,8 +328,14 @@ def decode_bench(be, cfg=LLAMA_8B, batches=(1, 8, 32), prefill=512, steps=256, w
         prompts = rng.integers(0, cfg["vocab"], (B, prefill))
         t0 = time.perf_counter()
         nxt = None
-        for p in range(prefill):
-            _, nxt = model.decode(prompts[:, p], seqs, want_logits=False)
+        if prefill_mode == "reserve":
+            for sq in seqs:
+                sq.reserve(model.blocks, prefill)
+                sq.sequence_len = prefill
+            nxt = prompts[:, -1].astype(np.uint32)
+        else:
+            for p in range(prefill):
+                _, nxt = model.decode(prompts[:, p], seqs, want_logits=False)
         prefill_s = time.perf_counter() - t0
         for sq in seqs:
             sq.reserve(model.blocks, steps * runs + warm)
@@ -360,7 +377,7 @@ def decode_bench(be, cfg=LLAMA_8B, batches=(1, 8, 32), prefill=512, steps=256, w
                        "bytes_per_step": int(bytes_step), "achieved_gbs": round(bytes_step / sec / 1e9, 1),
                        "roofline_frac": round(bytes_step / sec / 1e9 / peak, 4),
                        "roofline_tokens_per_s": round(B * peak * 1e9 / bytes_step, 1),
-                       "prefill_tokens_per_s": round(B * prefill / prefill_s, 1)}
+                       "prefill_tokens_per_s": round(B * prefill / prefill_s, 1) if prefill_mode == "tokens" else None}
         if world > 1:
             out[str(B)]["exchange"] = modes[0]
             out[str(B)]["tokens_per_s_by_exchange"] = {k: round(B / v, 1) for k, v in per_mode.items()}
@@ -368,17 +385,28 @@ def decode_bench(be, cfg=LLAMA_8B, batches=(1, 8, 32), prefill=512, steps=256, w
             sq.free(model.blocks)
     model.close()
     torch.cuda.empty_cache()
-    return {"model": "llama-3-8b architecture, INT4 g128 projections (GPU quantizer), f16 embed/lm_head, "
+    return {"model": f"{name} architecture, INT4 g128 projections (GPU quantizer"
+                     + (f", {outlier_sigma}-sigma outliers" if outlier_sigma else "") + "), f16 embed/lm_head, "
                      "random-init N(0,0.02)", "kv": "fp16 pages of 16 tokens", "prefill": prefill,
+            "context": "prefill tokens fed one by one" if prefill_mode == "tokens" else
+                       "pages reserved for the prefill length (no prefill compute)",
             "parallelism": f"tp{world}" if world > 1 else "single GPU",
             "bytes_per_step": "per GPU: its weight shard + its kv heads' pages (roofline = that / measured HBM peak)",
             "decode_steps_timed": steps - 1, "build_s": round(build_s, 1), "per_batch": out}
 
 
 def decode_batches(args):
-    if args.decode_batches in ("", "none"):
+    spec = args.decode_batches if args.decode_batches is not None else DECODE_MODELS[args.decode_model][1]
+    if spec in ("", "none"):
         return ()
-    return tuple(int(b) for b in args.decode_batches.split(","))
+    return tuple(int(b) for b in spec.split(","))
+
+
+def decode_kwargs(args):
+    cfg, _, ctx, mode, osig = DECODE_MODELS[args.decode_model]
+    return dict(cfg=cfg, prefill=args.decode_prefill if args.decode_prefill is not None else ctx,
+                prefill_mode=mode, outlier_sigma=osig, name={"llama8b": "llama-3-8b", "llama70b": "llama-3-70b"}[
+                    args.decode_model])
 
 
 def run_decode_only(args):
@@ -394,8 +422,8 @@ def run_decode_only(args):
         bg = batched_gemv_bench(be, batches=tuple(int(b) for b in args.batched_sizes.split(",")))
     d = None
     if decode_batches(args):
-        d = decode_bench(be, batches=decode_batches(args), prefill=args.decode_prefill, steps=args.decode_steps,
-                         world=world, rank=rank)
+        d = decode_bench(be, batches=decode_batches(args), steps=args.decode_steps, world=world, rank=rank,
+                         **decode_kwargs(args))
     if rank == 0:
         print(json.dumps({"batched_gemv": bg, "decode": d}), flush=True)
     be.close()
@@ -510,8 +538,8 @@ def run_ours(args):
 
     decode = None
     if not args.no_decode:
-        decode = decode_bench(be, batches=decode_batches(args), prefill=args.decode_prefill,
-                              steps=args.decode_steps, world=world, rank=rank)
+        decode = decode_bench(be, batches=decode_batches(args), steps=args.decode_steps, world=world, rank=rank,
+                              **decode_kwargs(args))
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -562,8 +590,10 @@ def main():
                     help="run only the decode benchmark (one JSON object; for launch lists and captures)")
     ap.add_argument("--with-batched", action="store_true", help="--decode-only: also run the batched GEMV bench")
     ap.add_argument("--batched-sizes", default="1,4,16,64", help="--with-batched: rows of x per call")
-    ap.add_argument("--decode-batches", default="1,8,32", help="comma list, or 'none'")
-    ap.add_argument("--decode-prefill", type=int, default=512)
+    ap.add_argument("--decode-model", default="llama8b", choices=sorted(DECODE_MODELS),
+                    help="decode workload (the default run uses llama8b)")
+    ap.add_argument("--decode-batches", default=None, help="comma list, or 'none' (default: the model's)")
+    ap.add_argument("--decode-prefill", type=int, default=None, help="context before the timed steps")
     ap.add_argument("--decode-steps", type=int, default=256)
     args = ap.parse_args()
     if args.warmup < 3:

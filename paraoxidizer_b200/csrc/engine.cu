@@ -68,6 +68,17 @@ __device__ __forceinline__ void rope_cs(uint32_t p, int i, int hd, float theta, 
         s = sinf(angle);
     }
 }
+// The (cos, sin) table of every position a sequence of the model can reach, computed once with
+// rope_cs, so attention looks the values up instead of evaluating powf / cosf / sinf in each of
+// its context splits (identical bits either way).
+__global__ void rope_table_kernel(float2* __restrict__ t, int npos, int hd, float theta) {
+    const int half = hd / 2;
+    const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= (long long)npos * half) return;
+    float c, s;
+    rope_cs((uint32_t)(idx / half), (int)(idx % half), hd, theta, c, s);
+    t[idx] = make_float2(c, s);
+}
 __device__ __forceinline__ float2 rope_pair(float a0, float a1, float c, float s) {
     return make_float2(__fsub_rn(__fmul_rn(a0, c), __fmul_rn(a1, s)), __fadd_rn(__fmul_rn(a0, s), __fmul_rn(a1, c)));
 }
@@ -85,14 +96,15 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const float* __restric
                                                           const uint32_t* __restrict__ pos,
                                                           const int32_t* __restrict__ btab, int mbps,
                                                           __half* __restrict__ kc, __half* __restrict__ vc, int layer,
-                                                          int L, int nq, int nkv, int G, int max_splits, float theta,
-                                                          float* __restrict__ apart) {
+                                                          int L, int nq, int nkv, int G, int max_splits,
+                                                          const float2* __restrict__ rope, float* __restrict__ apart) {
     constexpr int DH = HD / 2;   // K dims per lane (two lanes per token)
     constexpr int DPL = HD / 32; // V dims per lane
     pdl_launch_dependents();
     pdl_wait();
     const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const uint32_t p = pos[b];
+    if (p >= (uint32_t)mbps * kPage) return;  // beyond the block table (invalid input): no out-of-range access
     const int ctx = (int)p + 1;
     const int t0 = split * kSplitTok;
     if (t0 >= ctx) return;  // the combine kernel reads only ceil(ctx / 64) splits
@@ -103,12 +115,12 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const float* __restric
     __shared__ float red_m[4][8], red_l[4][8];
     __shared__ float acc_s[4][8][HD];
     const float* row = qkv + (size_t)b * qkv_rows;
+    const float2* rp = rope + (size_t)p * DH;  // (cos, sin) of the pairs at position p
     for (int j = tid; j < G * DH; j += 128) {
         const int g = j / DH, i = j % DH;
-        float c, sn;
-        rope_cs(p, i, HD, theta, c, sn);
+        const float2 cs = rp[i];
         const float* q = row + (size_t)(h * G + g) * HD;
-        const float2 r = rope_pair(q[2 * i], q[2 * i + 1], c, sn);
+        const float2 r = rope_pair(q[2 * i], q[2 * i + 1], cs.x, cs.y);
         qs[g][2 * i] = r.x;
         qs[g][2 * i + 1] = r.y;
     }
@@ -118,9 +130,8 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const float* __restric
         const float* k = row + (size_t)(nq + h) * HD;
         const float* v = row + (size_t)(nq + nkv + h) * HD;
         for (int i = tid; i < DH; i += 128) {
-            float c, sn;
-            rope_cs(p, i, HD, theta, c, sn);
-            const float2 r = rope_pair(k[2 * i], k[2 * i + 1], c, sn);
+            const float2 cs = rp[i];
+            const float2 r = rope_pair(k[2 * i], k[2 * i + 1], cs.x, cs.y);
             *reinterpret_cast<__half2*>(kc + off + 2 * i) = __floats2half2_rn(r.x, r.y);
             *reinterpret_cast<__half2*>(vc + off + 2 * i) = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
         }
@@ -272,7 +283,7 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const uint32_t* __res
     const int blk = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
     const int e = blk * 128 + d, hq = e / hd, dd = e % hd;
     if (e >= nq * hd) return;  // only when nq hd % 128 != 0, where nothing is prepared (no barrier below)
-    const int ns = ((int)pos[b] + 1 + kSplitTok - 1) / kSplitTok;
+    const int ns = min(max_splits, (int)((pos[b] + (uint32_t)kSplitTok) / kSplitTok));  // ceil((pos + 1) / 64)
     const int h = hq / G, g = hq % G;
     const float* base = apart + (((size_t)b * nkv + h) * max_splits * G + g) * (hd + 2);
     const size_t sstride = (size_t)G * (hd + 2);
@@ -524,15 +535,15 @@ static int decode_step(pox_model* m, int B, cudaStream_t st) {
         if (m->hd == 128)
             e = launch_pdl(attn_decode_kernel<128>, ag, dim3(128), 0, st, (const float*)m->qkv, m->qkv_rows,
                            (const uint32_t*)m->pos, (const int32_t*)m->btab, (int)m->max_blocks_per_seq, m->kc, m->vc,
-                           l, m->L, m->nq, m->nkv, m->G, m->max_splits, m->cfg.rope_theta, m->apart);
+                           l, m->L, m->nq, m->nkv, m->G, m->max_splits, (const float2*)m->rope, m->apart);
         else if (m->hd == 64)
             e = launch_pdl(attn_decode_kernel<64>, ag, dim3(128), 0, st, (const float*)m->qkv, m->qkv_rows,
                            (const uint32_t*)m->pos, (const int32_t*)m->btab, (int)m->max_blocks_per_seq, m->kc, m->vc,
-                           l, m->L, m->nq, m->nkv, m->G, m->max_splits, m->cfg.rope_theta, m->apart);
+                           l, m->L, m->nq, m->nkv, m->G, m->max_splits, (const float2*)m->rope, m->apart);
         else
             e = launch_pdl(attn_decode_kernel<32>, ag, dim3(128), 0, st, (const float*)m->qkv, m->qkv_rows,
                            (const uint32_t*)m->pos, (const int32_t*)m->btab, (int)m->max_blocks_per_seq, m->kc, m->vc,
-                           l, m->L, m->nq, m->nkv, m->G, m->max_splits, m->cfg.rope_theta, m->apart);
+                           l, m->L, m->nq, m->nkv, m->G, m->max_splits, (const float2*)m->rope, m->apart);
         if (e != cudaSuccess) return cuda_error(e, "attention launch");
         // the combine writes the o projection's prepared input when that tensor takes one
         OPrep op;
@@ -648,6 +659,7 @@ extern "C" int pox_cuda_model_create_tp(pox_cuda_ctx* ctx, const pox_llama_confi
         {(void**)&m->pos, B * 4},
         {(void**)&m->next, B * 4},
         {(void**)&m->btab, B * max_blocks_per_seq * 4},
+        {(void**)&m->rope, (size_t)max_blocks_per_seq * kPage * (m->hd / 2) * sizeof(float2)},
     };
     for (auto& a : allocs) {
         e = cudaMalloc(a.p, a.bytes);
@@ -668,6 +680,11 @@ extern "C" int pox_cuda_model_create_tp(pox_cuda_ctx* ctx, const pox_llama_confi
     }
     cudaMemsetAsync(m->kc, 0, kv_elems * 2, ctx->stream);
     cudaMemsetAsync(m->vc, 0, kv_elems * 2, ctx->stream);
+    {
+        const long long n = (long long)max_blocks_per_seq * kPage * (m->hd / 2);
+        rope_table_kernel<<<(unsigned)((n + 255) / 256), 256, 0, ctx->stream>>>(
+            m->rope, (int)(max_blocks_per_seq * kPage), m->hd, m->cfg.rope_theta);
+    }
     e = cudaStreamSynchronize(ctx->stream);
     if (e != cudaSuccess) return cuda_error(e, "cudaMemset(KV pages)");
     ctx->models.push_back(m);
@@ -702,7 +719,7 @@ static void destroy_model(pox_model* m) {
     }
     free_tensor(ctx, m->lm_head);
     void* bufs[] = {m->embed, m->final_norm, m->kc, m->vc, m->x, m->qkv, m->att, m->gu, m->logits, m->apart,
-                    m->amax, m->tok, m->pos, m->next, m->btab};
+                    m->amax, m->tok, m->pos, m->next, m->btab, m->rope};
     for (void* p : bufs) cudaFree(p);
     comm_free(m->comm);
     delete m;

@@ -47,6 +47,7 @@ struct pox_model {
     float* gu = nullptr;      // [B][2 I]
     float* logits = nullptr;  // [B][V]
     float* apart = nullptr;   // [B][nkv][max_splits][G][hd + 2]
+    float2* rope = nullptr;   // [max_blocks_per_seq * 16][hd / 2]: (cos, sin) of RoPE pair i at position p
     float2* amax = nullptr;   // [B][kArgmaxParts] first-pass argmax pairs
     uint32_t* tok = nullptr;  // [B]
     uint32_t* pos = nullptr;  // [B]

@@ -70,13 +70,18 @@ def oracle_weights(weights: dict) -> dict:
 
 
 def build_llama_on_device(backend, cfg: dict, max_batch: int, kv_blocks: int, max_blocks_per_seq: int, seed: int = 0,
-                          sigma: float = 0.02, tp_rank: int = 0, tp_size: int = 1):
+                          sigma: float = 0.02, tp_rank: int = 0, tp_size: int = 1, outlier_sigma=None):
     """A CudaModel with random-init N(0, sigma) weights generated on the GPU: projections quantized
     INT4 g128 by the GPU quantizer (bit-exact with quantize_int4_group) and uploaded from device
     memory; embedding and lm_head f16; norms 1.0. q/k/v and gate/up are drawn as stacked
     tensors (per-row quantization makes that identical to quantizing them separately).
     With tp_size > 1 only rank tp_rank's shard is drawn (shapes of tp.shard_llama; the draws
-    differ from the whole model's, which a throughput benchmark does not need)."""
+    differ from the whole model's, which a throughput benchmark does not need).
+    With outlier_sigma (3.5 = the Automatic policy) each drawn projection first loses the values
+    with |w - mean| > outlier_sigma * std to an f16 outlier table (extract_and_zero_outliers,
+    outlier.rs:57-85, over the stacked tensor, with torch's mean / std instead of the sequential
+    f32 sums: the table is for throughput, not parity); those tensors are uploaded from host
+    memory, as the outlier upload requires."""
     import ctypes as C
 
     import torch
@@ -94,20 +99,42 @@ def build_llama_on_device(backend, cfg: dict, max_batch: int, kv_blocks: int, ma
 
     def tensor(rows, cols):
         w = torch.randn(rows * cols, device="cuda", generator=gen, dtype=torch.float32).mul_(sigma)
+        table = None
+        if outlier_sigma:
+            mean = w.mean()
+            thr = outlier_sigma * w.std(correction=0)
+            idx = torch.nonzero((w - mean).abs() > thr).flatten()
+            vals = w[idx].half()
+            w[idx] = 0.0
+            n = idx.numel()
+            table = np.empty(4 + 6 * n, np.uint8)
+            table[:4] = np.frombuffer(np.uint32(n).tobytes(), np.uint8)
+            table[4:4 + 4 * n] = idx.to(torch.int32).cpu().numpy().view(np.uint8)
+            table[4 + 4 * n:] = vals.cpu().numpy().view(np.uint8)
+            del idx, vals
+            outlier_bytes[0] += table.size
         p = torch.empty(rows * cols // 2, dtype=torch.uint8, device="cuda")
         s = torch.empty(rows * cols // 128 * 4, dtype=torch.uint8, device="cuda")
         torch.cuda.synchronize()
         L.check(lib.pox_cuda_quantize_int4(backend.ctx, w.data_ptr(), rows * cols, 128, p.data_ptr(), s.data_ptr(),
                                            None))
         backend.synchronize()
+        del w
         d = L.TensorDesc()
         d.dtype, d.rows, d.cols, d.group_size = L.POX_I4, rows, cols, 128
-        d.data, d.data_len, d.scales, d.scale_len = p.data_ptr(), p.numel(), s.data_ptr(), s.numel()
+        if table is None:
+            d.data, d.data_len, d.scales, d.scale_len = p.data_ptr(), p.numel(), s.data_ptr(), s.numel()
+        else:
+            ph, sh = p.cpu().numpy(), s.cpu().numpy()
+            d.data, d.data_len = ph.ctypes.data, ph.size
+            d.scales, d.scale_len = sh.ctypes.data, sh.size
+            d.outliers, d.outlier_len = table.ctypes.data, table.size
         h = C.c_void_p()
         L.check(lib.pox_cuda_tensor_upload(backend.ctx, C.byref(d), C.byref(h)))
         return h.value
 
     ones = np.ones(H, np.float32).astype(np.float16).view(np.uint16)
+    outlier_bytes = [0]
     weight_bytes = 0
     for l in range(cfg["layers"]):
         shapes = [(qd + 2 * kvd, H), (H, qd), (2 * I, H), (H, I)]
@@ -121,5 +148,5 @@ def build_llama_on_device(backend, cfg: dict, max_batch: int, kv_blocks: int, ma
     model.set_embeddings_device(embed.data_ptr(), fn.data_ptr(), head.data_ptr())
     del embed, head, fn
     torch.cuda.empty_cache()
-    model.weight_bytes = weight_bytes + V * H * 2 + (2 * cfg["layers"] + 1) * H * 2
+    model.weight_bytes = weight_bytes + outlier_bytes[0] + V * H * 2 + (2 * cfg["layers"] + 1) * H * 2
     return model

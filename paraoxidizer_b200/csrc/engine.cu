@@ -255,6 +255,193 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const float* __restric
     }
 }
 
+// Tensor-core variant of attn_decode_kernel for head_dim 128 and 4..8 query heads per kv head
+// (the Llama-3 8B / 70B layouts); same grid, splits, RoPE, KV append and partial output. Each warp
+// stages its page of K and V (16 tokens) in shared memory and runs both products on mma.sync
+// m16n8k16 with f32 accumulation: S = Q K^T with the G query heads as the rows of A (padded to
+// 16) and q split into two f16 terms (hi = f16(q), lo = f16(q - hi), so q keeps 22 bits), then
+// O = P V with P likewise split. Fragments come from ldmatrix (V transposed); rows of a page past
+// the context are zero.
+__device__ __forceinline__ void ldsm_x4(uint32_t a, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(a));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t a, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(a));
+}
+// (hi, lo) f16 pairs of (x0, x1): hi = f16(x), lo = f16(x - hi)
+__device__ __forceinline__ void split_f16x2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(x0, x1);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(x0 - hf.x, x1 - hf.y);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+template <int HD>
+__global__ void __launch_bounds__(128) attn_decode_tc_kernel(const float* __restrict__ qkv, int qkv_rows,
+                                                             const uint32_t* __restrict__ pos,
+                                                             const int32_t* __restrict__ btab, int mbps,
+                                                             __half* __restrict__ kc, __half* __restrict__ vc,
+                                                             int layer, int L, int nq, int nkv, int G,
+                                                             int max_splits, const float2* __restrict__ rope,
+                                                             float* __restrict__ apart) {
+    static_assert(HD == 128, "head_dim 128");
+    constexpr int DH = HD / 2;
+    constexpr int RS = HD + 8;  // staged row stride in halves (272 B: ldmatrix rows in distinct banks)
+    pdl_launch_dependents();
+    pdl_wait();
+    const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+    const uint32_t p = pos[b];
+    if (p >= (uint32_t)mbps * kPage) return;  // beyond the block table (invalid input): no out-of-range access
+    const int ctx = (int)p + 1;
+    const int t0 = split * kSplitTok;
+    if (t0 >= ctx) return;  // the combine kernel reads only ceil(ctx / 64) splits
+    const int nt = min(ctx - t0, kSplitTok);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    __shared__ float qs[8][HD];
+    __shared__ float red_m[4][8], red_l[4][8];
+    __shared__ __align__(16) __half kv_s[2][4][16][RS];  // [K, V][warp][token][dim]; then the warps' outputs
+    float (*acc_s)[8][HD] = reinterpret_cast<float (*)[8][HD]>(&kv_s[0][0][0][0]);
+    const float* row = qkv + (size_t)b * qkv_rows;
+    const float2* rp = rope + (size_t)p * DH;  // (cos, sin) of the pairs at position p
+    for (int j = tid; j < G * DH; j += 128) {
+        const int g = j / DH, i = j % DH;
+        const float2 cs = rp[i];
+        const float* q = row + (size_t)(h * G + g) * HD;
+        const float2 r = rope_pair(q[2 * i], q[2 * i + 1], cs.x, cs.y);
+        qs[g][2 * i] = r.x;
+        qs[g][2 * i + 1] = r.y;
+    }
+    if ((int)p < t0 + kSplitTok) {  // this split holds the new position: append k, v
+        const int blk = btab[(size_t)b * mbps + p / kPage];
+        const size_t off = ((((size_t)blk * L + layer) * nkv + h) * kPage + p % kPage) * HD;
+        const float* k = row + (size_t)(nq + h) * HD;
+        const float* v = row + (size_t)(nq + nkv + h) * HD;
+        for (int i = tid; i < DH; i += 128) {
+            const float2 cs = rp[i];
+            const float2 r = rope_pair(k[2 * i], k[2 * i + 1], cs.x, cs.y);
+            *reinterpret_cast<__half2*>(kc + off + 2 * i) = __floats2half2_rn(r.x, r.y);
+            *reinterpret_cast<__half2*>(vc + off + 2 * i) = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+        }
+    }
+    __syncthreads();
+
+    // this warp's page (tokens t0 + 16 warp ..) staged in shared memory, rows past the context zero
+    const int nw = max(0, min(16, nt - 16 * warp));
+    {
+        size_t page = 0;
+        if (nw > 0) {
+            const int blk = btab[(size_t)b * mbps + (t0 + 16 * warp) / kPage];
+            page = (((size_t)blk * L + layer) * nkv + h) * kPage * HD;
+        }
+#pragma unroll
+        for (int u = 0; u < 16 * (HD / 8) / 32; u++) {
+            const int idx = lane + 32 * u, r = idx / (HD / 8), c = idx % (HD / 8);
+            uint4 kv = make_uint4(0u, 0u, 0u, 0u), vv = kv;
+            if (r < nw) {
+                kv = __ldcg(reinterpret_cast<const uint4*>(kc + page + (size_t)r * HD) + c);
+                vv = __ldcg(reinterpret_cast<const uint4*>(vc + page + (size_t)r * HD) + c);
+            }
+            *reinterpret_cast<uint4*>(&kv_s[0][warp][r][8 * c]) = kv;
+            *reinterpret_cast<uint4*>(&kv_s[1][warp][r][8 * c]) = vv;
+        }
+    }
+    __syncwarp();
+
+    const int g = lane >> 2, t = lane & 3, mi = lane >> 3, mr = lane & 7;
+    // S = Q K^T: A rows = query heads (g < G; rows g + 8 are padding), B = the staged K rows
+    float sacc[2][4];
+#pragma unroll
+    for (int nb = 0; nb < 2; nb++) sacc[nb][0] = sacc[nb][1] = sacc[nb][2] = sacc[nb][3] = 0.f;
+    const uint32_t kbase = smem_u32(&kv_s[0][warp][0][0]), vbase = smem_u32(&kv_s[1][warp][0][0]);
+#pragma unroll
+    for (int ks = 0; ks < HD / 16; ks++) {
+        uint32_t qh0, ql0, qh1, ql1;
+        const int c0 = 16 * ks + 2 * t;
+        split_f16x2(g < G ? qs[g][c0] : 0.f, g < G ? qs[g][c0 + 1] : 0.f, qh0, ql0);
+        split_f16x2(g < G ? qs[g][c0 + 8] : 0.f, g < G ? qs[g][c0 + 9] : 0.f, qh1, ql1);
+        uint32_t b00, b01, b10, b11;  // tokens 0-7: (b00, b01), tokens 8-15: (b10, b11)
+        ldsm_x4(kbase + (uint32_t)(((8 * (mi >> 1) + mr) * RS + 16 * ks + 8 * (mi & 1)) * 2), b00, b01, b10, b11);
+        mma_16816(sacc[0], qh0, 0u, qh1, 0u, b00, b01);
+        mma_16816(sacc[0], ql0, 0u, ql1, 0u, b00, b01);
+        mma_16816(sacc[1], qh0, 0u, qh1, 0u, b10, b11);
+        mma_16816(sacc[1], ql0, 0u, ql1, 0u, b10, b11);
+    }
+    // scores of head g: tokens 8 nb + 2 t + e of this page
+    const float scale = 1.0f / sqrtf(fmaxf((float)HD, 1.0f));
+    float sc[2][2];
+    float m = -INFINITY;
+#pragma unroll
+    for (int nb = 0; nb < 2; nb++)
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            const int jj = 8 * nb + 2 * t + e;
+            sc[nb][e] = (g < G && jj < nw) ? sacc[nb][e] * scale : -INFINITY;
+            m = fmaxf(m, sc[nb][e]);
+        }
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    if (t == 0 && g < G) red_m[warp][g] = m;
+    __syncthreads();
+    float mx = g < G ? fmaxf(fmaxf(red_m[0][g], red_m[1][g]), fmaxf(red_m[2][g], red_m[3][g])) : 0.f;
+    if (!isfinite(mx)) mx = 0.f;
+    float pv[2][2], l = 0.f;
+#pragma unroll
+    for (int nb = 0; nb < 2; nb++)
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            float v = 0.f;
+            if (g < G && 8 * nb + 2 * t + e < nw) {
+                v = expf(sc[nb][e] - mx);
+                if (!isfinite(v)) v = 0.f;
+            }
+            pv[nb][e] = v;
+            l += v;
+        }
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    if (t == 0 && g < G) red_l[warp][g] = l;
+    // O = P V: A = P (tokens 2t, 2t+1 | 2t+8, 2t+9 of head g), B = V rows through ldmatrix.trans
+    uint32_t ph0, pl0, ph1, pl1;
+    split_f16x2(pv[0][0], pv[0][1], ph0, pl0);
+    split_f16x2(pv[1][0], pv[1][1], ph1, pl1);
+    float oacc[HD / 8][4];
+#pragma unroll
+    for (int nd = 0; nd < HD / 8; nd++) oacc[nd][0] = oacc[nd][1] = oacc[nd][2] = oacc[nd][3] = 0.f;
+#pragma unroll
+    for (int j = 0; j < HD / 16; j++) {
+        uint32_t v00, v01, v10, v11;  // dims 16 j ..: (v00, v01), dims 16 j + 8 ..: (v10, v11)
+        ldsm_x4_t(vbase + (uint32_t)(((8 * (mi & 1) + mr) * RS + 16 * j + 8 * (mi >> 1)) * 2), v00, v01, v10, v11);
+        mma_16816(oacc[2 * j], ph0, 0u, ph1, 0u, v00, v01);
+        mma_16816(oacc[2 * j], pl0, 0u, pl1, 0u, v00, v01);
+        mma_16816(oacc[2 * j + 1], ph0, 0u, ph1, 0u, v10, v11);
+        mma_16816(oacc[2 * j + 1], pl0, 0u, pl1, 0u, v10, v11);
+    }
+    __syncthreads();  // every warp is done with the staged pages (acc_s reuses them) and red_l is complete
+    if (g < G)
+#pragma unroll
+        for (int nd = 0; nd < HD / 8; nd++) {
+            acc_s[warp][g][8 * nd + 2 * t] = oacc[nd][0];
+            acc_s[warp][g][8 * nd + 2 * t + 1] = oacc[nd][1];
+        }
+    __syncthreads();
+    float* out = apart + ((((size_t)b * nkv + h) * max_splits + split) * G) * (HD + 2);
+    for (int i = tid; i < G * HD; i += 128) {
+        const int gg = i / HD, d = i % HD;
+        out[(size_t)gg * (HD + 2) + 2 + d] = (acc_s[0][gg][d] + acc_s[1][gg][d]) + (acc_s[2][gg][d] + acc_s[3][gg][d]);
+    }
+    if (tid < G) {
+        float mt = fmaxf(fmaxf(red_m[0][tid], red_m[1][tid]), fmaxf(red_m[2][tid], red_m[3][tid]));
+        if (!isfinite(mt)) mt = 0.f;
+        out[(size_t)tid * (HD + 2)] = mt;
+        out[(size_t)tid * (HD + 2) + 1] = (red_l[0][tid] + red_l[1][tid]) + (red_l[2][tid] + red_l[3][tid]);
+    }
+}
+
 // Combines the splits of the attention output and prepares it as the o projection's input:
 // att = sum_s e^(m_s - M) acc_s / sum_s e^(m_s - M) l_s (the reference's 1 / sum_exp, 0 when the
 // sum is <= 1e-9). CTA (128-element block blk of the row, batch row b); thread d = element
@@ -533,7 +720,7 @@ static int decode_step(pox_model* m, int B, cudaStream_t st) {
         const dim3 ag(m->max_splits, m->nkv, B);
         cudaError_t e;
         if (m->hd == 128)
-            e = launch_pdl(attn_decode_kernel<128>, ag, dim3(128), 0, st, (const float*)m->qkv, m->qkv_rows,
+            e = launch_pdl(m->G >= 4 ? attn_decode_tc_kernel<128> : attn_decode_kernel<128>, ag, dim3(128), 0, st, (const float*)m->qkv, m->qkv_rows,
                            (const uint32_t*)m->pos, (const int32_t*)m->btab, (int)m->max_blocks_per_seq, m->kc, m->vc,
                            l, m->L, m->nq, m->nkv, m->G, m->max_splits, (const float2*)m->rope, m->apart);
         else if (m->hd == 64)

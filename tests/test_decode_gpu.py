@@ -32,6 +32,9 @@ CONFIGS = {
     # rank holds at tensor-parallel 8), scaled down
     "l70": {"hidden": 1024, "inter": 2048, "layers": 2, "n_heads": 8, "n_kv_heads": 1, "vocab": 1000,
             "rms_eps": 1e-5, "rope_theta": 500000.0},
+    # the Llama-3-8B head layout (head_dim 128, 4 query heads per kv head), scaled down
+    "l8": {"hidden": 512, "inter": 1024, "layers": 2, "n_heads": 4, "n_kv_heads": 1, "vocab": 1000,
+           "rms_eps": 1e-5, "rope_theta": 500000.0},
 }
 
 
@@ -45,10 +48,11 @@ def be():
 @pytest.mark.parametrize("name,outliers,nseq", [("hd128", None, 3), ("hd128", "automatic", 3), ("fixture", None, 3),
                                                 ("hd64", "aggressive", 3), ("hd128", "automatic", 11),
                                                 ("hd64", None, 10), ("l70", "automatic", 3), ("l70", "automatic", 17),
-                                                ("l70", None, 12)])
+                                                ("l70", None, 12), ("l8", "automatic", 3), ("l8", None, 9)])
 def test_decode_matches_forward_token(be, name, outliers, nseq):
-    """nseq 3: the batch <= 8 GEMV path; nseq 10-17: the small-M tensor-core paths (batch >= 9
-    while every sequence is active; f16 tiles with outliers, the integer kernel without)."""
+    """nseq 3: the batch <= 8 GEMV path; nseq 9-17: the small-M tensor-core paths (batch >= 9
+    while every sequence is active; f16 tiles with outliers, the integer kernel without). Head
+    layouts with 4-8 query heads of 128 per kv head (l8, l70) take the tensor-core attention."""
     cfg = CONFIGS[name]
     w = make_llama(cfg, seed=11, outlier_policy=outliers, norm_jitter=0.1)
     model = CudaModel(be, cfg, max_batch=nseq, kv_blocks=16 * nseq, max_blocks_per_seq=16)

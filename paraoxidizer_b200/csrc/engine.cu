@@ -6,9 +6,11 @@
 // Per layer: 4 GEMV launches on resident re-tiled weights (QKV and gate/up are concatenated at
 // load, so every projection row is computed exactly as in the separate tensors):
 //   qkv  = W_qkv  rmsnorm(x, attn_norm)            (norm fused into the GEMV's x preparation)
-//   att  = paged GQA attention over 0..=pos          (attn_decode_kernel: RoPE on q and k, k and v
-//          appended to the KV pages, split-context partials; attn_combine_kernel: the splits
-//          combined and written as the o projection's prepared input)
+//   att  = paged GQA attention over 0..=pos          (attn_decode_tc_kernel on the tensor cores for
+//          head_dim 128 with 4-8 query heads per kv head, attn_decode_kernel otherwise: RoPE on q
+//          and k from the model's (cos, sin) table, k and v appended to the KV pages,
+//          split-context partials; attn_combine_kernel: the splits combined and written as the o
+//          projection's prepared input)
 //   x   += W_o att                                   (residual fused into the GEMV epilogue)
 //   gu   = W_gu   rmsnorm(x, mlp_norm)
 //   x   += W_down silu(g) * u                        (SwiGLU fused into the x preparation)

@@ -261,7 +261,8 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const float* __restric
 // (the Llama-3 8B / 70B layouts); same grid, splits, RoPE, KV append and partial output. Each warp
 // stages its page of K and V (16 tokens) in shared memory and runs both products on mma.sync
 // m16n8k16 with f32 accumulation: S = Q K^T with the G query heads as the rows of A (padded to
-// 16) and q split into two f16 terms (hi = f16(q), lo = f16(q - hi), so q keeps 22 bits), then
+// 16) and q split into two f16 terms (hi = f16(q), lo = f16(q - hi): about 22 significant bits for
+// |q| >= 2^-4, an absolute error under 2^-24 below), then
 // O = P V with P likewise split. Fragments come from ldmatrix (V transposed); rows of a page past
 // the context are zero.
 __device__ __forceinline__ void ldsm_x4(uint32_t a, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {

@@ -2,9 +2,8 @@
  * pox_cuda.h -- C ABI of the B200 (sm_100a) CUDA backend for ParaOxidizer's decode hot path.
  *
  * Plain pointers and sizes only: no C++ or torch types cross this boundary, so the Rust side
- * binds it with an `extern "C"` block (the binding a maintainer adds is shown in
- * INTEGRATION.md). Every entry point cites the reference interface it replaces; paths are
- * relative to the reference repository root.
+ * binds it with an `extern "C"` block. Every entry point cites the reference interface it
+ * replaces; paths are relative to the reference repository root.
  *
  * Layout contract: all weight buffers are the unchanged `.pox` payloads
  * (crates/paraoxidizer-format/src/pox.rs:434-495): INT4 = packed nibbles (low nibble = even
@@ -120,9 +119,12 @@ typedef struct {
  * for 128-bit loads and tensor-core fragments; outlier table turned into a per-row CSR with
  * precomputed corrections). Replaces the per-call copies of metal_backend.rs:111-129 and the
  * per-call SparseOutlierTable::from_bytes of engine.rs:150-151. The host pointers are
- * remembered so that pox_cuda_gemv_int4* calls on the same slices reuse the resident copy:
- * the caller must not modify those host bytes while the tensor is alive (they are an
- * immutable mmap in the reference, pox.rs:171-175). */
+ * remembered so that pox_cuda_gemv_int4* / pox_cuda_gemv_int8 calls on the same slices reuse the
+ * resident copy. The match is by identity, not content: same addresses and lengths of the data,
+ * scale and outlier slices, same shape, dtype and group size. So the caller must not modify those
+ * host bytes, or free them and put another tensor at the same addresses, while the resident tensor
+ * is alive (free it first): the calls would keep using the old resident copy. In the reference
+ * these slices are an immutable mmap that outlives the engine (pox.rs:171-175). */
 int pox_cuda_tensor_upload(pox_cuda_ctx* ctx, const pox_tensor_desc* desc, pox_tensor** out);
 /* Frees a resident tensor (NULL is a no-op). */
 int pox_cuda_tensor_free(pox_cuda_ctx* ctx, pox_tensor* t);
@@ -154,8 +156,11 @@ int pox_cuda_tensor_gemv_host(pox_cuda_ctx* ctx, const pox_tensor* t, const floa
  * memory, shared by every call on a device and held until the process exits; the call allocates
  * and frees nothing. Limit: cols <= 32768 (larger -> POX_ERR_UNSUPPORTED). Calls whose kernels
  * overlap on the same device (other streams or contexts) race on the shared array: serialize
- * them. The first call on a device looks up the array's device address, so make that first call
- * before any stream capture. */
+ * them. The first call on a device looks up the array's device address (again after a context of
+ * that device is destroyed), so make that first call before any stream capture. The call returns
+ * before its kernels finish: a bounded wait that runs out inside them is returned as POX_ERR_TIMEOUT
+ * by the next call of this entry point on the context (which then launches nothing) or by
+ * pox_cuda_synchronize. */
 int pox_cuda_tensor_gemv_noalloc(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x_dev, size_t batch,
                                  float* y_dev, void* stream);
 /* Operation fused into a GEMV's input (the decode step's RMSNorm before q/k/v and gate/up,
@@ -232,13 +237,19 @@ int pox_cuda_model_decode(pox_model* m, uint32_t batch, const uint32_t* tokens, 
                           const int32_t* block_tables, float* logits, uint32_t* next_tokens);
 /* Device-pointer variant, asynchronous on `stream` (NULL: the context's stream). NULL inputs keep
  * the model's current device buffers (pox_cuda_model_buffers); advance != 0 then feeds the greedy
- * tokens back and increments the positions on the device, so consecutive calls decode greedily. */
+ * tokens back and increments the positions on the device, so consecutive calls decode greedily.
+ * The pages for every position a step reaches must be in the block tables already (reserve them
+ * before a run of steps): a position at or beyond 16 max_blocks_per_seq or a page entry outside
+ * [0, kv_blocks) is caught on the device, that part of the attention is left out, and the next
+ * pox_cuda_synchronize returns POX_ERR_INVALID. */
 int pox_cuda_model_decode_device(pox_model* m, uint32_t batch, const uint32_t* tokens_dev,
                                  const uint32_t* positions_dev, const int32_t* block_tables_dev, float* logits_dev,
                                  uint32_t* next_dev, int advance, void* stream);
 /* Loads a batch state into the model's device buffers without running a step (host arrays:
  * tokens [batch], positions [batch], block_tables [batch][max_blocks_per_seq]); a following
- * pox_cuda_model_decode_device with NULL inputs continues from it. Synchronous. */
+ * pox_cuda_model_decode_device with NULL inputs continues from it. Synchronous. Every page up to
+ * each row's position must be a block in [0, kv_blocks) (POX_ERR_INVALID otherwise; later pages may
+ * be -1 = not yet allocated, as BlockTable leaves them). */
 int pox_cuda_model_set_state(pox_model* m, uint32_t batch, const uint32_t* tokens, const uint32_t* positions,
                              const int32_t* block_tables);
 /* The model's device buffers (any out pointer may be NULL): tokens [max_batch], positions
@@ -246,6 +257,27 @@ int pox_cuda_model_set_state(pox_model* m, uint32_t batch, const uint32_t* token
  * tokens [max_batch]. */
 int pox_cuda_model_buffers(pox_model* m, uint32_t** tokens_dev, uint32_t** positions_dev, int32_t** block_tables_dev,
                            float** logits_dev, uint32_t** next_dev);
+
+/* Paged GQA decode attention over an fp16 KV cache that already holds every position attended: the
+ * attention of forward_token (crates/paraoxidizer-runtime/src/engine.rs:580-641) on the pages of
+ * crates/paraoxidizer-runtime/src/paged_cache.rs:149-162 (page = position / 16, slot = position % 16),
+ * exported for a kernel-level check. For batch row b and query head h (kv head h / (heads / kv_heads)):
+ *   out[b][h] = sum over t <= positions[b] of p_t v_t,  p = softmax_t(q[b][h] . k_t / sqrt(head_dim))
+ * with the reference's guards (non-finite max -> 0, non-finite terms -> 0, 1 / sum only when the sum
+ * is > 1e-9). Device memory: q_dev [batch][heads][head_dim] f32 (already rotated), k_pages_dev and
+ * v_pages_dev [num_blocks][kv_heads][16][head_dim] f16 bits (16-byte aligned), block_tables_dev
+ * [batch][max_blocks_per_seq] int32, positions_dev [batch] u32 (last position attended), out_dev
+ * [batch][heads][head_dim] f32. head_dim 32, 64 or 128 with at most 8 query heads per kv head (else
+ * POX_ERR_UNSUPPORTED). Asynchronous on `stream` (NULL: the context's stream). A position at or
+ * beyond 16 max_blocks_per_seq (that row's output is 0) or a page entry outside [0, num_blocks) (the
+ * page is left out) is caught on the device, and the next pox_cuda_synchronize returns
+ * POX_ERR_INVALID. The first call, and one with larger sizes, allocates the split partials: make it
+ * before any stream capture. The decode step runs the same kernels with RoPE and the KV append fused. */
+int pox_cuda_paged_attention(pox_cuda_ctx* ctx, const float* q_dev, const uint16_t* k_pages_dev,
+                             const uint16_t* v_pages_dev, const int32_t* block_tables_dev,
+                             const uint32_t* positions_dev, uint32_t batch, uint32_t heads, uint32_t kv_heads,
+                             uint32_t head_dim, uint32_t num_blocks, uint32_t max_blocks_per_seq, float* out_dev,
+                             void* stream);
 
 /* ---- tensor-parallel decode across the GPUs of one node (one process and context per GPU) ----
  * The reference decodes on one device; the shard layout is the standard Megatron split, chosen so

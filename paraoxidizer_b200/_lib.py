@@ -114,6 +114,7 @@ def _declare(L):
         "pox_cuda_model_set_state": (i32, [vp, u32, vp, vp, vp]),
         "pox_cuda_model_buffers": (i32, [vp, C.POINTER(vp), C.POINTER(vp), C.POINTER(vp), C.POINTER(vp),
                                          C.POINTER(vp)]),
+        "pox_cuda_paged_attention": (i32, [vp, vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, vp, vp]),
         "pox_cuda_tensor_dequant": (i32, [vp, vp, vp, vp]),
         "pox_cuda_tensor_dequant_host": (i32, [vp, vp, vp]),
     }

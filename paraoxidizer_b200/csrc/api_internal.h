@@ -5,6 +5,7 @@
 #include <stdint.h>
 
 #include <mutex>
+#include <unordered_map>
 #include <vector>
 
 #include "../../include/pox_cuda.h"
@@ -41,6 +42,16 @@ struct pox_cuda_ctx {
     cudaStream_t stream = nullptr;
     std::mutex mu;
     std::vector<pox_tensor*> tensors;
+    // resident tensors by the host address of their weight payload (the key of the host-slice calls)
+    std::unordered_multimap<const void*, pox_tensor*> by_host;
+    // host-slice calls on tiled tensors: pinned, device-mapped staging for x and y (the x preparation
+    // reads x over PCIe and the GEMV writes y there: no DMA copies)
+    float* pin_x = nullptr;
+    float* pin_x_dev = nullptr;
+    size_t pin_x_bytes = 0;
+    float* pin_y = nullptr;
+    float* pin_y_dev = nullptr;
+    size_t pin_y_bytes = 0;
     void* scratch_x = nullptr;
     size_t scratch_x_bytes = 0;
     void* scratch_y = nullptr;
@@ -49,7 +60,9 @@ struct pox_cuda_ctx {
     size_t tc_scratch_bytes = 0;
     int* tc_tickets = nullptr;   // small-M path: per row block split counters (zeroed, self-resetting)
     size_t tc_tickets_n = 0;
-    int* err_host = nullptr;  // kernel error flag (host-mapped); nonzero = a bounded wait expired
+    void* attn_scratch = nullptr;  // kernel-level paged attention: split partials
+    size_t attn_scratch_bytes = 0;
+    int* err_host = nullptr;  // kernel error flag (host-mapped); nonzero = a bounded wait expired or bad input
     int* err_dev = nullptr;
     std::vector<pox_model*> models;  // decode models created on this context (destroyed with it)
 };
@@ -84,6 +97,9 @@ void destroy_ctx_extras(pox_cuda_ctx* ctx);
 // Small-M path scratch for a tensor of rows x cols at `batch` rows of x (grown outside stream
 // capture only; a captured graph keeps the buffers it was captured with).
 int ensure_tc_scratch(pox_cuda_ctx* ctx, size_t rows, size_t cols, size_t batch, cudaStream_t st);
-// After a synchronize: turns a raised kernel error flag into POX_ERR_TIMEOUT (and clears it).
+// After a synchronize: turns a raised kernel error flag into POX_ERR_TIMEOUT, or POX_ERR_INVALID for
+// input rejected on the device (and clears it).
 int take_kernel_error(pox_cuda_ctx* ctx);
+// Drops the cached device address of the no-allocation GEMV's scratch array for `device`.
+void noalloc_forget_device(int device);
 }  // namespace pox

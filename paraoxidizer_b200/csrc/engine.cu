@@ -85,6 +85,47 @@ __device__ __forceinline__ float2 rope_pair(float a0, float a1, float c, float s
     return make_float2(__fsub_rn(__fmul_rn(a0, c), __fmul_rn(a1, s)), __fadd_rn(__fmul_rn(a0, s), __fmul_rn(a1, c)));
 }
 
+// q of the CTA's G query heads into shared memory (qs [8][HD]), rotated by RoPE (engine.rs:353-408)
+// from the model's (cos, sin) table when FUSED; with FUSED the CTA whose split holds position p also
+// rotates k and appends k and v to the page btab_row[p / 16], slot p % 16 (an entry outside
+// [0, kv_blocks) is reported and nothing is written). Without FUSED, q is taken as given and the
+// pages already hold every position attended (the kernel-level entry point).
+template <int HD, bool FUSED>
+__device__ __forceinline__ void load_q_append_kv(const float* row, uint32_t p, const int32_t* btab_row, int kv_blocks,
+                                                 __half* kc, __half* vc, int layer, int L, int nq, int nkv, int h,
+                                                 int G, const float2* rope, int t0, float* qs, int* err) {
+    constexpr int DH = HD / 2;
+    const int tid = threadIdx.x;
+    const float2* rp = FUSED ? rope + (size_t)p * DH : nullptr;  // (cos, sin) of the pairs at position p
+    for (int j = tid; j < G * DH; j += blockDim.x) {
+        const int g = j / DH, i = j % DH;
+        const float* q = row + (size_t)(h * G + g) * HD;
+        float2 r = make_float2(q[2 * i], q[2 * i + 1]);
+        if (FUSED) {
+            const float2 cs = rp[i];
+            r = rope_pair(r.x, r.y, cs.x, cs.y);
+        }
+        qs[g * HD + 2 * i] = r.x;
+        qs[g * HD + 2 * i + 1] = r.y;
+    }
+    if (FUSED && (int)p < t0 + kSplitTok) {  // this split holds the new position: append k, v
+        const int blk = btab_row[p / kPage];
+        if (blk < 0 || blk >= kv_blocks) {
+            if (h == 0 && tid == 0) atomicOr(err, kErrAttnPage);
+            return;
+        }
+        const size_t off = ((((size_t)blk * L + layer) * nkv + h) * kPage + p % kPage) * HD;
+        const float* k = row + (size_t)(nq + h) * HD;
+        const float* v = row + (size_t)(nq + nkv + h) * HD;
+        for (int i = tid; i < DH; i += blockDim.x) {
+            const float2 cs = rp[i];
+            const float2 r = rope_pair(k[2 * i], k[2 * i + 1], cs.x, cs.y);
+            *reinterpret_cast<__half2*>(kc + off + 2 * i) = __floats2half2_rn(r.x, r.y);
+            *reinterpret_cast<__half2*>(vc + off + 2 * i) = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+        }
+    }
+}
+
 // ---- paged GQA decode attention (engine.rs:580-641), split over the context, RoPE and the KV
 // append fused in ----
 // CTA (split, kv head, batch row) takes tokens [64 split, min(ctx, 64 split + 64)) for the G query
@@ -93,20 +134,24 @@ __device__ __forceinline__ float2 rope_pair(float a0, float a1, float c, float s
 // takes the 16 tokens of one page: two lanes per token read its K row (one half each) and the
 // warp reads the 16 V rows, all issued before any use; scores, the split's softmax partial and
 // sum_t p_t v_t follow. Writes (max, sum, acc[hd]) per query head for the combine kernel.
-template <int HD>
+template <int HD, bool FUSED>
 __global__ void __launch_bounds__(128) attn_decode_kernel(const float* __restrict__ qkv, int qkv_rows,
                                                           const uint32_t* __restrict__ pos,
-                                                          const int32_t* __restrict__ btab, int mbps,
+                                                          const int32_t* __restrict__ btab, int mbps, int kv_blocks,
                                                           __half* __restrict__ kc, __half* __restrict__ vc, int layer,
                                                           int L, int nq, int nkv, int G, int max_splits,
-                                                          const float2* __restrict__ rope, float* __restrict__ apart) {
+                                                          const float2* __restrict__ rope, float* __restrict__ apart,
+                                                          int* __restrict__ err) {
     constexpr int DH = HD / 2;   // K dims per lane (two lanes per token)
     constexpr int DPL = HD / 32; // V dims per lane
     pdl_launch_dependents();
     pdl_wait();
     const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const uint32_t p = pos[b];
-    if (p >= (uint32_t)mbps * kPage) return;  // beyond the block table (invalid input): no out-of-range access
+    if (p >= (uint32_t)mbps * kPage) {  // beyond the block table (invalid input): reported, nothing read
+        if (split == 0 && h == 0 && threadIdx.x == 0) atomicOr(err, kErrAttnPos);
+        return;
+    }
     const int ctx = (int)p + 1;
     const int t0 = split * kSplitTok;
     if (t0 >= ctx) return;  // the combine kernel reads only ceil(ctx / 64) splits
@@ -117,36 +162,21 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const float* __restric
     __shared__ float red_m[4][8], red_l[4][8];
     __shared__ float acc_s[4][8][HD];
     const float* row = qkv + (size_t)b * qkv_rows;
-    const float2* rp = rope + (size_t)p * DH;  // (cos, sin) of the pairs at position p
-    for (int j = tid; j < G * DH; j += 128) {
-        const int g = j / DH, i = j % DH;
-        const float2 cs = rp[i];
-        const float* q = row + (size_t)(h * G + g) * HD;
-        const float2 r = rope_pair(q[2 * i], q[2 * i + 1], cs.x, cs.y);
-        qs[g][2 * i] = r.x;
-        qs[g][2 * i + 1] = r.y;
-    }
-    if ((int)p < t0 + kSplitTok) {  // this split holds the new position: append k, v
-        const int blk = btab[(size_t)b * mbps + p / kPage];
-        const size_t off = ((((size_t)blk * L + layer) * nkv + h) * kPage + p % kPage) * HD;
-        const float* k = row + (size_t)(nq + h) * HD;
-        const float* v = row + (size_t)(nq + nkv + h) * HD;
-        for (int i = tid; i < DH; i += 128) {
-            const float2 cs = rp[i];
-            const float2 r = rope_pair(k[2 * i], k[2 * i + 1], cs.x, cs.y);
-            *reinterpret_cast<__half2*>(kc + off + 2 * i) = __floats2half2_rn(r.x, r.y);
-            *reinterpret_cast<__half2*>(vc + off + 2 * i) = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
-        }
-    }
+    load_q_append_kv<HD, FUSED>(row, p, btab + (size_t)b * mbps, kv_blocks, kc, vc, layer, L, nq, nkv, h, G,
+                                rope, t0, &qs[0][0], err);
     __syncthreads();
 
     // this warp's page: tokens t0 + 16 warp .. + 15 (t0 is a multiple of 64, pages hold 16)
     const int jt = 16 * warp + (lane & 15), hh = lane >> 4;
-    const int nw = max(0, min(16, nt - 16 * warp));  // valid tokens of this warp
+    int nw = max(0, min(16, nt - 16 * warp));  // valid tokens of this warp
     uint4 kr[DH / 8];
     uint2 vr[16];
+    const int blk = nw > 0 ? btab[(size_t)b * mbps + (t0 + 16 * warp) / kPage] : 0;
+    if (nw > 0 && (blk < 0 || blk >= kv_blocks)) {  // invalid page: reported, its tokens left out
+        if (lane == 0) atomicOr(err, kErrAttnPage);
+        nw = 0;
+    }
     if (nw > 0) {
-        const int blk = btab[(size_t)b * mbps + (t0 + 16 * warp) / kPage];
         const size_t page = (((size_t)blk * L + layer) * nkv + h) * kPage * HD;
         if ((lane & 15) < nw) {
             const __half* kp = kc + page + (size_t)(lane & 15) * HD + hh * DH;
@@ -284,22 +314,25 @@ __device__ __forceinline__ void split_f16x2(float x0, float x1, uint32_t& hi, ui
     lo = *reinterpret_cast<const uint32_t*>(&l);
 }
 
-template <int HD>
+template <int HD, bool FUSED>
 __global__ void __launch_bounds__(128) attn_decode_tc_kernel(const float* __restrict__ qkv, int qkv_rows,
                                                              const uint32_t* __restrict__ pos,
                                                              const int32_t* __restrict__ btab, int mbps,
-                                                             __half* __restrict__ kc, __half* __restrict__ vc,
-                                                             int layer, int L, int nq, int nkv, int G,
-                                                             int max_splits, const float2* __restrict__ rope,
-                                                             float* __restrict__ apart) {
+                                                             int kv_blocks, __half* __restrict__ kc,
+                                                             __half* __restrict__ vc, int layer, int L, int nq,
+                                                             int nkv, int G, int max_splits,
+                                                             const float2* __restrict__ rope,
+                                                             float* __restrict__ apart, int* __restrict__ err) {
     static_assert(HD == 128, "head_dim 128");
-    constexpr int DH = HD / 2;
     constexpr int RS = HD + 8;  // staged row stride in halves (272 B: ldmatrix rows in distinct banks)
     pdl_launch_dependents();
     pdl_wait();
     const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const uint32_t p = pos[b];
-    if (p >= (uint32_t)mbps * kPage) return;  // beyond the block table (invalid input): no out-of-range access
+    if (p >= (uint32_t)mbps * kPage) {  // beyond the block table (invalid input): reported, nothing read
+        if (split == 0 && h == 0 && threadIdx.x == 0) atomicOr(err, kErrAttnPos);
+        return;
+    }
     const int ctx = (int)p + 1;
     const int t0 = split * kSplitTok;
     if (t0 >= ctx) return;  // the combine kernel reads only ceil(ctx / 64) splits
@@ -310,36 +343,22 @@ __global__ void __launch_bounds__(128) attn_decode_tc_kernel(const float* __rest
     __shared__ __align__(16) __half kv_s[2][4][16][RS];  // [K, V][warp][token][dim]; then the warps' outputs
     float (*acc_s)[8][HD] = reinterpret_cast<float (*)[8][HD]>(&kv_s[0][0][0][0]);
     const float* row = qkv + (size_t)b * qkv_rows;
-    const float2* rp = rope + (size_t)p * DH;  // (cos, sin) of the pairs at position p
-    for (int j = tid; j < G * DH; j += 128) {
-        const int g = j / DH, i = j % DH;
-        const float2 cs = rp[i];
-        const float* q = row + (size_t)(h * G + g) * HD;
-        const float2 r = rope_pair(q[2 * i], q[2 * i + 1], cs.x, cs.y);
-        qs[g][2 * i] = r.x;
-        qs[g][2 * i + 1] = r.y;
-    }
-    if ((int)p < t0 + kSplitTok) {  // this split holds the new position: append k, v
-        const int blk = btab[(size_t)b * mbps + p / kPage];
-        const size_t off = ((((size_t)blk * L + layer) * nkv + h) * kPage + p % kPage) * HD;
-        const float* k = row + (size_t)(nq + h) * HD;
-        const float* v = row + (size_t)(nq + nkv + h) * HD;
-        for (int i = tid; i < DH; i += 128) {
-            const float2 cs = rp[i];
-            const float2 r = rope_pair(k[2 * i], k[2 * i + 1], cs.x, cs.y);
-            *reinterpret_cast<__half2*>(kc + off + 2 * i) = __floats2half2_rn(r.x, r.y);
-            *reinterpret_cast<__half2*>(vc + off + 2 * i) = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
-        }
-    }
+    load_q_append_kv<HD, FUSED>(row, p, btab + (size_t)b * mbps, kv_blocks, kc, vc, layer, L, nq, nkv, h, G,
+                                rope, t0, &qs[0][0], err);
     __syncthreads();
 
     // this warp's page (tokens t0 + 16 warp ..) staged in shared memory, rows past the context zero
-    const int nw = max(0, min(16, nt - 16 * warp));
+    int nw = max(0, min(16, nt - 16 * warp));
     {
         size_t page = 0;
         if (nw > 0) {
             const int blk = btab[(size_t)b * mbps + (t0 + 16 * warp) / kPage];
-            page = (((size_t)blk * L + layer) * nkv + h) * kPage * HD;
+            if (blk < 0 || blk >= kv_blocks) {  // invalid page: reported, its tokens left out (rows zero)
+                if (lane == 0) atomicOr(err, kErrAttnPage);
+                nw = 0;
+            } else {
+                page = (((size_t)blk * L + layer) * nkv + h) * kPage * HD;
+            }
         }
 #pragma unroll
         for (int u = 0; u < 16 * (HD / 8) / 32; u++) {
@@ -465,15 +484,18 @@ struct OPrep {
     float2* xm = nullptr;
     int Bp = 0;
 };
-__global__ void __launch_bounds__(128) attn_combine_kernel(const uint32_t* __restrict__ pos, int nq, int nkv, int G,
-                                                           int hd, int max_splits, const float* __restrict__ apart,
-                                                           float* __restrict__ att, OPrep op) {
+__global__ void __launch_bounds__(128) attn_combine_kernel(const uint32_t* __restrict__ pos, uint32_t max_pos, int nq,
+                                                           int nkv, int G, int hd, int max_splits,
+                                                           const float* __restrict__ apart, float* __restrict__ att,
+                                                           OPrep op) {
     pdl_launch_dependents();
     pdl_wait();
     const int blk = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
     const int e = blk * 128 + d, hq = e / hd, dd = e % hd;
     if (e >= nq * hd) return;  // only when nq hd % 128 != 0, where nothing is prepared (no barrier below)
-    const int ns = min(max_splits, (int)((pos[b] + (uint32_t)kSplitTok) / kSplitTok));  // ceil((pos + 1) / 64)
+    // ceil((pos + 1) / 64) splits; none (output 0) for a position beyond the block table, which the
+    // attention kernel reported and skipped
+    const int ns = pos[b] >= max_pos ? 0 : min(max_splits, (int)((pos[b] + (uint32_t)kSplitTok) / kSplitTok));
     const int h = hq / G, g = hq % G;
     const float* base = apart + (((size_t)b * nkv + h) * max_splits * G + g) * (hd + 2);
     const size_t sstride = (size_t)G * (hd + 2);
@@ -606,6 +628,40 @@ __global__ void advance_kernel(uint32_t* tok, uint32_t* pos, const uint32_t* nex
     }
 }
 
+// Launch of the split-context attention kernels (decode step: FUSED = RoPE + KV append; the
+// kernel-level entry point: q as given over pages already filled). Tensor cores for head_dim 128
+// with 4..8 query heads per kv head, the FMA kernel otherwise.
+struct AttnLaunch {
+    const float* qkv = nullptr;
+    int qkv_rows = 0;
+    const uint32_t* pos = nullptr;
+    const int32_t* btab = nullptr;
+    int mbps = 0, kv_blocks = 0;
+    __half* kc = nullptr;
+    __half* vc = nullptr;
+    int layer = 0, L = 1, nq = 0, nkv = 0, hd = 0, G = 0, max_splits = 0;
+    const float2* rope = nullptr;
+    float* apart = nullptr;
+    int* err = nullptr;
+};
+template <bool FUSED>
+static cudaError_t launch_attention_t(const AttnLaunch& a, int B, cudaStream_t st) {
+    const dim3 grid(a.max_splits, a.nkv, B), block(128);
+    if (a.hd == 128)
+        return launch_pdl(a.G >= 4 ? attn_decode_tc_kernel<128, FUSED> : attn_decode_kernel<128, FUSED>, grid, block,
+                          0, st, a.qkv, a.qkv_rows, a.pos, a.btab, a.mbps, a.kv_blocks, a.kc, a.vc, a.layer, a.L, a.nq,
+                          a.nkv, a.G, a.max_splits, a.rope, a.apart, a.err);
+    if (a.hd == 64)
+        return launch_pdl(attn_decode_kernel<64, FUSED>, grid, block, 0, st, a.qkv, a.qkv_rows, a.pos, a.btab, a.mbps,
+                          a.kv_blocks, a.kc, a.vc, a.layer, a.L, a.nq, a.nkv, a.G, a.max_splits, a.rope, a.apart,
+                          a.err);
+    return launch_pdl(attn_decode_kernel<32, FUSED>, grid, block, 0, st, a.qkv, a.qkv_rows, a.pos, a.btab, a.mbps,
+                      a.kv_blocks, a.kc, a.vc, a.layer, a.L, a.nq, a.nkv, a.G, a.max_splits, a.rope, a.apart, a.err);
+}
+static cudaError_t launch_attention(const AttnLaunch& a, int B, bool fused, cudaStream_t st) {
+    return fused ? launch_attention_t<true>(a, B, st) : launch_attention_t<false>(a, B, st);
+}
+
 static void destroy_model(pox_model* m);
 
 // Destroys the models still registered on a context that is being destroyed.
@@ -720,20 +776,26 @@ static int decode_step(pox_model* m, int B, cudaStream_t st) {
         if (!w.qkv) return set_error(POX_ERR_INVALID, "layer %d has no weights", l);
         norm.norm_w = w.attn_norm;
         if ((rc = gemv_launch(ctx, w.qkv, m->x, B, m->qkv, st, &norm))) return rc;
-        const dim3 ag(m->max_splits, m->nkv, B);
-        cudaError_t e;
-        if (m->hd == 128)
-            e = launch_pdl(m->G >= 4 ? attn_decode_tc_kernel<128> : attn_decode_kernel<128>, ag, dim3(128), 0, st, (const float*)m->qkv, m->qkv_rows,
-                           (const uint32_t*)m->pos, (const int32_t*)m->btab, (int)m->max_blocks_per_seq, m->kc, m->vc,
-                           l, m->L, m->nq, m->nkv, m->G, m->max_splits, (const float2*)m->rope, m->apart);
-        else if (m->hd == 64)
-            e = launch_pdl(attn_decode_kernel<64>, ag, dim3(128), 0, st, (const float*)m->qkv, m->qkv_rows,
-                           (const uint32_t*)m->pos, (const int32_t*)m->btab, (int)m->max_blocks_per_seq, m->kc, m->vc,
-                           l, m->L, m->nq, m->nkv, m->G, m->max_splits, (const float2*)m->rope, m->apart);
-        else
-            e = launch_pdl(attn_decode_kernel<32>, ag, dim3(128), 0, st, (const float*)m->qkv, m->qkv_rows,
-                           (const uint32_t*)m->pos, (const int32_t*)m->btab, (int)m->max_blocks_per_seq, m->kc, m->vc,
-                           l, m->L, m->nq, m->nkv, m->G, m->max_splits, (const float2*)m->rope, m->apart);
+        AttnLaunch al;
+        al.qkv = m->qkv;
+        al.qkv_rows = m->qkv_rows;
+        al.pos = m->pos;
+        al.btab = m->btab;
+        al.mbps = (int)m->max_blocks_per_seq;
+        al.kv_blocks = (int)m->kv_blocks;
+        al.kc = m->kc;
+        al.vc = m->vc;
+        al.layer = l;
+        al.L = m->L;
+        al.nq = m->nq;
+        al.nkv = m->nkv;
+        al.hd = m->hd;
+        al.G = m->G;
+        al.max_splits = m->max_splits;
+        al.rope = m->rope;
+        al.apart = m->apart;
+        al.err = ctx->err_dev;
+        cudaError_t e = launch_attention(al, B, true, st);
         if (e != cudaSuccess) return cuda_error(e, "attention launch");
         // the combine writes the o projection's prepared input when that tensor takes one
         OPrep op;
@@ -753,8 +815,8 @@ static int decode_step(pox_model* m, int B, cudaStream_t st) {
             op.Bp = xt.Bp;
         }
         e = launch_pdl(attn_combine_kernel, dim3((m->nq * m->hd + 127) / 128, B), dim3(128), 0, st,
-                       (const uint32_t*)m->pos, m->nq, m->nkv, m->G, m->hd, m->max_splits, (const float*)m->apart,
-                       m->att, op);
+                       (const uint32_t*)m->pos, (uint32_t)(m->max_blocks_per_seq * kPage), m->nq, m->nkv, m->G, m->hd,
+                       m->max_splits, (const float*)m->apart, m->att, op);
         if (e != cudaSuccess) return cuda_error(e, "attention combine launch");
         if ((rc = row_split_gemv(m, w.o, m->att, B, 2 * l, nullptr, st, fuse))) return rc;
         norm.norm_w = w.mlp_norm;
@@ -1090,6 +1152,15 @@ extern "C" int pox_cuda_model_set_state(pox_model* m, uint32_t batch, const uint
     for (uint32_t b = 0; b < batch * m->max_blocks_per_seq; b++)
         if (block_tables[b] >= (int32_t)m->kv_blocks)
             return set_error(POX_ERR_INVALID, "block table entry %d out of range", block_tables[b]);
+    for (uint32_t b = 0; b < batch; b++) {  // the pages up to each row's next position must exist
+        const uint32_t nb = positions[b] / kPage + 1;
+        if (nb > m->max_blocks_per_seq)
+            return set_error(POX_ERR_OOM, "position %u needs %u KV blocks, max_blocks_per_seq is %u", positions[b], nb,
+                             m->max_blocks_per_seq);
+        for (uint32_t j = 0; j < nb; j++)
+            if (block_tables[(size_t)b * m->max_blocks_per_seq + j] < 0)
+                return set_error(POX_ERR_INVALID, "row %u: page %u (position %u) has no block", b, j, positions[b]);
+    }
     pox_cuda_ctx* ctx = m->ctx;
     std::lock_guard<std::mutex> lk(ctx->mu);
     cudaError_t e = cudaSetDevice(ctx->device);
@@ -1162,5 +1233,75 @@ extern "C" int pox_cuda_model_comm_mode(pox_model* m, int mode) {
     if (mode == POX_COMM_PEER && !m->comm.peer_ready) return set_error(POX_ERR_INVALID, "peer buffers not opened");
     if (mode != POX_COMM_NCCL && mode != POX_COMM_PEER) return set_error(POX_ERR_INVALID, "unknown mode %d", mode);
     m->comm.mode = mode;
+    return POX_OK;
+}
+
+extern "C" int pox_cuda_paged_attention(pox_cuda_ctx* ctx, const float* q_dev, const uint16_t* k_pages_dev,
+                                        const uint16_t* v_pages_dev, const int32_t* block_tables_dev,
+                                        const uint32_t* positions_dev, uint32_t batch, uint32_t heads,
+                                        uint32_t kv_heads, uint32_t head_dim, uint32_t num_blocks,
+                                        uint32_t max_blocks_per_seq, float* out_dev, void* stream) {
+    if (!ctx) return set_error(POX_ERR_INVALID, "ctx is NULL");
+    if (batch == 0) return POX_OK;
+    if (!q_dev || !k_pages_dev || !v_pages_dev || !block_tables_dev || !positions_dev || !out_dev)
+        return set_error(POX_ERR_INVALID, "NULL device pointer");
+    if (!heads || !kv_heads || !num_blocks || !max_blocks_per_seq)
+        return set_error(POX_ERR_INVALID, "zero heads, kv_heads, num_blocks or max_blocks_per_seq");
+    if (heads % kv_heads || heads / kv_heads > 8 || (head_dim != 32 && head_dim != 64 && head_dim != 128))
+        return set_error(POX_ERR_UNSUPPORTED, "%u heads over %u kv heads of dim %u (supported: head_dim 32/64/128, "
+                         "at most 8 query heads per kv head)", heads, kv_heads, head_dim);
+    if ((((uintptr_t)k_pages_dev | (uintptr_t)v_pages_dev) & 15) || ((uintptr_t)q_dev & 7) || ((uintptr_t)out_dev & 3))
+        return set_error(POX_ERR_INVALID, "K/V pages must be 16-byte aligned, q 8-byte aligned");
+    if (batch > 65535 || max_blocks_per_seq > (1u << 20))
+        return set_error(POX_ERR_UNSUPPORTED, "batch %u / max_blocks_per_seq %u too large", batch, max_blocks_per_seq);
+    const int G = (int)(heads / kv_heads);
+    const int max_splits = (int)((max_blocks_per_seq * kPage + kSplitTok - 1) / kSplitTok);
+    const size_t need = (size_t)batch * kv_heads * max_splits * G * (head_dim + 2) * sizeof(float);
+    cudaError_t e = cudaSetDevice(ctx->device);
+    if (e != cudaSuccess) return cuda_error(e, "cudaSetDevice");
+    cudaStream_t st = stream ? (cudaStream_t)stream : ctx->stream;
+    float* apart = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(ctx->mu);
+        if (need > ctx->attn_scratch_bytes) {
+            cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+            if (cudaStreamIsCapturing(st, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone)
+                return set_error(POX_ERR_INVALID, "attention scratch must be sized by a call before stream capture");
+            e = cudaDeviceSynchronize();  // the old scratch may still be in use by earlier calls
+            if (e == cudaSuccess) {
+                cudaFree(ctx->attn_scratch);
+                ctx->attn_scratch = nullptr;
+                ctx->attn_scratch_bytes = 0;
+                e = cudaMalloc(&ctx->attn_scratch, need);
+            }
+            if (e != cudaSuccess) return cuda_error(e, "cudaMalloc(attention partials)");
+            ctx->attn_scratch_bytes = need;
+        }
+        apart = static_cast<float*>(ctx->attn_scratch);
+    }
+    AttnLaunch al;
+    al.qkv = q_dev;
+    al.qkv_rows = (int)(heads * head_dim);
+    al.pos = positions_dev;
+    al.btab = block_tables_dev;
+    al.mbps = (int)max_blocks_per_seq;
+    al.kv_blocks = (int)num_blocks;
+    al.kc = reinterpret_cast<__half*>(const_cast<uint16_t*>(k_pages_dev));  // read only without FUSED
+    al.vc = reinterpret_cast<__half*>(const_cast<uint16_t*>(v_pages_dev));
+    al.layer = 0;
+    al.L = 1;
+    al.nq = (int)heads;
+    al.nkv = (int)kv_heads;
+    al.hd = (int)head_dim;
+    al.G = G;
+    al.max_splits = max_splits;
+    al.apart = apart;
+    al.err = ctx->err_dev;
+    e = launch_attention(al, (int)batch, false, st);
+    if (e != cudaSuccess) return cuda_error(e, "attention launch");
+    e = launch_pdl(attn_combine_kernel, dim3((heads * head_dim + 127) / 128, batch), dim3(128), 0, st, positions_dev,
+                   (uint32_t)(max_blocks_per_seq * kPage), (int)heads, (int)kv_heads, G, (int)head_dim, max_splits,
+                   (const float*)apart, out_dev, OPrep());
+    if (e != cudaSuccess) return cuda_error(e, "attention combine launch");
     return POX_OK;
 }

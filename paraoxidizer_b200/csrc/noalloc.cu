@@ -31,7 +31,9 @@ constexpr size_t kNoAllocScratchBytes = (size_t)1 << 20 | (size_t)16 << 10;  // 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 // Device address of g_noalloc_scratch per device, looked up once (the symbol's host-side name is
-// only a stand-in; a kernel must be given the address cudaGetSymbolAddress returns).
+// only a stand-in; a kernel must be given the address cudaGetSymbolAddress returns). Destroying a
+// context of a device forgets that device's address, so a context created after a device reset looks
+// it up again instead of using a stale one.
 std::mutex g_mu;
 void* g_addr[64] = {};
 
@@ -50,6 +52,12 @@ int scratch_address(int device, void** out) {
 
 }  // namespace
 
+void pox::noalloc_forget_device(int device) {
+    if (device < 0 || device >= 64) return;
+    std::lock_guard<std::mutex> lk(g_mu);
+    g_addr[device] = nullptr;
+}
+
 extern "C" int pox_cuda_tensor_gemv_noalloc(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x_dev,
                                             size_t batch, float* y_dev, void* stream) {
     using namespace pox;
@@ -57,6 +65,10 @@ extern "C" int pox_cuda_tensor_gemv_noalloc(pox_cuda_ctx* ctx, const pox_tensor*
     if (batch && (!x_dev || !y_dev)) return set_error(POX_ERR_INVALID, "x/y is NULL");
     const cudaError_t se = cudaSetDevice(ctx->device);
     if (se != cudaSuccess) return cuda_error(se, "cudaSetDevice");
+    // The call returns before its kernels finish, so a bounded wait that ran out in an earlier call's
+    // kernels (this entry point's or another on the context) is reported here, before new work.
+    const int prev = take_kernel_error(ctx);
+    if (prev) return prev;
     if (t->rows == 0 || t->cols == 0 || batch == 0) return POX_OK;
     if (((uintptr_t)x_dev & 15) != 0) return set_error(POX_ERR_INVALID, "x must be 16-byte aligned");
     cudaStream_t st = stream ? (cudaStream_t)stream : ctx->stream;

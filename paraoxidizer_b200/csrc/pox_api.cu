@@ -131,13 +131,18 @@ extern "C" void pox_cuda_destroy(pox_cuda_ctx* ctx) {
             delete t;
         }
         ctx->tensors.clear();
+        ctx->by_host.clear();
+        cudaFreeHost(ctx->pin_x);
+        cudaFreeHost(ctx->pin_y);
         cudaFree(ctx->scratch_x);
         cudaFree(ctx->scratch_y);
         cudaFree(ctx->tc_scratch);
         cudaFree(ctx->tc_tickets);
+        cudaFree(ctx->attn_scratch);
         cudaFreeHost(ctx->err_host);
         cudaStreamDestroy(ctx->stream);
     }
+    pox::noalloc_forget_device(ctx->device);
     delete ctx;
 }
 
@@ -145,6 +150,10 @@ int pox::take_kernel_error(pox_cuda_ctx* ctx) {
     const int f = *(volatile int*)ctx->err_host;
     if (f == 0) return POX_OK;
     *(volatile int*)ctx->err_host = 0;
+    if ((f & ~kErrInputMask) == 0)
+        return set_error(POX_ERR_INVALID, "attention input rejected on the device (flag 0x%x:%s%s); results of that call "
+                         "are invalid", f, (f & kErrAttnPos) ? " a position beyond its block table" : "",
+                         (f & kErrAttnPage) ? " a block-table entry outside [0, kv_blocks)" : "");
     return set_error(POX_ERR_TIMEOUT, "a kernel's bounded wait expired (flag 0x%x); results of that call are invalid", f);
 }
 
@@ -308,7 +317,10 @@ int pox::upload_tensor_locked(pox_cuda_ctx* ctx, const pox_tensor_desc* d, pox_t
     t->h_outliers = d->outliers;
     t->h_outlier_len = d->outlier_len;
     if (d->rows == 0 || d->cols == 0) {
-        if (keep) ctx->tensors.push_back(t);
+        if (keep) {
+            ctx->tensors.push_back(t);
+            ctx->by_host.emplace(t->h_data, t);
+        }
         *out = t;
         return POX_OK;
     }
@@ -435,7 +447,10 @@ int pox::upload_tensor_locked(pox_cuda_ctx* ctx, const pox_tensor_desc* d, pox_t
     cudaFree(tmp);
     cudaFree(tmp_s);
 #undef CKF
-    if (keep) ctx->tensors.push_back(t);
+    if (keep) {
+        ctx->tensors.push_back(t);
+        ctx->by_host.emplace(t->h_data, t);
+    }
     *out = t;
     return POX_OK;
 }
@@ -457,6 +472,11 @@ extern "C" int pox_cuda_tensor_free(pox_cuda_ctx* ctx, pox_tensor* t) {
     cudaSetDevice(ctx->device);
     cudaStreamSynchronize(ctx->stream);
     ctx->tensors.erase(it);
+    for (auto r = ctx->by_host.equal_range(t->h_data); r.first != r.second; ++r.first)
+        if (r.first->second == t) {
+            ctx->by_host.erase(r.first);
+            break;
+        }
     free_tensor_mem(t);
     delete t;
     return POX_OK;
@@ -763,10 +783,35 @@ extern "C" int pox_cuda_tensor_gemv_ex(pox_cuda_ctx* ctx, const pox_tensor* t, c
     return gemv_launch(ctx, t, x_dev, batch, y_dev, st, &p, resid_dev);
 }
 
+static int ensure_pinned(float** host, float** dev, size_t* have, size_t need) {
+    if (need <= *have) return POX_OK;
+    cudaFreeHost(*host);
+    *host = *dev = nullptr;
+    *have = 0;
+    CK(cudaHostAlloc((void**)host, need, cudaHostAllocMapped), "cudaHostAlloc(staging)");
+    CK(cudaHostGetDevicePointer((void**)dev, *host, 0), "cudaHostGetDevicePointer(staging)");
+    *have = need;
+    return POX_OK;
+}
+
 // Host x in, host y out, synchronous. Caller holds ctx->mu.
+// Tiled tensors: x goes through pinned, device-mapped staging that the x preparation reads directly,
+// and the GEMV writes y into pinned staging: one host copy each way, no DMA, one stream sync.
+// The raw-layout kernels re-read x for every row, so they get x in device memory.
 static int gemv_host_locked(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x, size_t batch, float* y) {
     if (t->rows == 0 || t->cols == 0 || batch == 0) return POX_OK;
     const size_t xb = batch * t->cols * sizeof(float), yb = batch * t->rows * sizeof(float);
+    if (t->tiled) {
+        int rc = ensure_pinned(&ctx->pin_x, &ctx->pin_x_dev, &ctx->pin_x_bytes, xb);
+        if (!rc) rc = ensure_pinned(&ctx->pin_y, &ctx->pin_y_dev, &ctx->pin_y_bytes, yb);
+        if (rc) return rc;
+        std::memcpy(ctx->pin_x, x, xb);
+        rc = gemv_launch(ctx, t, ctx->pin_x_dev, batch, ctx->pin_y_dev, ctx->stream);
+        if (rc) return rc;
+        CK(cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
+        std::memcpy(y, ctx->pin_y, yb);
+        return take_kernel_error(ctx);
+    }
     int rc = ensure_scratch(ctx, xb, yb);
     if (rc) return rc;
     CK(cudaMemcpyAsync(ctx->scratch_x, x, xb, cudaMemcpyHostToDevice, ctx->stream), "cudaMemcpy(x)");
@@ -786,13 +831,17 @@ extern "C" int pox_cuda_tensor_gemv_host(pox_cuda_ctx* ctx, const pox_tensor* t,
     return gemv_host_locked(ctx, t, x, batch, y);
 }
 
+// The resident tensor uploaded from exactly these host slices (same addresses and lengths, shape,
+// dtype, group size), looked up by the weight payload's address.
 static pox_tensor* find_registered(pox_cuda_ctx* ctx, const pox_tensor_desc& d) {
-    for (pox_tensor* t : ctx->tensors)
-        if (t->dtype == d.dtype && t->h_data == d.data && t->h_data_len == d.data_len && t->h_scales == d.scales &&
+    for (auto r = ctx->by_host.equal_range(d.data); r.first != r.second; ++r.first) {
+        pox_tensor* t = r.first->second;
+        if (t->dtype == d.dtype && t->h_data_len == d.data_len && t->h_scales == d.scales &&
             t->h_scale_len == d.scale_len && t->rows == d.rows && t->cols == d.cols &&
             (d.dtype != POX_I4 || (t->gs == d.group_size && t->h_outliers == d.outliers &&
                                    t->h_outlier_len == d.outlier_len)))
             return t;
+    }
     return nullptr;
 }
 

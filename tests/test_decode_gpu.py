@@ -89,6 +89,64 @@ def test_decode_matches_forward_token(be, name, outliers, nseq):
     model.close()
 
 
+# The Llama-3-8B widths (d 4096, 32 / 8 heads of 128, FFN 14336, vocab 128256, f16 embedding and
+# lm_head), two layers so the oracle's scalar forward_token stays within seconds per token.
+LLAMA8B_2L = {"hidden": 4096, "inter": 14336, "layers": 2, "n_heads": 32, "n_kv_heads": 8, "vocab": 128256,
+              "rms_eps": 1e-5, "rope_theta": 500000.0}
+
+
+@pytest.fixture(scope="module")
+def llama8b_2l(be):
+    w = make_llama(LLAMA8B_2L, seed=17, norm_jitter=0.1)
+    model = CudaModel(be, LLAMA8B_2L, max_batch=32, kv_blocks=64, max_blocks_per_seq=2)
+    load_into(model, w)
+    yield model, oracle_weights(w)
+    model.close()
+
+
+@pytest.mark.parametrize("nseq", [1, 9, 32])
+def test_decode_llama8b_widths(be, llama8b_2l, nseq):
+    """Every kernel of the step at its Llama-3-8B size (the batch <= 8 GEMV at 1, the integer small-M
+    kernel and the f16 lm_head tiles at 9 and 32, the tensor-core attention with 4 query heads per
+    kv head): 3-5 prompt tokens then 5 greedy steps per sequence, teacher-forced on the oracle."""
+    from concurrent.futures import ThreadPoolExecutor
+    import os
+
+    model, ow = llama8b_2l
+    cfg = LLAMA8B_2L
+    rng = np.random.default_rng(100 + nseq)
+    prompts = [list(rng.integers(0, cfg["vocab"], int(n))) for n in rng.integers(3, 6, nseq)]
+    steps = 5
+    oracles = [O.OracleModel(cfg, ow, max_seq=32, kv_f16=True) for _ in prompts]
+    seqs = [model.new_sequence() for _ in prompts]
+    feeds = [list(p) for p in prompts]
+    pool = ThreadPoolExecutor(max_workers=min(32, os.cpu_count() or 1))  # the oracle releases the GIL
+    agree = total = 0
+    worst = 0.0
+    for t in range(max(len(p) for p in prompts) + steps):
+        active = [i for i in range(nseq) if t < len(prompts[i]) + steps]
+        tokens = [int(feeds[i][t]) for i in active]
+        logits, nxt = model.decode(tokens, [seqs[i] for i in active])
+        refs = list(pool.map(lambda j: oracles[active[j]].forward_token(tokens[j], t), range(len(active))))
+        for j, i in enumerate(active):
+            ref = refs[j]
+            err = float(np.max(np.abs(logits[j] - ref)))
+            worst = max(worst, err)
+            assert err <= E2E_TOL, (nseq, i, t, err)
+            top = np.sort(ref)[-2:]
+            ref_tok = int(np.argmax(ref))
+            if top[1] - top[0] > E2E_TOL:
+                total += 1
+                agree += int(nxt[j]) == ref_tok
+            if t + 1 >= len(prompts[i]):
+                feeds[i].append(ref_tok)
+    pool.shutdown()
+    for sq in seqs:
+        sq.free(model.blocks)
+    print(f"llama-8b widths, batch {nseq}: worst logit |diff| {worst:.2e}, greedy agreement {agree}/{total}")
+    assert total > 0 and agree == total, (agree, total)
+
+
 def test_decode_rejects_bad_inputs(be):
     from paraoxidizer_b200 import _lib as L
 
@@ -102,4 +160,33 @@ def test_decode_rejects_bad_inputs(be):
     seq.allocated_block_ids = [0, 1]
     with pytest.raises(L.PoxError):
         model.decode([1], [seq])
+    # set_state: every page up to a row's next position must be a block (BlockTable pads with -1)
+    s2 = model.new_sequence()
+    s2.sequence_len, s2.allocated_block_ids = 16, [0]  # position 16 needs page 1, which has no block
+    with pytest.raises(L.PoxError) as ei:
+        model.set_state([1], [s2])
+    assert ei.value.code == L.POX_ERR_INVALID
+    # the device path advances positions on the GPU: a step that reaches a page without a block, or a
+    # position beyond the block table, is caught by the attention kernel (nothing outside the KV pages
+    # is touched) and reported by the next synchronize; the context stays usable
+    s3 = model.new_sequence()
+    s3.sequence_len, s3.allocated_block_ids = 15, [1]
+    model.set_state([1], [s3])
+    model.decode_device(1, True)  # position 15 (page 0 = block 1), then advances to 16
+    be.synchronize()
+    model.decode_device(1, True)  # position 16: page 1 is -1
+    with pytest.raises(L.PoxError) as ei:
+        be.synchronize()
+    assert ei.value.code == L.POX_ERR_INVALID and "block-table entry" in str(ei.value)
+    s4 = model.new_sequence()
+    s4.sequence_len, s4.allocated_block_ids = 31, [2, 3]
+    model.set_state([1], [s4])
+    model.decode_device(1, True)  # position 31, the last the table holds
+    be.synchronize()
+    model.decode_device(1, True)  # position 32 = 16 x max_blocks_per_seq
+    with pytest.raises(L.PoxError) as ei:
+        be.synchronize()
+    assert "beyond its block table" in str(ei.value)
+    logits, _ = model.decode([5], [model.new_sequence()])  # usable afterwards
+    assert np.all(np.isfinite(logits))
     model.close()

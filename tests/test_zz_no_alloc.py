@@ -57,6 +57,19 @@ def test_noalloc_matches_tensor_gemv_on_two_calls():
             for b in range(batch):
                 assert max_rel(yn[b * rows:(b + 1) * rows], yr[b * rows:(b + 1) * rows]) <= GEMV_TOL, (seed, b)
 
+        # batch 11: two launches of up to 8 rows inside one call, both through the shared array
+        batch = 11
+        x = torch.from_numpy(rng.standard_normal(batch * cols, dtype=np.float32)).to(dev)
+        y_ref = torch.zeros(batch * rows, dtype=torch.float32, device=dev)
+        y_new = torch.full((batch * rows,), float("nan"), dtype=torch.float32, device=dev)
+        torch.cuda.synchronize()
+        L.check(lib.pox_cuda_tensor_gemv(be.ctx, t8.handle, x.data_ptr(), batch, y_ref.data_ptr(), None))
+        L.check(lib.pox_cuda_tensor_gemv_noalloc(be.ctx, t8.handle, x.data_ptr(), batch, y_new.data_ptr(), None))
+        be.synchronize()
+        yr, yn = y_ref.cpu().numpy(), y_new.cpu().numpy()
+        for b in range(batch):
+            assert max_rel(yn[b * rows:(b + 1) * rows], yr[b * rows:(b + 1) * rows]) <= GEMV_TOL, ("b11", b)
+
         # beyond the array: a clear error, nothing launched
         big = 40960
         wb = rng.standard_normal(16 * big, dtype=np.float32) * np.float32(0.02)
@@ -72,4 +85,86 @@ def test_noalloc_matches_tensor_gemv_on_two_calls():
     finally:
         t4.free()
         t8.free()
+        be.close()
+
+
+def test_noalloc_f16_at_the_array_limit():
+    """An F16 tensor with cols = 32768 fills the array exactly (prepared x of 8 rows as f16 hi / lo
+    pairs: 1 MiB, plus 16 KiB of block metadata): accepted and equal to pox_cuda_tensor_gemv on two
+    calls in a row. cols = 32800 (one 32-column block more) is rejected with POX_ERR_UNSUPPORTED."""
+    import torch
+
+    be = CudaBackend.create(0)
+    lib = L.lib()
+    dev = torch.device("cuda", 0)
+    rng = np.random.default_rng(41)
+    try:
+        rows, cols = 64, 32768
+        wb = (rng.standard_normal(rows * cols, dtype=np.float32) * np.float32(0.02)).astype(np.float16)
+        t = be.upload_f16(wb.view(np.uint16), rows, cols)
+        for batch in (8, 3):
+            x = torch.from_numpy(rng.standard_normal(batch * cols, dtype=np.float32)).to(dev)
+            y_ref = torch.zeros(batch * rows, dtype=torch.float32, device=dev)
+            y_new = torch.full((batch * rows,), float("nan"), dtype=torch.float32, device=dev)
+            torch.cuda.synchronize()
+            L.check(lib.pox_cuda_tensor_gemv(be.ctx, t.handle, x.data_ptr(), batch, y_ref.data_ptr(), None))
+            L.check(lib.pox_cuda_tensor_gemv_noalloc(be.ctx, t.handle, x.data_ptr(), batch, y_new.data_ptr(), None))
+            be.synchronize()
+            yr, yn = y_ref.cpu().numpy(), y_new.cpu().numpy()
+            assert np.all(np.isfinite(yn))
+            for b in range(batch):
+                assert max_rel(yn[b * rows:(b + 1) * rows], yr[b * rows:(b + 1) * rows]) <= GEMV_TOL, (batch, b)
+        t.free()
+        cols = 32800
+        wb = np.zeros(16 * cols, np.uint16)
+        t = be.upload_f16(wb, 16, cols)
+        x = torch.zeros(cols, dtype=torch.float32, device=dev)
+        y = torch.zeros(16, dtype=torch.float32, device=dev)
+        torch.cuda.synchronize()
+        rc = lib.pox_cuda_tensor_gemv_noalloc(be.ctx, t.handle, x.data_ptr(), 1, y.data_ptr(), None)
+        assert rc == L.POX_ERR_UNSUPPORTED and "32768" in L.last_error()
+        t.free()
+    finally:
+        be.close()
+
+
+def test_noalloc_reports_an_earlier_kernel_error():
+    """The call returns before its kernels run, so an error a kernel raised on the context's flag is
+    returned by the next call instead of being dropped: here the flag is raised by a paged attention
+    call given a page outside the pool, the next no-alloc GEMV returns it and launches nothing, and
+    the call after that runs normally."""
+    import torch
+
+    be = CudaBackend.create(0)
+    lib = L.lib()
+    dev = torch.device("cuda", 0)
+    rng = np.random.default_rng(43)
+    try:
+        rows, cols = 256, 1024
+        w = rng.standard_normal(rows * cols, dtype=np.float32) * np.float32(0.02)
+        packed, scales = Q.quantize_int4_group(w, 128)
+        t = be.upload_int4(packed, scales, rows, cols, 128)
+        heads, kvh, hd, nblk = 4, 1, 128, 2
+        q = torch.zeros(heads * hd, dtype=torch.float32, device=dev)
+        kp = torch.zeros(nblk * kvh * 16 * hd, dtype=torch.int16, device=dev)
+        tab = torch.tensor([nblk + 7], dtype=torch.int32, device=dev)  # outside the pool
+        pos = torch.tensor([3], dtype=torch.int32, device=dev)
+        out = torch.zeros(heads * hd, dtype=torch.float32, device=dev)
+        torch.cuda.synchronize()
+        L.check(lib.pox_cuda_paged_attention(be.ctx, q.data_ptr(), kp.data_ptr(), kp.data_ptr(), tab.data_ptr(),
+                                             pos.data_ptr(), 1, heads, kvh, hd, nblk, 1, out.data_ptr(), None))
+        torch.cuda.synchronize()  # the attention kernel has raised the flag; nothing has read it yet
+        x = torch.from_numpy(rng.standard_normal(cols, dtype=np.float32)).to(dev)
+        y = torch.full((rows,), float("nan"), dtype=torch.float32, device=dev)
+        rc = lib.pox_cuda_tensor_gemv_noalloc(be.ctx, t.handle, x.data_ptr(), 1, y.data_ptr(), None)
+        assert rc == L.POX_ERR_INVALID, (rc, L.last_error())
+        be.synchronize()
+        assert torch.isnan(y).all()  # nothing was launched
+        y_ref = torch.zeros(rows, dtype=torch.float32, device=dev)
+        L.check(lib.pox_cuda_tensor_gemv_noalloc(be.ctx, t.handle, x.data_ptr(), 1, y.data_ptr(), None))
+        L.check(lib.pox_cuda_tensor_gemv(be.ctx, t.handle, x.data_ptr(), 1, y_ref.data_ptr(), None))
+        be.synchronize()
+        assert max_rel(y.cpu().numpy(), y_ref.cpu().numpy()) <= GEMV_TOL
+        t.free()
+    finally:
         be.close()

@@ -33,3 +33,13 @@ def test_overrides_and_none():
     assert bench.decode_batches(args(decode_batches="none")) == ()
     assert bench.decode_batches(args(decode_batches="2,4")) == (2, 4)
     assert bench.decode_kwargs(args(decode_prefill=64))["prefill"] == 64
+
+
+def test_tp_check_models_shard_at_their_rank_counts():
+    """The tensor-parallel check's small models give every rank a kv head, whole 128-column groups
+    of o_proj / down_proj and an equal vocab slice (tp.check_tp), at 2, 4 and 8 ranks."""
+    from paraoxidizer_b200 import tp as TP
+
+    for world, cfg in bench.TP_CHECK_CFGS.items():
+        TP.check_tp(cfg, world)
+        assert cfg["n_kv_heads"] >= world and (cfg["hidden"] // cfg["n_heads"]) * cfg["n_heads"] // world % 128 == 0

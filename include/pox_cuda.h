@@ -39,7 +39,10 @@ typedef enum {
     POX_ERR_NCCL = 4,        /* collective failure */
     POX_ERR_TIMEOUT = 5,     /* a bounded wait ran out */
     POX_ERR_OOM = 6,         /* device memory or paged-KV blocks exhausted */
-    POX_ERR_INVALID = 7      /* null pointer, bad handle or argument */
+    POX_ERR_INVALID = 7,     /* null pointer, bad handle or argument */
+    POX_ERR_FORMAT = 8,      /* malformed .pox container (PoxError::Format / InvalidMagic / UnsupportedVersion /
+                                Security / Json) */
+    POX_ERR_INTEGRITY = 9    /* a tensor's SHA-256 differs from its index entry (PoxError::IntegrityHashMismatch) */
 } pox_status;
 
 /* DType codes, crates/paraoxidizer-core/src/tensor.rs:4-20 */
@@ -320,6 +323,63 @@ int pox_cuda_model_comm_mode(pox_model* m, int mode);
  * *wait_seconds (may be NULL) = the kernel's duration. The context stays usable. No counterpart
  * in the reference (one process, no exchanges). */
 int pox_cuda_comm_check_missing_rank(pox_cuda_ctx* ctx, double* wait_seconds);
+
+/* ---- the .pox container on the host (crates/paraoxidizer-format/src/pox.rs) --------------------- */
+
+typedef struct pox_file pox_file;
+
+/* One entry of the tensor index: TensorMeta (crates/paraoxidizer-core/src/tensor.rs:116-128). Offsets
+ * are absolute in the file; name and sha256 (lower-case hex) stay valid while the file is open. */
+typedef struct {
+    const char* name;
+    int dtype;              /* POX_F32 .. POX_I4; -1 for the F8E4M3 / F8E5M2 entries this backend does not serve */
+    uint32_t group_size;    /* QuantGroupSize: 0 (None), 32, 64, 128 or 256 */
+    uint32_t rank;          /* shape rank (first 8 dims in dims) */
+    uint64_t dims[8];
+    uint64_t data_offset, data_len, scale_offset, scale_len, outlier_offset, outlier_len;
+    const char* sha256;
+} pox_tensor_meta;
+
+/* Replaces PoxFile::open (pox.rs:171-175, from_mmap :248-310): maps the file read-only, checks the
+ * 128-byte header (magic "POX\x01", version 1) and the bounds of every section, and parses the JSON
+ * metadata, tensor index, quant plan, manifest and signature. POX_ERR_FORMAT with the reference's
+ * message on a malformed file, POX_ERR_INVALID when it cannot be opened. */
+int pox_file_open(const char* path, pox_file** out);
+/* Replaces PoxFile::from_bytes (pox.rs:177-246): the same checks on a byte buffer, which is copied. */
+int pox_file_from_bytes(const uint8_t* bytes, size_t len, pox_file** out);
+void pox_file_close(pox_file* f);
+int pox_file_tensor_count(const pox_file* f, size_t* n);
+int pox_file_tensor_meta(const pox_file* f, size_t index, pox_tensor_meta* out);
+/* tensor_map lookup (pox.rs:199-202; a repeated name maps to its last entry). POX_ERR_INVALID if absent. */
+int pox_file_find(const pox_file* f, const char* name, size_t* index);
+/* get_tensor_data / get_scale_data / get_outlier_data (pox.rs:311-353): zero-copy slices of the file.
+ * *ptr = NULL, *len = 0 where the reference returns None (unknown name, empty scale / outlier section,
+ * a range past the end). */
+int pox_file_tensor_data(const pox_file* f, const char* name, const uint8_t** ptr, size_t* len);
+int pox_file_scale_data(const pox_file* f, const char* name, const uint8_t** ptr, size_t* len);
+int pox_file_outlier_data(const pox_file* f, const char* name, const uint8_t** ptr, size_t* len);
+/* metadata.model_config (ModelConfig, crates/paraoxidizer-core/src/arch.rs:96-112) as the decode
+ * configuration; *tie_word_embeddings (may be NULL) = its tie_word_embeddings flag. */
+int pox_file_model_config(const pox_file* f, pox_llama_config* cfg, int* tie_word_embeddings);
+/* Replaces PoxFile::verify_integrity (pox.rs:356-383): SHA-256 of data || scales || outliers of every
+ * tensor against its index entry; the first mismatch in index order -> POX_ERR_INTEGRITY. The tensors
+ * are hashed by `threads` host threads (<= 0: one per core). */
+int pox_file_verify_integrity(const pox_file* f, int threads);
+/* Rank tp_rank's shard of a 2-D INT4 tensor for tensor-parallel decode, in .pox payload form: split 0 =
+ * rows [r tp_rank, r (tp_rank + 1)) with r = rows / tp_size, split 1 = columns likewise (whole groups);
+ * outlier entries outside the shard dropped, the rest re-indexed to the shard, order kept. With buffers
+ * too small (or NULL) the sizes are stored and POX_ERR_LAYOUT returned. No counterpart in the reference
+ * (one device). */
+int pox_file_tensor_shard(const pox_file* f, const char* name, int split, uint32_t tp_rank, uint32_t tp_size,
+                          uint8_t* data, size_t* data_len, uint8_t* scales, size_t* scale_len, uint8_t* outliers,
+                          size_t* outlier_len);
+/* A decode model built from a .pox file on the context's GPU: the engine's tensors (engine.rs:424-713;
+ * model.embed_tokens / model.norm / lm_head F16, the seven INT4 projections of every layer with their
+ * outlier tables, input / post-attention norms F16; tie_word_embeddings without lm_head uses the
+ * embedding) uploaded once, as rank tp_rank of tp_size (pox_cuda_model_create_tp's split). Other dtypes
+ * -> POX_ERR_UNSUPPORTED. The file may be closed afterwards. */
+int pox_cuda_model_load(pox_cuda_ctx* ctx, const pox_file* f, uint32_t max_batch, uint32_t kv_blocks,
+                        uint32_t max_blocks_per_seq, uint32_t tp_rank, uint32_t tp_size, pox_model** out);
 
 #ifdef __cplusplus
 }

@@ -15,7 +15,9 @@ HEADER = os.path.join(os.path.dirname(_PKG), "include", "pox_cuda.h")
 
 POX_OK, POX_ERR_LAYOUT, POX_ERR_UNSUPPORTED, POX_ERR_CUDA = 0, 1, 2, 3
 POX_ERR_NCCL, POX_ERR_TIMEOUT, POX_ERR_OOM, POX_ERR_INVALID = 4, 5, 6, 7
-STATUS_NAMES = {0: "OK", 1: "LAYOUT", 2: "UNSUPPORTED", 3: "CUDA", 4: "NCCL", 5: "TIMEOUT", 6: "OOM", 7: "INVALID"}
+POX_ERR_FORMAT, POX_ERR_INTEGRITY = 8, 9
+STATUS_NAMES = {0: "OK", 1: "LAYOUT", 2: "UNSUPPORTED", 3: "CUDA", 4: "NCCL", 5: "TIMEOUT", 6: "OOM", 7: "INVALID",
+                8: "FORMAT", 9: "INTEGRITY"}
 
 # DType codes (crates/paraoxidizer-core/src/tensor.rs:4-20)
 POX_F32, POX_F16, POX_BF16, POX_I8, POX_I4 = 0, 1, 2, 3, 4
@@ -69,7 +71,7 @@ def declared_symbols() -> list[str]:
     with open(HEADER) as f:
         src = f.read()
     src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
-    return sorted(set(re.findall(r"\b(pox_cuda_\w+)\s*\(", src)))
+    return sorted(set(re.findall(r"\b(pox_(?:cuda|file)_\w+)\s*\(", src)))
 
 
 POX_COMM_NCCL, POX_COMM_PEER = 1, 2
@@ -115,6 +117,20 @@ def _declare(L):
         "pox_cuda_model_buffers": (i32, [vp, C.POINTER(vp), C.POINTER(vp), C.POINTER(vp), C.POINTER(vp),
                                          C.POINTER(vp)]),
         "pox_cuda_paged_attention": (i32, [vp, vp, vp, vp, vp, vp, u32, u32, u32, u32, u32, u32, vp, vp]),
+        "pox_file_open": (i32, [C.c_char_p, C.POINTER(vp)]),
+        "pox_file_from_bytes": (i32, [vp, sz, C.POINTER(vp)]),
+        "pox_file_close": (None, [vp]),
+        "pox_file_tensor_count": (i32, [vp, C.POINTER(sz)]),
+        "pox_file_tensor_meta": (i32, [vp, sz, vp]),
+        "pox_file_find": (i32, [vp, C.c_char_p, C.POINTER(sz)]),
+        "pox_file_tensor_data": (i32, [vp, C.c_char_p, C.POINTER(vp), C.POINTER(sz)]),
+        "pox_file_scale_data": (i32, [vp, C.c_char_p, C.POINTER(vp), C.POINTER(sz)]),
+        "pox_file_outlier_data": (i32, [vp, C.c_char_p, C.POINTER(vp), C.POINTER(sz)]),
+        "pox_file_model_config": (i32, [vp, C.POINTER(LlamaConfig), C.POINTER(C.c_int)]),
+        "pox_file_verify_integrity": (i32, [vp, i32]),
+        "pox_file_tensor_shard": (i32, [vp, C.c_char_p, i32, u32, u32, vp, C.POINTER(sz), vp, C.POINTER(sz), vp,
+                                        C.POINTER(sz)]),
+        "pox_cuda_model_load": (i32, [vp, vp, u32, u32, u32, u32, u32, C.POINTER(vp)]),
         "pox_cuda_tensor_dequant": (i32, [vp, vp, vp, vp]),
         "pox_cuda_tensor_dequant_host": (i32, [vp, vp, vp]),
     }

@@ -16,7 +16,7 @@ CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libpox_cuda.so")
 BUILD_DIR = os.path.join(PKG, "_build")
 
-SOURCES = ["pox_api.cu", "gemv.cu", "gemm_tc05.cu", "gemm_tcq.cu", "engine.cu", "comm.cu", "quantize.cu", "noalloc.cu"]
+SOURCES = ["pox_api.cu", "gemv.cu", "gemv_stream.cu", "gemm_tc05.cu", "gemm_tcq.cu", "engine.cu", "comm.cu", "quantize.cu", "noalloc.cu", "pox_file.cpp"]
 HEADERS = ["common.cuh", "gemv.cuh", "api_internal.h", "model.h", "comm.cuh", "tc05.cuh"]
 
 
@@ -68,7 +68,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
     objs = []
     procs = []
     for s in SOURCES:
-        o = os.path.join(BUILD_DIR, s.replace(".cu", ".o"))
+        o = os.path.join(BUILD_DIR, os.path.splitext(s)[0] + ".o")
         cmd = [nvcc, *ARCH, *FLAGS, *inc, "-c", os.path.join(CSRC, s), "-o", o]
         if verbose:
             print(" ".join(cmd), file=sys.stderr)

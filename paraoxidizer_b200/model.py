@@ -52,6 +52,26 @@ class CudaModel:
         self.max_blocks_per_seq = max_blocks_per_seq
         self.blocks = BlockManager(kv_blocks, DEFAULT_BLOCK_SIZE)
 
+    @classmethod
+    def from_pox(cls, backend, pox_file, max_batch: int, kv_blocks: int, max_blocks_per_seq: int, tp_rank: int = 0,
+                 tp_size: int = 1) -> "CudaModel":
+        """The model of a .pox file (pox_format.PoxFile), rank tp_rank of tp_size, uploaded once
+        (pox_cuda_model_load); its configuration is the file's model_config."""
+        cfg = pox_file.model_config()
+        h = C.c_void_p()
+        L.check(L.lib().pox_cuda_model_load(backend.ctx, pox_file.handle, max_batch, kv_blocks, max_blocks_per_seq,
+                                            tp_rank, tp_size, C.byref(h)))
+        self = cls.__new__(cls)
+        self.backend = backend
+        self.cfg = {k: v for k, v in cfg.items() if k != "tie_word_embeddings"}
+        self.tp_rank, self.tp_size = tp_rank, tp_size
+        self.handle = h.value
+        backend._children.append(weakref.ref(self))
+        self.max_batch = max_batch
+        self.max_blocks_per_seq = max_blocks_per_seq
+        self.blocks = BlockManager(kv_blocks, DEFAULT_BLOCK_SIZE)
+        return self
+
     @property
     def vocab_local(self) -> int:
         return self.cfg["vocab"] // self.tp_size

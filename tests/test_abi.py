@@ -26,7 +26,7 @@ def test_exported_symbols_have_c_linkage():
     # nm -D shows the plain (unmangled) names for every declared entry point
     import subprocess
     out = subprocess.run(["nm", "-D", "--defined-only", L.LIB_PATH], capture_output=True, text=True).stdout
-    names = set(re.findall(r"\b(pox_cuda_\w+)\b", out))
+    names = set(re.findall(r"\b(pox_(?:cuda|file)_\w+)\b", out))
     assert set(L.declared_symbols()) <= names
 
 

@@ -147,6 +147,39 @@ def test_decode_llama8b_widths(be, llama8b_2l, nseq):
     assert total > 0 and agree == total, (agree, total)
 
 
+def test_decode_from_pox_file(be, tmp_path):
+    """The model read from a .pox file (pox_cuda_model_load over the C++ container reader: mmap,
+    tensor index, one verify_integrity) decodes like forward_token on the same weights."""
+    from paraoxidizer_b200.pox_format import PoxFile, llama_pox_bytes
+
+    cfg = CONFIGS["l8"]
+    w = make_llama(cfg, seed=13, outlier_policy="automatic", norm_jitter=0.1)
+    path = tmp_path / "llama.pox"
+    path.write_bytes(llama_pox_bytes(cfg, w))
+    f = PoxFile.open(str(path))
+    f.verify_integrity()
+    model = CudaModel.from_pox(be, f, max_batch=3, kv_blocks=48, max_blocks_per_seq=16)
+    f.close()  # the model holds its own copies on the GPU
+    assert model.cfg["hidden"] == cfg["hidden"] and model.cfg["vocab"] == cfg["vocab"]
+    ow = oracle_weights(w)
+    rng = np.random.default_rng(6)
+    prompts = [list(rng.integers(0, cfg["vocab"], n)) for n in (4, 70, 19)]
+    oracles = [O.OracleModel(cfg, ow, max_seq=256, kv_f16=True) for _ in prompts]
+    seqs = [model.new_sequence() for _ in prompts]
+    feeds = [list(p) for p in prompts]
+    steps = 6
+    for t in range(max(len(p) for p in prompts) + steps):
+        active = [i for i in range(3) if t < len(prompts[i]) + steps]
+        tokens = [int(feeds[i][t]) for i in active]
+        logits, nxt = model.decode(tokens, [seqs[i] for i in active])
+        for j, i in enumerate(active):
+            ref = oracles[i].forward_token(tokens[j], t)
+            assert float(np.max(np.abs(logits[j] - ref))) <= E2E_TOL, (i, t)
+            if t + 1 >= len(prompts[i]):
+                feeds[i].append(int(np.argmax(ref)))
+    model.close()
+
+
 def test_decode_rejects_bad_inputs(be):
     from paraoxidizer_b200 import _lib as L
 

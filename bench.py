@@ -177,6 +177,78 @@ def cpu_baseline_sample(packed, scales, tab, budget_s: float = 12.0, rows_per_ca
     return gbs, rows_done, t_total
 
 
+def host_cpu():
+    """The host CPU model and the number of cores this process may use."""
+    model = "unknown"
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    try:
+        n = len(os.sched_getaffinity(0))
+    except AttributeError:
+        n = os.cpu_count() or 1
+    return model, n
+
+
+def cpu_decode_baseline(be, cfg=None, positions=3):
+    """The reference's forward_token (the oracle's C restatement, single-threaded like the reference)
+    timed at the Llama-3-8B widths on a reduced schedule: a 1-layer and a 2-layer model share the
+    first layer's weights (INT4 g128 from the GPU quantizer, f16 embedding / lm_head), each decodes
+    `positions` tokens; the difference gives one layer's time and the rest the embedding / norm /
+    lm_head, so tokens/s of the full model = 1 / (rest + layers x layer). Random-init weights."""
+    import torch
+
+    from oracle import oracle as O
+    from paraoxidizer_b200 import _lib as L
+
+    cfg = dict(cfg or LLAMA_8B)
+    H, I, V = cfg["hidden"], cfg["inter"], cfg["vocab"]
+    hd = H // cfg["n_heads"]
+    qd, kvd = cfg["n_heads"] * hd, cfg["n_kv_heads"] * hd
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(4)
+    shapes = {"q": (qd, H), "k": (kvd, H), "v": (kvd, H), "o": (H, qd), "gate": (I, H), "up": (I, H), "down": (H, I)}
+    layer = {}
+    for name, (r, c) in shapes.items():
+        w = torch.randn(r * c, device="cuda", generator=gen).mul_(0.02)
+        p = torch.empty(r * c // 2, dtype=torch.uint8, device="cuda")
+        sc = torch.empty(r * c // 128 * 4, dtype=torch.uint8, device="cuda")
+        torch.cuda.synchronize()
+        L.check(L.lib().pox_cuda_quantize_int4(be.ctx, w.data_ptr(), r * c, 128, p.data_ptr(), sc.data_ptr(), None))
+        be.synchronize()
+        layer[name] = {"packed": p.cpu().numpy(), "scales": sc.cpu().numpy(), "rows": r, "cols": c, "group_size": 128,
+                       "outliers": None}
+        del w, p, sc
+    ones = np.ones(H, np.float32).astype(np.float16).view(np.uint16)
+    layer["attn_norm"] = layer["mlp_norm"] = ones
+    emb = torch.randn(V * H, device="cuda", generator=gen).mul_(0.02).half().cpu().numpy().view(np.uint16)
+    head = torch.randn(V * H, device="cuda", generator=gen).mul_(0.02).half().cpu().numpy().view(np.uint16)
+    times = {}
+    for nl in (1, 2):
+        c = dict(cfg, layers=nl)
+        m = O.OracleModel(c, {"embed": emb, "lm_head": head, "final_norm": ones, "layers": [layer] * nl},
+                          max_seq=positions + 1, kv_f16=False)
+        t0 = time.perf_counter()
+        for pos in range(positions):
+            m.forward_token(7 + pos, pos)
+        times[nl] = (time.perf_counter() - t0) / positions
+    t_layer = max(times[2] - times[1], 1e-9)
+    t_rest = max(times[1] - t_layer, 0.0)
+    per_token = t_rest + cfg["layers"] * t_layer
+    model, n = host_cpu()
+    return {"tokens_per_s": round(1.0 / per_token, 4), "s_per_token": round(per_token, 3), "cores": 1,
+            "kind": "port", "cpu_model": model, "host_cores": n,
+            "sample": f"forward_token (oracle C restatement, single-threaded like the reference) at the Llama-3-8B "
+                      f"widths: {positions} tokens through a 1-layer and a 2-layer model ({times[1]:.3f} / "
+                      f"{times[2]:.3f} s per token), extrapolated to {cfg['layers']} layers "
+                      f"(one layer {t_layer:.3f} s, embedding + norm + lm_head {t_rest:.3f} s)"}
+
+
 def run_reference(args):
     world, rank, _ = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), 0
     if rank != 0:
@@ -572,7 +644,7 @@ def run_ours(args):
     clocks = cs.summary()
 
     kname = tensors[0].gemv_kernel(1)
-    launches_per_step = 1 if kname == "gemv_stream_kernel" else 2  # the stream kernel prepares x itself
+    launches_per_step = 2  # x preparation + GEMV
     bytes_per = algorithmic_bytes(nnz)
     total_bytes = bytes_per * args.steps * world
     gbs = total_bytes / (ms * 1e-3) / 1e9
@@ -632,9 +704,13 @@ def run_ours(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cgbs, crows, ct = cpu_baseline_sample(packed, scales, tab)
+        cmodel, ncores = host_cpu()
         cpu = {"value": round(cgbs, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+               "cpu_model": cmodel, "host_cores": ncores,
                "sample": f"{crows} rows ({crows / ROWS:.2f} GEMVs) of the same workload in {ct:.1f} s through the "
                          f"oracle's quant::gemv_int4 (single-threaded, as the reference)"}
+        if not args.no_decode:
+            cpu["decode"] = cpu_decode_baseline(be)
 
     if rank == 0:
         line = {"metric": METRIC, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -650,10 +726,8 @@ def run_ours(args):
                 "pct_of_peak": round(100.0 * achieved / peak, 2),
                 "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                              "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                             "kernel": (f"{kname}<INT4,1> (x preparation fused in; one launch per step)"
-                                        if launches_per_step == 1 else
-                                        f"{kname}<INT4,1> with its x preparation (one step = both launches, "
-                                        "PDL-overlapped, timed together with CUDA events)"),
+                             "kernel": f"{kname}<INT4,1> with its x preparation (one step = both launches, "
+                                       "PDL-overlapped, timed together with CUDA events)",
                              "traffic": traffic},
                 "e2e": {"value": round(e2e_gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": COLS * 4,
                         "d2h_bytes_per_step": ROWS * 4, "steps": e2e_steps,

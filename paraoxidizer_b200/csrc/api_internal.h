@@ -26,8 +26,6 @@ struct pox_tensor {
     size_t nnz = 0;
     void* scratch = nullptr;      // prepared x of the tiled GEMV (up to 8 batch rows)
     size_t scratch_bytes = 0;
-    void* stream_ws = nullptr;    // tiled: partials of split row tiles + tickets of the stream GEMV
-    int stream_ws_sms = 0;        // CTAs the workspace holds partials for
     size_t bytes = 0;
     // host slices the tensor was uploaded from (registry key of the host-slice entry points)
     const uint8_t* h_data = nullptr;
@@ -95,8 +93,6 @@ struct XTarget {
 };
 int gemv_x_target(pox_cuda_ctx* ctx, const pox_tensor* t, size_t batch, cudaStream_t st, XTarget* out);
 bool gemv_uses_small_m(const pox_tensor* t, size_t batch);
-// The batch <= 8 GEMV of t at `batch` rows runs the persistent stream kernel (x prepared inside it).
-bool gemv_uses_stream(const pox_tensor* t, size_t batch);
 void destroy_ctx_extras(pox_cuda_ctx* ctx);
 // Small-M path scratch for a tensor of rows x cols at `batch` rows of x (grown outside stream
 // capture only; a captured graph keeps the buffers it was captured with).

@@ -158,29 +158,6 @@ cudaError_t launch_xprep(int kind, const float* x, int B, int K, const XPrep& xp
 // before the previous kernel in the stream (the x preparation) has finished.
 cudaError_t launch_gemv_tc(int kind, const GemvArgs& a, bool pdl, cudaStream_t st);
 
-// The batch <= 8 GEMV as one persistent stream per SM with the x preparation fused in
-// (gemv_stream.cu): x is the raw f32 input (op applied), ws / tickets the tensor's stream workspace.
-struct StreamArgs {
-    const uint8_t* w;        // tile blobs (TileLayout)
-    float i8_scale;          // INT8 per-tensor scale
-    const uint32_t* row_ptr; // outlier CSR by row [N+1] (nullptr if none)
-    const uint2* ent;        // (col, f32 bits of v - dequant(q)), 2 pad entries at the end
-    const float* x;          // raw input rows (op.ld_x stride; 16-byte aligned)
-    PrepOp op;               // RMSNorm / SwiGLU fused into the preparation
-    float* y;                // [B][N]
-    const float* resid;      // nullptr, or [B][N] added to the result (y may alias it)
-    float* ws;               // [CTAs][2][128] partial sums of split row tiles
-    int* tickets;            // [nT] zero-initialised, self-resetting
-    int* err;
-    int N, K, B, nT, nkb, C; // C: CTAs (set by the launcher)
-};
-// Whether the stream kernel takes a GEMV of `B` rows of x over K columns (its x staging and ring fit
-// half an SM's shared memory).
-bool gemv_stream_fits(int kind, int B, int K, bool outliers);
-// Bytes of the stream workspace of a tensor with nT row tiles (partials, then the tickets).
-size_t gemv_stream_ws_bytes(int num_sms, int nT);
-cudaError_t launch_gemv_stream(int kind, const StreamArgs& a, int num_sms, bool pdl, cudaStream_t st);
-
 // Row-per-warp GEMV over the raw .pox layout (any even group size, any cols).
 struct GemvGenericArgs {
     const uint8_t* raw;

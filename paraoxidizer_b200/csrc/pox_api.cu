@@ -110,9 +110,7 @@ static void free_tensor_mem(pox_tensor* t) {
     cudaFree(t->tile_ptr);
     cudaFree(t->tile_ent);
     cudaFree(t->scratch);
-    cudaFree(t->stream_ws);
     t->scratch = nullptr;
-    t->stream_ws = nullptr;
     t->w = t->scales_dev = nullptr;
     t->row_ptr = nullptr;
     t->entries = nullptr;
@@ -444,11 +442,6 @@ int pox::upload_tensor_locked(pox_cuda_ctx* ctx, const pox_tensor_desc* d, pox_t
         CKF(cudaMalloc(&t->scratch, sb), "cudaMalloc(prepared x)");
         t->scratch_bytes = sb;
         t->bytes += sb;
-        const size_t wsb = gemv_stream_ws_bytes(ctx->num_sms, (int)((d->rows + 15) / 16));
-        CKF(cudaMalloc(&t->stream_ws, wsb), "cudaMalloc(stream workspace)");
-        CKF(cudaMemsetAsync(t->stream_ws, 0, wsb, st), "cudaMemset(stream workspace)");  // tickets start at 0
-        t->stream_ws_sms = ctx->num_sms;
-        t->bytes += wsb;
     }
     CKF(cudaStreamSynchronize(st), "cudaStreamSynchronize(upload)");
     cudaFree(tmp);
@@ -500,7 +493,6 @@ extern "C" int pox_cuda_tensor_info(const pox_tensor* t, size_t* rows, size_t* c
 }
 
 extern "C" const char* pox_cuda_tensor_gemv_kernel(const pox_tensor* t, size_t batch) {
-    if (t && gemv_uses_stream(t, batch)) return "gemv_stream_kernel";
     if (!t) return nullptr;
     if (!t->tiled) return "gemv_generic";
     if (batch == 0 || !gemv_uses_small_m(t, batch)) return "gemv_tc_kernel";
@@ -664,30 +656,9 @@ bool pox::gemv_uses_small_m(const pox_tensor* t, size_t batch) {
     return kind != kKindF16 && tq_below_9(t, kind, batch);
 }
 
-// Whether batch <= 8 GEMVs take the persistent stream kernel: POX_GEMV_STREAM=1 / 0 in the
-// environment (default: off, the per-row-tile GEMV).
-static bool stream_enabled() {
-    static const bool v = [] {
-        const char* s = getenv("POX_GEMV_STREAM");
-        return s && s[0] == '1';
-    }();
-    return v;
-}
-
-bool pox::gemv_uses_stream(const pox_tensor* t, size_t batch) {
-    if (!stream_enabled() || !t->tiled || !t->stream_ws || batch == 0 || gemv_uses_small_m(t, batch)) return false;
-    const int kind = t->dtype == POX_I4 ? kKindI4 : (t->dtype == POX_I8 ? kKindI8 : kKindF16);
-    const int b = (int)std::min<size_t>(batch, kMaxBatch);
-    return gemv_stream_fits(kind, b, (int)t->cols, t->nnz > 0) &&
-           (batch <= (size_t)kMaxBatch || gemv_stream_fits(kind, (int)((batch - 1) % kMaxBatch) + 1, (int)t->cols,
-                                                             t->nnz > 0));
-}
-
 int pox::gemv_x_target(pox_cuda_ctx* ctx, const pox_tensor* t, size_t batch, cudaStream_t st, XTarget* out) {
     *out = XTarget();
     if (!t->tiled || t->dtype != POX_I4 || t->cols % 128 != 0) return set_error(POX_ERR_UNSUPPORTED, "no prepared-x path");
-    if (gemv_uses_stream(t, batch))
-        return set_error(POX_ERR_UNSUPPORTED, "the stream GEMV prepares its own x");
     if (gemv_uses_small_m(t, batch)) {
         if (batch > 128) return set_error(POX_ERR_UNSUPPORTED, "prepared x holds up to 128 rows");
         int rc = ensure_tc_scratch(ctx, t->rows, t->cols, batch, st);
@@ -733,29 +704,7 @@ int pox::gemv_launch(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x, siz
         PrepOp opb = op;
         if (opb.up) opb.up += done * (size_t)opb.ld_up;
         cudaError_t e;
-        if (t->tiled && !prepared && t->stream_ws && gemv_uses_stream(t, batch)) {
-            const TileLayout TL(kind, N, K);
-            StreamArgs a = {};
-            a.w = (const uint8_t*)t->w;
-            a.i8_scale = t->i8_scale;
-            a.row_ptr = kind == kKindI4 ? t->row_ptr : nullptr;
-            a.ent = t->entries;
-            a.x = xb;
-            a.op = opb;
-            a.op.ld_x = (int)ldx;
-            a.y = yb;
-            a.resid = resid ? resid + done * t->rows : nullptr;
-            a.ws = static_cast<float*>(t->stream_ws);
-            a.tickets = reinterpret_cast<int*>(static_cast<char*>(t->stream_ws) +
-                                               (size_t)t->stream_ws_sms * 2 * 128 * sizeof(float));
-            a.err = ctx->err_dev;
-            a.N = N;
-            a.K = K;
-            a.B = (int)b;
-            a.nT = TL.nT;
-            a.nkb = TL.nkb;
-            e = launch_gemv_stream(kind, a, std::min(ctx->num_sms, t->stream_ws_sms), true, st);
-        } else if (t->tiled) {
+        if (t->tiled) {
             const TileLayout TL(kind, N, K);
             const XPrep xp = xprep_view(t->scratch, kind, K);
             if (!prepared) {
@@ -847,9 +796,8 @@ static int ensure_pinned(float** host, float** dev, size_t* have, size_t need) {
 
 // Host x in, host y out, synchronous. Caller holds ctx->mu.
 // Tiled tensors: x is copied into pinned staging on the host and from there by one DMA copy into
-// device memory (every CTA of the stream GEMV reads all of x, so it must not cross PCIe per CTA);
-// the GEMV writes y straight into pinned, device-mapped staging (each element once). One stream
-// sync. The raw-layout kernels get x and y in device memory.
+// device memory; the GEMV writes y straight into pinned, device-mapped staging (each element once).
+// One stream sync. The raw-layout kernels get x and y in device memory.
 static int gemv_host_locked(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x, size_t batch, float* y) {
     if (t->rows == 0 || t->cols == 0 || batch == 0) return POX_OK;
     const size_t xb = batch * t->cols * sizeof(float), yb = batch * t->rows * sizeof(float);

@@ -139,9 +139,8 @@ def test_small_m_agrees_with_gemv_path(be):
 
 
 def test_kernel_choice_by_batch(be):
-    """Which kernel serves a call: up to batch 8 the persistent stream GEMV when its prepared x
-    fits half an SM's shared memory (else the per-row-tile mma.sync GEMV), the integer tensor-core
-    path for INT8 and INT4 without outliers (padded batch <= 64), the f16 tiles otherwise;
+    """Which kernel serves a call: mma.sync GEMV up to batch 8, the integer tensor-core path for
+    INT8 and INT4 without outliers (padded batch <= 64), the f16 tiles otherwise;
     below batch 9 the integer path takes over where it was measured faster (INT4 with K >= 8192 from
     batch 6, INT8 with >= 16 M weights from batch 2)."""
     t4, _ = make(be, "i4", 256, 1024, 1)
@@ -149,16 +148,16 @@ def test_kernel_choice_by_batch(be):
     t8, _ = make(be, "i8", 256, 1024, 3)
     t4k, _ = make(be, "i4", 128, 8192, 4)
     t8big, _ = make(be, "i8", 4096, 4096, 5)
-    assert t4.gemv_kernel(8) in ("gemv_stream_kernel", "gemv_tc_kernel")
+    assert t4.gemv_kernel(8) == "gemv_tc_kernel"
     assert t4.gemv_kernel(16) == "gemm_tq_kernel"
     assert t4.gemv_kernel(64) == "gemm_tq_kernel"
     assert t4.gemv_kernel(65) == "gemm_tc05_kernel"
     assert t4o.gemv_kernel(16) == "gemm_tc05_kernel"
-    assert t8.gemv_kernel(4) in ("gemv_stream_kernel", "gemv_tc_kernel")
+    assert t8.gemv_kernel(4) == "gemv_tc_kernel"
     assert t8.gemv_kernel(64) == "gemm_tq_kernel"
     assert t8.gemv_kernel(65) == "gemm_tc05_kernel"
     assert [t4k.gemv_kernel(b) for b in (5, 6, 8)] == ["gemv_tc_kernel", "gemm_tq_kernel", "gemm_tq_kernel"]
-    assert t8big.gemv_kernel(1) in ("gemv_stream_kernel", "gemv_tc_kernel") and t8big.gemv_kernel(2) == "gemm_tq_kernel"
+    assert [t8big.gemv_kernel(b) for b in (1, 2)] == ["gemv_tc_kernel", "gemm_tq_kernel"]
     for t in (t4, t4o, t8, t4k, t8big):
         t.free()
 

@@ -373,8 +373,9 @@ DECODE_MODELS = {
 def decode_bench(be, cfg=LLAMA_8B, batches=(1, 8, 32), prefill=512, steps=256, warm=3, seed=0, world=1, rank=0,
                  modes=("peer", "nccl"), prefill_mode="tokens", outlier_sigma=None, name="llama-3-8b"):
     """Llama-3-8B-architecture INT4 g128 decode (random-init weights): prefill of `prefill` random
-    token ids fed token by token (the reference prefills through forward_token, engine.rs:760-762),
-    then `steps` greedy decode steps timed as CUDA-graph replays of one step on the device. With
+    token ids per sequence in passes of up to 256 rows (pox_cuda_model_prefill; the reference feeds
+    them token by token through forward_token, engine.rs:760-762), then `steps` greedy decode steps
+    timed as CUDA-graph replays of one step on the device. With
     world > 1 every rank holds a tensor-parallel shard and the step time is the max over ranks;
     each exchange implementation in `modes` is timed (the first is the default)."""
     import torch
@@ -385,8 +386,9 @@ def decode_bench(be, cfg=LLAMA_8B, batches=(1, 8, 32), prefill=512, steps=256, w
     runs = len(modes) if world > 1 else 1
     bps = (prefill + steps * runs + warm + 15) // 16
     t0 = time.perf_counter()
-    model = build_llama_on_device(be, cfg, max_b, max_b * bps, bps, seed=seed, tp_rank=rank, tp_size=world,
-                                  outlier_sigma=outlier_sigma)
+    # prefill passes take up to 256 rows (the KV cache is sized for the decode batches only)
+    model = build_llama_on_device(be, cfg, max(max_b, 256) if prefill_mode == "tokens" else max_b, max_b * bps, bps,
+                                  seed=seed, tp_rank=rank, tp_size=world, outlier_sigma=outlier_sigma)
     if world > 1:
         model.init_comm(modes=modes)
     build_s = time.perf_counter() - t0
@@ -406,8 +408,10 @@ def decode_bench(be, cfg=LLAMA_8B, batches=(1, 8, 32), prefill=512, steps=256, w
                 sq.sequence_len = prefill
             nxt = prompts[:, -1].astype(np.uint32)
         else:
-            for p in range(prefill):
-                _, nxt = model.decode(prompts[:, p], seqs, want_logits=False)
+            # the prompts through pox_cuda_model_prefill (tensor-core GEMMs over passes of 256 rows)
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            _, nxt = model.prefill([list(r) for r in prompts], seqs, want_logits=False)
         prefill_s = time.perf_counter() - t0
         for sq in seqs:
             sq.reserve(model.blocks, steps * runs + warm)
@@ -460,7 +464,7 @@ def decode_bench(be, cfg=LLAMA_8B, batches=(1, 8, 32), prefill=512, steps=256, w
     return {"model": f"{name} architecture, INT4 g128 projections (GPU quantizer"
                      + (f", {outlier_sigma}-sigma outliers" if outlier_sigma else "") + "), f16 embed/lm_head, "
                      "random-init N(0,0.02)", "kv": "fp16 pages of 16 tokens", "prefill": prefill,
-            "context": "prefill tokens fed one by one" if prefill_mode == "tokens" else
+            "context": "prompt through pox_cuda_model_prefill (passes of up to 256 rows)" if prefill_mode == "tokens" else
                        "pages reserved for the prefill length (no prefill compute)",
             "parallelism": f"tp{world}" if world > 1 else "single GPU",
             "bytes_per_step": "per GPU: its weight shard + its kv heads' pages (roofline = that / measured HBM peak)",

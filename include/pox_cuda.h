@@ -238,6 +238,18 @@ int pox_cuda_model_set_layer_tensors(pox_model* m, uint32_t layer, pox_tensor* q
  * to host memory when non-NULL. Synchronous. */
 int pox_cuda_model_decode(pox_model* m, uint32_t batch, const uint32_t* tokens, const uint32_t* positions,
                           const int32_t* block_tables, float* logits, uint32_t* next_tokens);
+/* Prefill: `rows` tokens through the model in one pass, replacing the token-by-token prefill of
+ * forward_sequence (crates/paraoxidizer-runtime/src/engine.rs:758-762). Row r feeds tokens[r] at
+ * positions[r] with its sequence's pages in block_tables[r * max_blocks_per_seq ..]; rows may belong
+ * to several sequences, and every row's k and v are written to the pages before any row attends, so
+ * each row attends to positions 0..positions[r] of its table, rows of the same pass included (the
+ * projections run as tensor-core GEMMs over the rows). logits [n_out][vocab] (this rank's slice) and
+ * the greedy next tokens [n_out] of rows out_rows[0 .. n_out) (typically each sequence's last
+ * prompt row) are written to host memory when non-NULL. rows <= max_batch (split longer prompts into
+ * passes: later passes see the pages earlier ones wrote). Synchronous. */
+int pox_cuda_model_prefill(pox_model* m, uint32_t rows, const uint32_t* tokens, const uint32_t* positions,
+                           const int32_t* block_tables, uint32_t n_out, const uint32_t* out_rows, float* logits,
+                           uint32_t* next_tokens);
 /* Device-pointer variant, asynchronous on `stream` (NULL: the context's stream). NULL inputs keep
  * the model's current device buffers (pox_cuda_model_buffers); advance != 0 then feeds the greedy
  * tokens back and increments the positions on the device, so consecutive calls decode greedily.

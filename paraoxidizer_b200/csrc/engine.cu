@@ -85,30 +85,34 @@ __device__ __forceinline__ float2 rope_pair(float a0, float a1, float c, float s
     return make_float2(__fsub_rn(__fmul_rn(a0, c), __fmul_rn(a1, s)), __fadd_rn(__fmul_rn(a0, s), __fmul_rn(a1, c)));
 }
 
+// What the attention kernels do besides attending: the decode step ropes q and appends the row's own
+// k and v; prefill ropes q over pages a separate kernel already filled for every row of the pass;
+// the kernel-level entry point takes q as given over filled pages.
+enum { kAttnDecode = 0, kAttnPrefill = 1, kAttnPlain = 2 };
+
 // q of the CTA's G query heads into shared memory (qs [8][HD]), rotated by RoPE (engine.rs:353-408)
-// from the model's (cos, sin) table when FUSED; with FUSED the CTA whose split holds position p also
-// rotates k and appends k and v to the page btab_row[p / 16], slot p % 16 (an entry outside
-// [0, kv_blocks) is reported and nothing is written). Without FUSED, q is taken as given and the
-// pages already hold every position attended (the kernel-level entry point).
-template <int HD, bool FUSED>
+// from the model's (cos, sin) table unless MODE is kAttnPlain; in kAttnDecode the CTA whose split
+// holds position p also rotates k and appends k and v to the page btab_row[p / 16], slot p % 16 (an
+// entry outside [0, kv_blocks) is reported and nothing is written).
+template <int HD, int MODE>
 __device__ __forceinline__ void load_q_append_kv(const float* row, uint32_t p, const int32_t* btab_row, int kv_blocks,
                                                  __half* kc, __half* vc, int layer, int L, int nq, int nkv, int h,
                                                  int G, const float2* rope, int t0, float* qs, int* err) {
     constexpr int DH = HD / 2;
     const int tid = threadIdx.x;
-    const float2* rp = FUSED ? rope + (size_t)p * DH : nullptr;  // (cos, sin) of the pairs at position p
+    const float2* rp = MODE != kAttnPlain ? rope + (size_t)p * DH : nullptr;  // (cos, sin) at position p
     for (int j = tid; j < G * DH; j += blockDim.x) {
         const int g = j / DH, i = j % DH;
         const float* q = row + (size_t)(h * G + g) * HD;
         float2 r = make_float2(q[2 * i], q[2 * i + 1]);
-        if (FUSED) {
+        if (MODE != kAttnPlain) {
             const float2 cs = rp[i];
             r = rope_pair(r.x, r.y, cs.x, cs.y);
         }
         qs[g * HD + 2 * i] = r.x;
         qs[g * HD + 2 * i + 1] = r.y;
     }
-    if (FUSED && (int)p < t0 + kSplitTok) {  // this split holds the new position: append k, v
+    if (MODE == kAttnDecode && (int)p < t0 + kSplitTok) {  // this split holds the new position: append k, v
         const int blk = btab_row[p / kPage];
         if (blk < 0 || blk >= kv_blocks) {
             if (h == 0 && tid == 0) atomicOr(err, kErrAttnPage);
@@ -134,7 +138,7 @@ __device__ __forceinline__ void load_q_append_kv(const float* row, uint32_t p, c
 // takes the 16 tokens of one page: two lanes per token read its K row (one half each) and the
 // warp reads the 16 V rows, all issued before any use; scores, the split's softmax partial and
 // sum_t p_t v_t follow. Writes (max, sum, acc[hd]) per query head for the combine kernel.
-template <int HD, bool FUSED>
+template <int HD, int MODE>
 __global__ void __launch_bounds__(128) attn_decode_kernel(const float* __restrict__ qkv, int qkv_rows,
                                                           const uint32_t* __restrict__ pos,
                                                           const int32_t* __restrict__ btab, int mbps, int kv_blocks,
@@ -162,7 +166,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const float* __restric
     __shared__ float red_m[4][8], red_l[4][8];
     __shared__ float acc_s[4][8][HD];
     const float* row = qkv + (size_t)b * qkv_rows;
-    load_q_append_kv<HD, FUSED>(row, p, btab + (size_t)b * mbps, kv_blocks, kc, vc, layer, L, nq, nkv, h, G,
+    load_q_append_kv<HD, MODE>(row, p, btab + (size_t)b * mbps, kv_blocks, kc, vc, layer, L, nq, nkv, h, G,
                                 rope, t0, &qs[0][0], err);
     __syncthreads();
 
@@ -314,7 +318,7 @@ __device__ __forceinline__ void split_f16x2(float x0, float x1, uint32_t& hi, ui
     lo = *reinterpret_cast<const uint32_t*>(&l);
 }
 
-template <int HD, bool FUSED>
+template <int HD, int MODE>
 __global__ void __launch_bounds__(128) attn_decode_tc_kernel(const float* __restrict__ qkv, int qkv_rows,
                                                              const uint32_t* __restrict__ pos,
                                                              const int32_t* __restrict__ btab, int mbps,
@@ -343,7 +347,7 @@ __global__ void __launch_bounds__(128) attn_decode_tc_kernel(const float* __rest
     __shared__ __align__(16) __half kv_s[2][4][16][RS];  // [K, V][warp][token][dim]; then the warps' outputs
     float (*acc_s)[8][HD] = reinterpret_cast<float (*)[8][HD]>(&kv_s[0][0][0][0]);
     const float* row = qkv + (size_t)b * qkv_rows;
-    load_q_append_kv<HD, FUSED>(row, p, btab + (size_t)b * mbps, kv_blocks, kc, vc, layer, L, nq, nkv, h, G,
+    load_q_append_kv<HD, MODE>(row, p, btab + (size_t)b * mbps, kv_blocks, kc, vc, layer, L, nq, nkv, h, G,
                                 rope, t0, &qs[0][0], err);
     __syncthreads();
 
@@ -628,9 +632,8 @@ __global__ void advance_kernel(uint32_t* tok, uint32_t* pos, const uint32_t* nex
     }
 }
 
-// Launch of the split-context attention kernels (decode step: FUSED = RoPE + KV append; the
-// kernel-level entry point: q as given over pages already filled). Tensor cores for head_dim 128
-// with 4..8 query heads per kv head, the FMA kernel otherwise.
+// Launch of the split-context attention kernels (MODE: kAttnDecode, kAttnPrefill or kAttnPlain).
+// Tensor cores for head_dim 128 with 4..8 query heads per kv head, the FMA kernel otherwise.
 struct AttnLaunch {
     const float* qkv = nullptr;
     int qkv_rows = 0;
@@ -644,22 +647,67 @@ struct AttnLaunch {
     float* apart = nullptr;
     int* err = nullptr;
 };
-template <bool FUSED>
+template <int MODE>
 static cudaError_t launch_attention_t(const AttnLaunch& a, int B, cudaStream_t st) {
     const dim3 grid(a.max_splits, a.nkv, B), block(128);
     if (a.hd == 128)
-        return launch_pdl(a.G >= 4 ? attn_decode_tc_kernel<128, FUSED> : attn_decode_kernel<128, FUSED>, grid, block,
+        return launch_pdl(a.G >= 4 ? attn_decode_tc_kernel<128, MODE> : attn_decode_kernel<128, MODE>, grid, block,
                           0, st, a.qkv, a.qkv_rows, a.pos, a.btab, a.mbps, a.kv_blocks, a.kc, a.vc, a.layer, a.L, a.nq,
                           a.nkv, a.G, a.max_splits, a.rope, a.apart, a.err);
     if (a.hd == 64)
-        return launch_pdl(attn_decode_kernel<64, FUSED>, grid, block, 0, st, a.qkv, a.qkv_rows, a.pos, a.btab, a.mbps,
+        return launch_pdl(attn_decode_kernel<64, MODE>, grid, block, 0, st, a.qkv, a.qkv_rows, a.pos, a.btab, a.mbps,
                           a.kv_blocks, a.kc, a.vc, a.layer, a.L, a.nq, a.nkv, a.G, a.max_splits, a.rope, a.apart,
                           a.err);
-    return launch_pdl(attn_decode_kernel<32, FUSED>, grid, block, 0, st, a.qkv, a.qkv_rows, a.pos, a.btab, a.mbps,
+    return launch_pdl(attn_decode_kernel<32, MODE>, grid, block, 0, st, a.qkv, a.qkv_rows, a.pos, a.btab, a.mbps,
                       a.kv_blocks, a.kc, a.vc, a.layer, a.L, a.nq, a.nkv, a.G, a.max_splits, a.rope, a.apart, a.err);
 }
-static cudaError_t launch_attention(const AttnLaunch& a, int B, bool fused, cudaStream_t st) {
-    return fused ? launch_attention_t<true>(a, B, st) : launch_attention_t<false>(a, B, st);
+static cudaError_t launch_attention(const AttnLaunch& a, int B, int mode, cudaStream_t st) {
+    if (mode == kAttnDecode) return launch_attention_t<kAttnDecode>(a, B, st);
+    if (mode == kAttnPrefill) return launch_attention_t<kAttnPrefill>(a, B, st);
+    return launch_attention_t<kAttnPlain>(a, B, st);
+}
+
+// Prefill: every row's k (rotated at its position) and v appended to its page before any row attends,
+// so rows of one sequence in the same pass see each other causally. Block (kv head, row); thread i =
+// RoPE pair i (engine.rs:383-390 order), the arithmetic of load_q_append_kv's append.
+__global__ void kv_append_kernel(const float* __restrict__ qkv, int qkv_rows, const uint32_t* __restrict__ pos,
+                                 const int32_t* __restrict__ btab, int mbps, int kv_blocks, __half* __restrict__ kc,
+                                 __half* __restrict__ vc, int layer, int L, int nq, int nkv, int hd,
+                                 const float2* __restrict__ rope, int* __restrict__ err) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int h = blockIdx.x, b = blockIdx.y, half = hd / 2;
+    const uint32_t p = pos[b];
+    if (p >= (uint32_t)mbps * kPage) {
+        if (h == 0 && threadIdx.x == 0) atomicOr(err, kErrAttnPos);
+        return;
+    }
+    const int blk = btab[(size_t)b * mbps + p / kPage];
+    if (blk < 0 || blk >= kv_blocks) {
+        if (h == 0 && threadIdx.x == 0) atomicOr(err, kErrAttnPage);
+        return;
+    }
+    const float* row = qkv + (size_t)b * qkv_rows;
+    const float* k = row + (size_t)(nq + h) * hd;
+    const float* v = row + (size_t)(nq + nkv + h) * hd;
+    const float2* rp = rope + (size_t)p * half;
+    const size_t off = ((((size_t)blk * L + layer) * nkv + h) * kPage + p % kPage) * hd;
+    for (int i = threadIdx.x; i < half; i += blockDim.x) {
+        const float2 cs = rp[i];
+        const float2 r = rope_pair(k[2 * i], k[2 * i + 1], cs.x, cs.y);
+        *reinterpret_cast<__half2*>(kc + off + 2 * i) = __floats2half2_rn(r.x, r.y);
+        *reinterpret_cast<__half2*>(vc + off + 2 * i) = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
+    }
+}
+
+// Rows sel[j] of x gathered into out [n][H] (the rows prefill returns logits for).
+__global__ void gather_rows_kernel(const float* __restrict__ x, const uint32_t* __restrict__ sel, int H,
+                                   float* __restrict__ out) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const float* src = x + (size_t)sel[blockIdx.x] * H;
+    float* dst = out + (size_t)blockIdx.x * H;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) dst[i] = src[i];
 }
 
 static void destroy_model(pox_model* m);
@@ -760,8 +808,11 @@ static int row_split_gemv(pox_model* m, const pox_tensor* t, const float* xin, i
     return comm_allreduce(m->comm, call, 2 * m->L + 1, m->x, (size_t)B * m->H, st);
 }
 
-// The decode step on device buffers already filled (m->tok, m->pos, m->btab).
-static int decode_step(pox_model* m, int B, cudaStream_t st) {
+// One pass of B rows through the model on device buffers already filled (m->tok, m->pos, m->btab).
+// Decode: each row appends its own k / v inside the attention kernel; logits of every row.
+// Prefill (n_out > 0): every row's k / v is appended before the attention of the layer, so rows of
+// one sequence see each other causally; logits only of the n_out rows listed in m->sel.
+static int forward_step(pox_model* m, int B, cudaStream_t st, bool prefill, int n_out) {
     pox_cuda_ctx* ctx = m->ctx;
     int rc;
     if (m->comm.tp > 1 && !m->comm.mode) return set_error(POX_ERR_INVALID, "tensor-parallel exchange not set up");
@@ -795,7 +846,13 @@ static int decode_step(pox_model* m, int B, cudaStream_t st) {
         al.rope = m->rope;
         al.apart = m->apart;
         al.err = ctx->err_dev;
-        cudaError_t e = launch_attention(al, B, true, st);
+        cudaError_t e = cudaSuccess;
+        if (prefill)
+            e = launch_pdl(kv_append_kernel, dim3(m->nkv, B), dim3(64), 0, st, (const float*)m->qkv, m->qkv_rows,
+                           (const uint32_t*)m->pos, (const int32_t*)m->btab, (int)m->max_blocks_per_seq,
+                           (int)m->kv_blocks, m->kc, m->vc, l, m->L, m->nq, m->nkv, m->hd, (const float2*)m->rope,
+                           ctx->err_dev);
+        if (e == cudaSuccess) e = launch_attention(al, B, prefill ? kAttnPrefill : kAttnDecode, st);
         if (e != cudaSuccess) return cuda_error(e, "attention launch");
         // the combine writes the o projection's prepared input when that tensor takes one
         OPrep op;
@@ -829,7 +886,15 @@ static int decode_step(pox_model* m, int B, cudaStream_t st) {
         if ((rc = row_split_gemv(m, w.down, m->gu, B, 2 * l + 1, &sw, st))) return rc;
     }
     norm.norm_w = m->final_norm;
-    if ((rc = gemv_launch(ctx, m->lm_head, m->x, B, m->logits, st, &norm))) return rc;
+    const float* xh = m->x;
+    if (prefill) {
+        le = launch_pdl(gather_rows_kernel, dim3(n_out), dim3(256), 0, st, (const float*)m->x, (const uint32_t*)m->sel,
+                        m->H, m->xsel);
+        if (le != cudaSuccess) return cuda_error(le, "gather launch");
+        xh = m->xsel;
+        B = n_out;
+    }
+    if ((rc = gemv_launch(ctx, m->lm_head, xh, B, m->logits, st, &norm))) return rc;
     const int parts = std::min(kArgmaxParts, (m->V + 2047) / 2048);
     const int chunk = (m->V + parts - 1) / parts;
     le = launch_pdl(argmax_part_kernel, dim3(parts, B), dim3(256), 0, st, m->logits, m->V, chunk, m->amax);
@@ -912,6 +977,8 @@ extern "C" int pox_cuda_model_create_tp(pox_cuda_ctx* ctx, const pox_llama_confi
         {(void**)&m->next, B * 4},
         {(void**)&m->btab, B * max_blocks_per_seq * 4},
         {(void**)&m->rope, (size_t)max_blocks_per_seq * kPage * (m->hd / 2) * sizeof(float2)},
+        {(void**)&m->sel, B * 4},
+        {(void**)&m->xsel, B * m->H * 4},
     };
     for (auto& a : allocs) {
         e = cudaMalloc(a.p, a.bytes);
@@ -971,7 +1038,7 @@ static void destroy_model(pox_model* m) {
     }
     free_tensor(ctx, m->lm_head);
     void* bufs[] = {m->embed, m->final_norm, m->kc, m->vc, m->x, m->qkv, m->att, m->gu, m->logits, m->apart,
-                    m->amax, m->tok, m->pos, m->next, m->btab, m->rope};
+                    m->amax, m->tok, m->pos, m->next, m->btab, m->rope, m->sel, m->xsel};
     for (void* p : bufs) cudaFree(p);
     comm_free(m->comm);
     delete m;
@@ -1095,7 +1162,7 @@ extern "C" int pox_cuda_model_decode_device(pox_model* m, uint32_t batch, const 
         cudaMemcpyAsync(m->pos, positions_dev, B * 4, cudaMemcpyDeviceToDevice, st);
     if (block_tables_dev && block_tables_dev != m->btab)
         cudaMemcpyAsync(m->btab, block_tables_dev, B * m->max_blocks_per_seq * 4, cudaMemcpyDeviceToDevice, st);
-    int rc = decode_step(m, (int)batch, st);
+    int rc = forward_step(m, (int)batch, st, false, 0);
     if (rc) return rc;
     if (logits_dev) cudaMemcpyAsync(logits_dev, m->logits, B * m->V * 4, cudaMemcpyDeviceToDevice, st);
     if (next_dev) cudaMemcpyAsync(next_dev, m->next, B * 4, cudaMemcpyDeviceToDevice, st);
@@ -1136,12 +1203,57 @@ extern "C" int pox_cuda_model_decode(pox_model* m, uint32_t batch, const uint32_
         e = cudaMemcpyAsync(m->btab, block_tables, B * m->max_blocks_per_seq * 4, cudaMemcpyHostToDevice, st);
     if (e != cudaSuccess) return cuda_error(e, "cudaMemcpy(decode inputs)");
     int rc = comm_reset(m->comm, st);
-    if (!rc) rc = decode_step(m, (int)batch, st);
+    if (!rc) rc = forward_step(m, (int)batch, st, false, 0);
     if (rc) return rc;
     if (logits) e = cudaMemcpyAsync(logits, m->logits, B * m->V * 4, cudaMemcpyDeviceToHost, st);
     if (e == cudaSuccess && next_tokens) e = cudaMemcpyAsync(next_tokens, m->next, B * 4, cudaMemcpyDeviceToHost, st);
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     if (e != cudaSuccess) return cuda_error(e, "decode step");
+    return take_kernel_error(ctx);
+}
+
+extern "C" int pox_cuda_model_prefill(pox_model* m, uint32_t rows, const uint32_t* tokens, const uint32_t* positions,
+                                      const int32_t* block_tables, uint32_t n_out, const uint32_t* out_rows,
+                                      float* logits, uint32_t* next_tokens) {
+    if (!m) return set_error(POX_ERR_INVALID, "model is NULL");
+    if (rows == 0) return POX_OK;
+    if (!tokens || !positions || !block_tables || (n_out && !out_rows)) return set_error(POX_ERR_INVALID, "NULL input");
+    if (rows > m->max_batch) return set_error(POX_ERR_INVALID, "%u rows > max_batch %u (split the pass)", rows, m->max_batch);
+    if (n_out == 0 || n_out > rows) return set_error(POX_ERR_INVALID, "n_out %u must be in 1..rows", n_out);
+    if (!m->embed || !m->lm_head) return set_error(POX_ERR_INVALID, "embeddings not set");
+    for (uint32_t j = 0; j < n_out; j++)
+        if (out_rows[j] >= rows) return set_error(POX_ERR_INVALID, "out_rows[%u] = %u >= rows", j, out_rows[j]);
+    for (uint32_t b = 0; b < rows; b++) {
+        const uint32_t nb = positions[b] / kPage + 1;
+        if (nb > m->max_blocks_per_seq)
+            return set_error(POX_ERR_OOM, "position %u needs %u KV blocks, max_blocks_per_seq is %u", positions[b], nb,
+                             m->max_blocks_per_seq);
+        for (uint32_t j = 0; j < nb; j++) {
+            const int32_t blk = block_tables[(size_t)b * m->max_blocks_per_seq + j];
+            if (blk < 0 || (uint32_t)blk >= m->kv_blocks)
+                return set_error(POX_ERR_INVALID, "block table entry %d of row %u out of range", blk, b);
+        }
+    }
+    pox_cuda_ctx* ctx = m->ctx;
+    std::lock_guard<std::mutex> lk(ctx->mu);
+    cudaError_t e = cudaSetDevice(ctx->device);
+    if (e != cudaSuccess) return cuda_error(e, "cudaSetDevice");
+    cudaStream_t st = ctx->stream;
+    const size_t B = rows;
+    e = cudaMemcpyAsync(m->tok, tokens, B * 4, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(m->pos, positions, B * 4, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess)
+        e = cudaMemcpyAsync(m->btab, block_tables, B * m->max_blocks_per_seq * 4, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(m->sel, out_rows, (size_t)n_out * 4, cudaMemcpyHostToDevice, st);
+    if (e != cudaSuccess) return cuda_error(e, "cudaMemcpy(prefill inputs)");
+    int rc = comm_reset(m->comm, st);
+    if (!rc) rc = forward_step(m, (int)rows, st, true, (int)n_out);
+    if (rc) return rc;
+    if (logits) e = cudaMemcpyAsync(logits, m->logits, (size_t)n_out * m->V * 4, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess && next_tokens)
+        e = cudaMemcpyAsync(next_tokens, m->next, (size_t)n_out * 4, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess) return cuda_error(e, "prefill");
     return take_kernel_error(ctx);
 }
 
@@ -1286,7 +1398,7 @@ extern "C" int pox_cuda_paged_attention(pox_cuda_ctx* ctx, const float* q_dev, c
     al.btab = block_tables_dev;
     al.mbps = (int)max_blocks_per_seq;
     al.kv_blocks = (int)num_blocks;
-    al.kc = reinterpret_cast<__half*>(const_cast<uint16_t*>(k_pages_dev));  // read only without FUSED
+    al.kc = reinterpret_cast<__half*>(const_cast<uint16_t*>(k_pages_dev));  // read only in kAttnPlain
     al.vc = reinterpret_cast<__half*>(const_cast<uint16_t*>(v_pages_dev));
     al.layer = 0;
     al.L = 1;
@@ -1297,7 +1409,7 @@ extern "C" int pox_cuda_paged_attention(pox_cuda_ctx* ctx, const float* q_dev, c
     al.max_splits = max_splits;
     al.apart = apart;
     al.err = ctx->err_dev;
-    e = launch_attention(al, (int)batch, false, st);
+    e = launch_attention(al, (int)batch, kAttnPlain, st);
     if (e != cudaSuccess) return cuda_error(e, "attention launch");
     e = launch_pdl(attn_combine_kernel, dim3((heads * head_dim + 127) / 128, batch), dim3(128), 0, st, positions_dev,
                    (uint32_t)(max_blocks_per_seq * kPage), (int)heads, (int)kv_heads, G, (int)head_dim, max_splits,

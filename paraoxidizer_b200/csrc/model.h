@@ -53,6 +53,8 @@ struct pox_model {
     uint32_t* pos = nullptr;  // [B]
     uint32_t* next = nullptr; // [B]
     int32_t* btab = nullptr;  // [B][max_blocks_per_seq]
+    uint32_t* sel = nullptr;  // [B] prefill: rows whose logits are returned
+    float* xsel = nullptr;    // [B][H] prefill: those rows of x
     int max_splits = 0;
     pox::TpComm comm;
 };

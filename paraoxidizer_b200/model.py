@@ -175,6 +175,42 @@ class CudaModel:
                                               None if logits is None else logits.ctypes.data, nxt.ctypes.data))
         return logits, nxt
 
+    def prefill(self, prompts: Sequence[Sequence[int]], seqs: Sequence[BlockTable], want_logits: bool = True):
+        """Feeds each sequence's prompt tokens at its next positions in passes of up to max_batch rows
+        (pox_cuda_model_prefill; the tensor-core GEMMs see all rows of a pass at once). Returns the
+        logits of each sequence's last prompt token ([n_seq][vocab / tp_size], or None) and the greedy
+        next tokens, like forward_token on the last prompt token (engine.rs:758-762)."""
+        assert len(prompts) == len(seqs) and len(seqs) > 0
+        rows = []  # (sequence, token, position)
+        for i, (p, s) in enumerate(zip(prompts, seqs)):
+            for tok in p:
+                rows.append((i, int(tok), s.sequence_len))
+                s.append_token(self.blocks)
+        last = {}
+        for r, (i, _, _) in enumerate(rows):
+            last[i] = r
+        n = len(seqs)
+        logits = np.zeros((n, self.vocab_local), np.float32) if want_logits else None
+        nxt = np.zeros(n, np.uint32)
+        lib = L.lib()
+        for c0 in range(0, len(rows), self.max_batch):
+            chunk = rows[c0:c0 + self.max_batch]
+            tok = np.array([t for _, t, _ in chunk], np.uint32)
+            pos = np.array([p for _, _, p in chunk], np.uint32)
+            tab = np.stack([seqs[i].as_array(self.max_blocks_per_seq) for i, _, _ in chunk]).astype(np.int32)
+            outs = [(i, r - c0) for i, r in last.items() if c0 <= r < c0 + len(chunk)]
+            sel = np.array([r for _, r in outs] or [len(chunk) - 1], np.uint32)
+            lg = np.zeros((len(sel), self.vocab_local), np.float32)
+            nx = np.zeros(len(sel), np.uint32)
+            L.check(lib.pox_cuda_model_prefill(self.handle, len(chunk), tok.ctypes.data, pos.ctypes.data,
+                                               tab.ctypes.data, len(sel), sel.ctypes.data,
+                                               lg.ctypes.data if want_logits else None, nx.ctypes.data))
+            for j, (i, _) in enumerate(outs):
+                nxt[i] = nx[j]
+                if want_logits:
+                    logits[i] = lg[j]
+        return logits, nxt
+
     def set_state(self, tokens, seqs: Sequence[BlockTable]) -> None:
         """Loads tokens, the sequences' next positions and their block tables into the device
         buffers (pox_cuda_model_set_state) for decode_device steps."""

@@ -147,6 +147,41 @@ def test_decode_llama8b_widths(be, llama8b_2l, nseq):
     assert total > 0 and agree == total, (agree, total)
 
 
+@pytest.mark.parametrize("name,max_batch", [("l8", 96), ("l8", 16), ("l70", 64), ("hd64", 32), ("fixture", 40)])
+def test_prefill_matches_forward_token(be, name, max_batch):
+    """Prompts fed in passes of up to max_batch rows (rows of several sequences together, a sequence
+    split across passes when max_batch is small) give the last prompt token's logits of the oracle's
+    token-by-token forward_token; decode steps continue from the pages prefill wrote."""
+    cfg = CONFIGS[name]
+    w = make_llama(cfg, seed=12, outlier_policy="automatic", norm_jitter=0.1)
+    model = CudaModel(be, cfg, max_batch=max_batch, kv_blocks=48, max_blocks_per_seq=16)
+    load_into(model, w)
+    ow = oracle_weights(w)
+    rng = np.random.default_rng(9)
+    prompts = [list(int(t) for t in rng.integers(0, cfg["vocab"], n)) for n in (5, 70, 19)]
+    oracles = [O.OracleModel(cfg, ow, max_seq=256, kv_f16=True) for _ in prompts]
+    seqs = [model.new_sequence() for _ in prompts]
+    logits, nxt = model.prefill(prompts, seqs)
+    feeds = []
+    for i, p in enumerate(prompts):
+        for t, tok in enumerate(p):
+            ref = oracles[i].forward_token(tok, t)
+        err = float(np.max(np.abs(logits[i] - ref)))
+        assert err <= E2E_TOL, (name, i, err)
+        top = np.sort(ref)[-2:]
+        if top[1] - top[0] > E2E_TOL:
+            assert int(nxt[i]) == int(np.argmax(ref))
+        feeds.append(int(np.argmax(ref)))
+    for step in range(4):  # decode continues over the prefilled pages
+        pos = [len(p) + step for p in prompts]
+        lg, nx = model.decode(feeds, seqs)
+        for i in range(3):
+            ref = oracles[i].forward_token(feeds[i], pos[i])
+            assert float(np.max(np.abs(lg[i] - ref))) <= E2E_TOL, (name, i, step)
+            feeds[i] = int(np.argmax(ref))
+    model.close()
+
+
 def test_decode_from_pox_file(be, tmp_path):
     """The model read from a .pox file (pox_cuda_model_load over the C++ container reader: mmap,
     tensor index, one verify_integrity) decodes like forward_token on the same weights."""

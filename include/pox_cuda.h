@@ -192,6 +192,18 @@ int pox_cuda_tensor_gemv_ex(pox_cuda_ctx* ctx, const pox_tensor* t, const float*
  * Asynchronous on `stream` (NULL: the context's stream). */
 int pox_cuda_quantize_int4(pox_cuda_ctx* ctx, const float* w_dev, size_t numel, size_t group_size,
                            uint8_t* packed_dev, uint8_t* scales_dev, void* stream);
+/* extract_and_zero_outliers (crates/paraoxidizer-quant/src/outlier.rs:57-85) on the GPU, bit-exact:
+ * the mean and the variance sum are the reference's sequential f32 sums in index order (one thread,
+ * IEEE round-to-nearest adds, the square a separate multiply), std = sqrt(var_sum / n), threshold =
+ * sigma * std; every element with |w - mean| > threshold (strict) goes, in ascending index order, into
+ * the .pox outlier table (count:u32 | indices:u32[count] | f16 values rounded to nearest even,
+ * outlier.rs:99-110) and is zeroed in w_dev (device, n floats). sigma is the policy's multiplier
+ * (Conservative 4.5, Automatic 3.5, Aggressive 2.8; outlier.rs:9-35). The table goes to host memory
+ * `table` (table_cap bytes); *table_len = its length, 0 where the reference returns None (no outlier
+ * or n == 0). A buffer too small: nothing is modified, *table_len is set, POX_ERR_LAYOUT. n <= 2^32.
+ * Synchronous; the two sums take about 4 ns per element. */
+int pox_cuda_extract_outliers(pox_cuda_ctx* ctx, float* w_dev, size_t n, float sigma, uint8_t* table,
+                              size_t table_cap, size_t* table_len);
 /* Dequantizes a resident tensor into out_dev ([rows][cols] f32, device), bit-exact with
  * dequantize_int4_group / dequantize_int8_symmetric (kernels.rs:85-128,157-173) followed by
  * SparseOutlierTable::apply_to (outlier.rs:88-95). Asynchronous on `stream`. */

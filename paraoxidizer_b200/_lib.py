@@ -109,6 +109,7 @@ def _declare(L):
         "pox_cuda_model_destroy": (None, [vp]),
         "pox_cuda_model_set_layer_tensors": (i32, [vp, u32, vp, vp, vp, vp, vp, vp]),
         "pox_cuda_quantize_int4": (i32, [vp, vp, sz, sz, vp, vp, vp]),
+        "pox_cuda_extract_outliers": (i32, [vp, vp, sz, C.c_float, vp, sz, C.POINTER(sz)]),
         "pox_cuda_model_set_embeddings": (i32, [vp, vp, vp, vp]),
         "pox_cuda_model_set_layer": (i32, [vp, u32, C.POINTER(TensorDesc), vp, vp]),
         "pox_cuda_model_decode": (i32, [vp, u32, vp, vp, vp, vp, vp]),

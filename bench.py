@@ -312,7 +312,11 @@ def batched_gemv_bench(be, batches=(1, 4, 16, 64), reps=400):
     q8, s8 = Q.quantize_int8_symmetric(w8)
     cases.append(("int8_14336x4096", 14336, 4096, [be.upload_int8(q8, s8, 14336, 4096) for _ in range(6)],
                   14336 * 4096 + 4))
-    del w8, q8
+    # the configuration as worded: one f16 scale per output row (the per-channel extension)
+    q8r, s8r = Q.quantize_int8_rows(w8, 14336, 4096)
+    cases.append(("int8_rowscale_14336x4096", 14336, 4096,
+                  [be.upload_int8_rows(q8r, s8r, 14336, 4096) for _ in range(6)], 14336 * 4096 + 2 * 14336))
+    del w8, q8, q8r
     packed, scales, tab, ob, _ = make_workload(seed=3)
     cases.append(("int4_g128_4096x14336", ROWS, COLS,  # the decode weights' format: no outlier table
                   [be.upload_int4(packed, scales, ROWS, COLS, GS) for _ in range(8)],

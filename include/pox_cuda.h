@@ -111,7 +111,10 @@ int pox_cuda_gemv_int8(pox_cuda_ctx* ctx, const uint8_t* q_weights, size_t q_len
 typedef struct {
     int dtype;            /* POX_I4, POX_I8 or POX_F16 */
     size_t rows, cols;    /* shape [rows, cols] (meta.shape.dims()[0..2]) */
-    size_t group_size;    /* INT4 group size (meta.group_size), ignored otherwise */
+    size_t group_size;    /* INT4: group size (meta.group_size). INT8: 0 = the .pox layout, one f32
+                             per-tensor scale (kernels.rs:131-154); 1 = an extension with one f16 scale
+                             per output row (scales = rows x 2 bytes LE; the reference's rules applied per
+                             row: max_abs / 127 rounded to f16, q = round(w / that scale)). F16: ignored. */
     const uint8_t* data;  size_t data_len;
     const uint8_t* scales; size_t scale_len;   /* may be NULL for F16 */
     const uint8_t* outliers; size_t outlier_len; /* may be NULL; ignored for I8 (engine.rs:232) */

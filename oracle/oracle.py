@@ -68,6 +68,11 @@ def lib():
                                            _sz, _f32p, _sz, _f32p, _sz, C.c_int]
         L.pox_oracle_gemv_int8.restype = C.c_int
         L.pox_oracle_gemv_int8.argtypes = [_u8p, _sz, _u8p, _sz, _sz, _sz, _f32p, _sz, _f32p, _sz]
+        L.pox_oracle_quantize_int8_rows.argtypes = [_f32p, _sz, _sz, _u8p, _u8p]
+        L.pox_oracle_dequantize_int8_rows.restype = C.c_int
+        L.pox_oracle_dequantize_int8_rows.argtypes = [_u8p, _sz, _sz, _u8p, _sz, _f32p]
+        L.pox_oracle_gemv_int8_rows.restype = C.c_int
+        L.pox_oracle_gemv_int8_rows.argtypes = [_u8p, _sz, _sz, _u8p, _sz, _f32p, _f32p]
         L.pox_oracle_gemv_f16.argtypes = [_u16p, _sz, _sz, _f32p, _f32p]
         L.pox_oracle_rms_norm.argtypes = [_f32p, _sz, C.c_void_p, C.c_float]
         L.pox_oracle_rope.argtypes = [_f32p, _sz, _f32p, _sz, _sz, _sz, C.c_float]
@@ -140,6 +145,36 @@ def dequantize_int8_symmetric(q, scales) -> np.ndarray:
     if lib().pox_oracle_dequantize_int8_symmetric(q, q.size, s, s.size, out, out.size) != 0:
         raise ValueError("dequantize_int8_symmetric: Err")
     return out[: q.size]
+
+
+def quantize_int8_rows(weights, rows: int, cols: int):
+    """Per-output-channel INT8 (the extension: the reference's rules per row, f16 row scales)
+    -> (q bytes, rows x 2 bytes of f16 scales)."""
+    w = _c(weights, np.float32).ravel()
+    q = np.zeros(max(w.size, 1), np.uint8)
+    s = np.zeros(max(2 * rows, 1), np.uint8)
+    lib().pox_oracle_quantize_int8_rows(w, rows, cols, q, s)
+    return q[: w.size].copy(), s[: 2 * rows].copy()
+
+
+def dequantize_int8_rows(q, scales, rows: int, cols: int) -> np.ndarray:
+    q = _c(q, np.uint8)
+    s = _c(scales, np.uint8)
+    out = np.zeros(max(rows * cols, 1), np.float32)
+    if lib().pox_oracle_dequantize_int8_rows(q, rows, cols, s, s.size, out) != 0:
+        raise ValueError("dequantize_int8_rows: scales too short")
+    return out[: rows * cols]
+
+
+def gemv_int8_rows(q, scales, rows: int, cols: int, x) -> np.ndarray:
+    """gemv_int8's arithmetic (kernels.rs:229-255) with the row's own f16 scale."""
+    q = _c(q, np.uint8)
+    s = _c(scales, np.uint8)
+    x = _c(x, np.float32)
+    y = np.zeros(rows, np.float32)
+    if lib().pox_oracle_gemv_int8_rows(q, rows, cols, s, s.size, x, y) != 0:
+        raise ValueError("gemv_int8_rows: scales too short")
+    return y
 
 
 def dot_product_simd(a, b, neon: bool = False) -> float:

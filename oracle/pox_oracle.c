@@ -211,6 +211,57 @@ int pox_oracle_dequantize_int8_symmetric(const uint8_t* q, size_t n, const uint8
     return ORACLE_OK;
 }
 
+/* Per-output-channel INT8 (the extension BASELINE-style configurations ask for; the reference's .pox
+ * INT8 is per tensor, kernels.rs:131-154): the reference's rules applied to each row -- max_abs of the
+ * row (floor 1e-4 below 1e-8), scale = max_abs / 127 (f32), stored as f16 (round to nearest even);
+ * q = round(w / s) clamped to +-127 with s = the f16 scale read back as f32, so that q * s is the
+ * value the stored table dequantizes to. scale_out: rows x 2 bytes LE. */
+void pox_oracle_quantize_int8_rows(const float* w, size_t rows, size_t cols, uint8_t* q_out, uint8_t* scale_out) {
+    for (size_t r = 0; r < rows; r++) {
+        const float* wr = w + r * cols;
+        float max_abs = 0.0f;
+        for (size_t c = 0; c < cols; c++) {
+            float a = fabsf(wr[c]);
+            if (a > max_abs) max_abs = a;
+        }
+        if (max_abs < 1e-8f) max_abs = 1e-4f;
+        const uint16_t sh = pox_oracle_f32_to_f16(max_abs / 127.0f);
+        const float s = pox_oracle_f16_to_f32(sh);
+        for (size_t c = 0; c < cols; c++)
+            q_out[r * cols + c] = (uint8_t)(int8_t)rust_round_clamp_cast(wr[c] / s, -127.0f, 127.0f);
+        wr_u16(scale_out + 2 * r, sh);
+    }
+}
+
+/* dequantization of the per-row layout: q * scale_r (one f32 multiply, as dequantize_int8_symmetric). */
+int pox_oracle_dequantize_int8_rows(const uint8_t* q, size_t rows, size_t cols, const uint8_t* scale_data,
+                                    size_t scale_len, float* out) {
+    if (scale_len < 2 * rows) return ORACLE_ERR;
+    for (size_t r = 0; r < rows; r++) {
+        const float s = pox_oracle_f16_to_f32(rd_u16(scale_data + 2 * r));
+        for (size_t c = 0; c < cols; c++) out[r * cols + c] = (float)(int8_t)q[r * cols + c] * s;
+    }
+    return ORACLE_OK;
+}
+
+/* gemv_int8's arithmetic (kernels.rs:229-255: sum += ((q as f32) * scale) * x[c], sequential per row)
+ * with the row's own scale. */
+int pox_oracle_gemv_int8_rows(const uint8_t* q, size_t rows, size_t cols, const uint8_t* scale_data,
+                              size_t scale_len, const float* x, float* y) {
+    if (scale_len < 2 * rows) return ORACLE_ERR;
+    for (size_t r = 0; r < rows; r++) {
+        const uint8_t* qr = q + r * cols;
+        const float s = pox_oracle_f16_to_f32(rd_u16(scale_data + 2 * r));
+        float sum = 0.0f;
+        for (size_t c = 0; c < cols; c++) {
+            float t = (float)(int8_t)qr[c] * s;
+            sum += t * x[c];
+        }
+        y[r] = sum;
+    }
+    return ORACLE_OK;
+}
+
 /* kernels.rs:293-316 dot_product_simd, non-aarch64 order: four strided accumulators summed
  * as ((s0+s1)+s2)+s3, then the scalar tail. */
 float pox_oracle_dot_x86(const float* a, const float* b, size_t len) {

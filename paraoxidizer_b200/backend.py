@@ -183,5 +183,9 @@ class CudaBackend:
     def upload_int8(self, q, scale, rows, cols) -> ResidentTensor:
         return self.upload(L.POX_I8, rows, cols, q, scale)
 
+    def upload_int8_rows(self, q, row_scales, rows, cols) -> ResidentTensor:
+        """INT8 with one f16 scale per output row (quant.quantize_int8_rows), the per-channel extension."""
+        return self.upload(L.POX_I8, rows, cols, q, row_scales, None, 1)
+
     def upload_f16(self, w_bits, rows, cols) -> ResidentTensor:
         return self.upload(L.POX_F16, rows, cols, w_bits)

@@ -18,6 +18,7 @@ struct pox_tensor {
     void* w = nullptr;         // tiles or raw payload
     void* scales_dev = nullptr;   // tiled INT4: scale words per tile; raw INT4: the .pox scale bytes
     float i8_scale = 0.f;
+    float* row_scales = nullptr;  // INT8 per-output-channel scales [rows] (f32 of the f16 table), or nullptr
     uint32_t* row_ptr = nullptr;  // outlier CSR by row [rows+1]
     uint2* entries = nullptr;     // (col, f32 bits of v - dequant(q))
     uint16_t* vals = nullptr;     // f16 outlier values (dequantization path)

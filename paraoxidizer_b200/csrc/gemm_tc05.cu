@@ -354,7 +354,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc05_kernel(TcArgs a) {
                         if (a.S > 1) {
                             dst[(size_t)b * a.Nout + row] = v[j];
                         } else {
-                            float r = v[j] * a.xscale[b] * a.wscale;
+                            float r = v[j] * a.xscale[b] * (a.row_scale ? a.row_scale[row] : a.wscale);
                             if (a.resid) r += a.resid[(size_t)b * a.Nout + row];
                             dst[(size_t)b * a.Nout + row] = r;
                         }
@@ -383,7 +383,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc05_kernel(TcArgs a) {
             const int items = a.B * per_b;
             for (int it = tid; it < items; it += kTcThreads) {
                 const int b = it / per_b, q = it % per_b;
-                const float sc = a.xscale[b] * a.wscale;
+                const float sc = a.xscale[b] * a.wscale;  // per-tensor scale; per-row scales below
                 if (vec) {
                     const size_t o = (size_t)b * a.Nout + r0 + 4 * q;
                     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -399,7 +399,15 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc05_kernel(TcArgs a) {
                             acc.z += part[sp].z;
                             acc.w += part[sp].w;
                         }
-                    float4 r = make_float4(acc.x * sc, acc.y * sc, acc.z * sc, acc.w * sc);
+                    float4 r;
+                    if (a.row_scale) {
+                        const int rw = r0 + 4 * q;
+                        const float xs = a.xscale[b];
+                        r = make_float4(acc.x * (xs * a.row_scale[rw]), acc.y * (xs * a.row_scale[rw + 1]),
+                                        acc.z * (xs * a.row_scale[rw + 2]), acc.w * (xs * a.row_scale[rw + 3]));
+                    } else {
+                        r = make_float4(acc.x * sc, acc.y * sc, acc.z * sc, acc.w * sc);
+                    }
                     if (a.resid) {
                         const float4 rr = *reinterpret_cast<const float4*>(a.resid + o);
                         r.x += rr.x;
@@ -412,7 +420,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc05_kernel(TcArgs a) {
                     const size_t o = (size_t)b * a.Nout + r0 + q;
                     float acc = 0.f;
                     for (int sp = 0; sp < a.S; sp++) acc += __ldcg(a.ws + (size_t)sp * a.Bp * a.Nout + o);
-                    float r = acc * sc;
+                    float r = acc * (a.row_scale ? a.xscale[b] * a.row_scale[r0 + q] : sc);
                     if (a.resid) r += a.resid[o];
                     a.y[o] = r;
                 }

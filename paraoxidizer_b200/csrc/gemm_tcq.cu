@@ -338,7 +338,7 @@ __global__ void __launch_bounds__(tq_threads(NP), 1) gemm_tq_kernel(TqArgs a) {
                 const int b = h * NBR + j;
                 if (b < a.B) {
                     const size_t o = (size_t)b * a.Nout + row;
-                    float v = acc[j] * a.wscale;
+                    float v = acc[j] * (a.row_scale ? a.row_scale[row] : a.wscale);
                     if (a.S == 1 && a.resid) v += a.resid[o];
                     dst[o] = v;
                 }

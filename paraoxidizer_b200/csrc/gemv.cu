@@ -512,7 +512,8 @@ __global__ void __launch_bounds__(512, 2) gemv_tc_kernel(const GemvArgs a) {
     if (S == 1) {
         if (tid < 128 && bb < B && row < a.N) {
             const size_t o = (size_t)bb * a.N + row;
-            a.y[o] = a.resid ? a.resid[o] + p * oscale : p * oscale;
+            const float os = KIND == kKindI8 && a.row_scale ? a.row_scale[row] : oscale;
+            a.y[o] = a.resid ? a.resid[o] + p * os : p * os;
         }
     } else {
         if (tid < 128) part[tid] = p;
@@ -521,7 +522,8 @@ __global__ void __launch_bounds__(512, 2) gemv_tc_kernel(const GemvArgs a) {
             for (int r = 1; r < S; r++) p += ld_dsmem_f32(part + tid, (uint32_t)r);
             if (row < a.N) {
                 const size_t o = (size_t)bb * a.N + row;
-                a.y[o] = a.resid ? a.resid[o] + p * oscale : p * oscale;
+                const float os = KIND == kKindI8 && a.row_scale ? a.row_scale[row] : oscale;
+                a.y[o] = a.resid ? a.resid[o] + p * os : p * os;
             }
         }
         cluster_sync_all();  // remote shared memory stays valid until rank 0 has read it
@@ -706,10 +708,11 @@ __global__ void gemv_i8_generic_kernel(GemvGenericArgs a) {
     const int lane = threadIdx.x & 31;
     if (row >= a.N) return;
     const int8_t* qrow = reinterpret_cast<const int8_t*>(a.raw) + (size_t)row * a.K;
+    const float sc = a.row_scale ? a.row_scale[row] : a.i8_scale;
     for (int b = 0; b < a.B; b++) {
         float s = 0.f;
         for (int c = lane; c < a.K; c += 32)
-            s = fmaf(__fmul_rn((float)qrow[c], a.i8_scale), a.x[(size_t)b * a.K + c], s);
+            s = fmaf(__fmul_rn((float)qrow[c], sc), a.x[(size_t)b * a.K + c], s);
         s = warp_sum(s);
         if (lane == 0) a.y[(size_t)b * a.N + row] = s;
     }
@@ -827,8 +830,8 @@ __global__ void dequant_i4_raw_kernel(const uint8_t* __restrict__ raw, const uin
     }
 }
 
-__global__ void dequant_i8_tiled_kernel(const uint8_t* __restrict__ tiles, float scale, float* __restrict__ out,
-                                        TileLayout L) {
+__global__ void dequant_i8_tiled_kernel(const uint8_t* __restrict__ tiles, float scale,
+                                        const float* __restrict__ row_scale, float* __restrict__ out, TileLayout L) {
     const size_t total = (size_t)L.N * L.K;
     for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total;
          idx += (size_t)gridDim.x * blockDim.x) {
@@ -838,15 +841,15 @@ __global__ void dequant_i8_tiled_kernel(const uint8_t* __restrict__ tiles, float
         const int kb = k / 64, kin = k % 64, t = kin / 16, j = kin % 16;
         const size_t tile = (size_t)T * L.nkb + kb;
         const int8_t q = (int8_t)tiles[tile * L.tb + s * 512 + (4 * g + t) * 16 + j];
-        out[idx] = __fmul_rn((float)q, scale);
+        out[idx] = __fmul_rn((float)q, row_scale ? row_scale[row] : scale);
     }
 }
 
-__global__ void dequant_i8_raw_kernel(const uint8_t* __restrict__ raw, float scale, float* __restrict__ out,
-                                      size_t total) {
+__global__ void dequant_i8_raw_kernel(const uint8_t* __restrict__ raw, float scale, const float* __restrict__ row_scale,
+                                      float* __restrict__ out, size_t total, int K) {
     for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total;
          idx += (size_t)gridDim.x * blockDim.x)
-        out[idx] = __fmul_rn((float)(int8_t)raw[idx], scale);
+        out[idx] = __fmul_rn((float)(int8_t)raw[idx], row_scale ? row_scale[idx / K] : scale);
 }
 
 __global__ void apply_outliers_kernel(const uint32_t* __restrict__ row_ptr, const uint2* __restrict__ entries,
@@ -896,13 +899,14 @@ cudaError_t launch_dequant_i4(bool tiled, const void* w, const void* scales, flo
     return cudaGetLastError();
 }
 
-cudaError_t launch_dequant_i8(bool tiled, const void* w, float scale, float* out, int N, int K, cudaStream_t st) {
+cudaError_t launch_dequant_i8(bool tiled, const void* w, float scale, const float* row_scale, float* out, int N, int K,
+                              cudaStream_t st) {
     const size_t total = (size_t)N * K;
     if (tiled)
-        dequant_i8_tiled_kernel<<<grid_for(total), 256, 0, st>>>((const uint8_t*)w, scale, out,
+        dequant_i8_tiled_kernel<<<grid_for(total), 256, 0, st>>>((const uint8_t*)w, scale, row_scale, out,
                                                                  TileLayout(kKindI8, N, K));
     else
-        dequant_i8_raw_kernel<<<grid_for(total), 256, 0, st>>>((const uint8_t*)w, scale, out, total);
+        dequant_i8_raw_kernel<<<grid_for(total), 256, 0, st>>>((const uint8_t*)w, scale, row_scale, out, total, K);
     return cudaGetLastError();
 }
 

@@ -136,6 +136,7 @@ __device__ __forceinline__ void block_rms_inv(const float* x, int ldx, int K, fl
 struct GemvArgs {
     const uint8_t* w;        // tile blobs (TileLayout)
     float i8_scale;          // INT8 per-tensor scale
+    const float* row_scale;  // INT8 per-output-channel scales [N] (nullptr: i8_scale)
     const uint32_t* row_ptr; // outlier CSR by row [N+1] (nullptr if none)
     const uint2* ent;        // (col, f32 bits of v - dequant(q))
     const void* xq;          // prepared x columns
@@ -163,6 +164,7 @@ struct GemvGenericArgs {
     const uint8_t* raw;
     const uint8_t* raw_scales;
     float i8_scale;
+    const float* row_scale;  // INT8 per-output-channel scales [N] (nullptr: i8_scale)
     const uint32_t* row_ptr;
     const uint2* entries;
     const float* x;
@@ -175,7 +177,8 @@ cudaError_t launch_repack(int kind, const uint8_t* src, uint8_t* tiles, int N, i
 cudaError_t launch_repack_i4_scales(const uint8_t* src, uint8_t* tiles, int N, int K, int gs, cudaStream_t st);
 cudaError_t launch_dequant_i4(bool tiled, const void* w, const void* scales, float* out, int N, int K, int groups,
                               int gs, cudaStream_t st);
-cudaError_t launch_dequant_i8(bool tiled, const void* w, float scale, float* out, int N, int K, cudaStream_t st);
+cudaError_t launch_dequant_i8(bool tiled, const void* w, float scale, const float* row_scale, float* out, int N, int K,
+                              cudaStream_t st);
 cudaError_t launch_apply_outliers(const uint32_t* row_ptr, const uint2* entries, const uint16_t* vals, float* out,
                                   int N, int K, cudaStream_t st);
 
@@ -189,6 +192,7 @@ struct TcArgs {
     const uint8_t* xs;         // prepared x: [K / 128][2][Bp][128 B], swizzled
     const float* xscale;       // [Bp] power-of-two scale of each x row
     float wscale;              // INT8 per-tensor scale (1 otherwise)
+    const float* row_scale;    // INT8 per-output-channel scales [Nout] (nullptr: wscale)
     float* y;                  // [B][Nout]
     const float* resid;        // nullptr, or [B][Nout] added (may alias y)
     float* ws;                 // k-split partials [S][Bp][Nout]
@@ -210,6 +214,7 @@ struct TqArgs {
     const uint8_t* xl;    // x limbs [K / 128][2 Bp][128 B], 128-byte swizzled (row 2b: hi, 2b + 1: lo)
     const float2* xm;     // [K / 128][Bp]: (max|x| / 16383, sum x) of each 128-k block of each x row
     float wscale;         // INT8 per-tensor scale (1 otherwise)
+    const float* row_scale;  // INT8 per-output-channel scales [Nout] (nullptr: wscale)
     float* y;             // [B][Nout]
     const float* resid;   // nullptr, or [B][Nout] added (may alias y)
     float* ws;            // k-split partials [S][Bp][Nout]

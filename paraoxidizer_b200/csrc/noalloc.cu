@@ -98,6 +98,7 @@ extern "C" int pox_cuda_tensor_gemv_noalloc(pox_cuda_ctx* ctx, const pox_tensor*
             GemvArgs a = {};
             a.w = (const uint8_t*)t->w;
             a.i8_scale = t->i8_scale;
+            a.row_scale = t->row_scales;
             a.row_ptr = kind == kKindI4 ? t->row_ptr : nullptr;
             a.ent = t->entries;
             a.xq = xp.cols;
@@ -121,6 +122,7 @@ extern "C" int pox_cuda_tensor_gemv_noalloc(pox_cuda_ctx* ctx, const pox_tensor*
             a.raw = (const uint8_t*)t->w;
             a.raw_scales = (const uint8_t*)t->scales_dev;
             a.i8_scale = t->i8_scale;
+            a.row_scale = t->row_scales;
             a.row_ptr = t->row_ptr;
             a.entries = t->entries;
             a.x = xb;

@@ -110,7 +110,9 @@ static void free_tensor_mem(pox_tensor* t) {
     cudaFree(t->tile_ptr);
     cudaFree(t->tile_ent);
     cudaFree(t->scratch);
+    cudaFree(t->row_scales);
     t->scratch = nullptr;
+    t->row_scales = nullptr;
     t->w = t->scales_dev = nullptr;
     t->row_ptr = nullptr;
     t->entries = nullptr;
@@ -216,7 +218,10 @@ static int validate_desc(const pox_tensor_desc* d) {
             return POX_OK;
         }
         case POX_I8:
-            if (d->data_len < d->rows * d->cols || d->scale_len < 4 || !d->scales)
+            if (d->group_size > 1)
+                return set_error(POX_ERR_UNSUPPORTED, "INT8 group_size %zu: 0 (per-tensor f32 scale) or 1 (f16 scale "
+                                 "per row)", d->group_size);
+            if (d->data_len < d->rows * d->cols || !d->scales || d->scale_len < (d->group_size == 1 ? 2 * d->rows : 4))
                 return set_error(POX_ERR_LAYOUT, "GEMV INT8 dimension mismatch");
             return POX_OK;
         case POX_F16:
@@ -405,7 +410,19 @@ int pox::upload_tensor_locked(pox_cuda_ctx* ctx, const pox_tensor_desc* d, pox_t
             CKF(cudaStreamSynchronize(st), "cudaStreamSynchronize(upload)");
         }
     } else if (d->dtype == POX_I8) {
-        CKF(cudaMemcpy(&t->i8_scale, d->scales, 4, cudaMemcpyDefault), "cudaMemcpy(int8 scale)");  // one f32 LE (kernels.rs:150-151)
+        if (d->group_size == 1) {  // f16 scale per output row (the per-channel extension)
+            std::vector<uint16_t> sh(d->rows);
+            std::vector<float> sf(d->rows);
+            CKF(cudaMemcpy(sh.data(), d->scales, 2 * d->rows, cudaMemcpyDefault), "cudaMemcpy(int8 row scales)");
+            for (size_t r = 0; r < d->rows; r++) sf[r] = h2f(sh[r]);
+            CKF(cudaMalloc(&t->row_scales, d->rows * sizeof(float)), "cudaMalloc(int8 row scales)");
+            CKF(cudaMemcpy(t->row_scales, sf.data(), d->rows * sizeof(float), cudaMemcpyHostToDevice),
+                "cudaMemcpy(int8 row scales)");
+            t->bytes += d->rows * sizeof(float);
+            t->i8_scale = 1.0f;
+        } else {
+            CKF(cudaMemcpy(&t->i8_scale, d->scales, 4, cudaMemcpyDefault), "cudaMemcpy(int8 scale)");  // one f32 LE (kernels.rs:150-151)
+        }
         const size_t raw_bytes = d->rows * d->cols;
         t->tiled = (K % 64 == 0);
         CKF(cudaMalloc(&tmp, raw_bytes), "cudaMalloc(raw)");
@@ -578,6 +595,7 @@ static int tc05_gemv(pox_cuda_ctx* ctx, const pox_tensor* t, int kind, const flo
             q.xl = xs;
             q.xm = xm;
             q.wscale = kind == kKindI8 ? t->i8_scale : 1.0f;
+            q.row_scale = kind == kKindI8 ? t->row_scales : nullptr;
             q.y = y + done * t->rows;
             q.resid = resid ? resid + done * t->rows : nullptr;
             q.ws = ws;
@@ -607,6 +625,7 @@ static int tc05_gemv(pox_cuda_ctx* ctx, const pox_tensor* t, int kind, const flo
         a.xs = xs;
         a.xscale = xscale;
         a.wscale = kind == kKindI8 ? t->i8_scale : 1.0f;
+        a.row_scale = kind == kKindI8 ? t->row_scales : nullptr;
         a.y = y + done * t->rows;
         a.resid = resid ? resid + done * t->rows : nullptr;
         a.ws = ws;
@@ -714,6 +733,7 @@ int pox::gemv_launch(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x, siz
             GemvArgs a = {};
             a.w = (const uint8_t*)t->w;
             a.i8_scale = t->i8_scale;
+            a.row_scale = t->row_scales;
             a.row_ptr = kind == kKindI4 ? t->row_ptr : nullptr;
             a.ent = t->entries;
             a.xq = xp.cols;
@@ -737,6 +757,7 @@ int pox::gemv_launch(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x, siz
             a.raw = (const uint8_t*)t->w;
             a.raw_scales = (const uint8_t*)t->scales_dev;
             a.i8_scale = t->i8_scale;
+            a.row_scale = t->row_scales;
             a.row_ptr = t->row_ptr;
             a.entries = t->entries;
             a.x = xb;
@@ -933,7 +954,7 @@ static int dequant_launch(const pox_tensor* t, float* out, cudaStream_t st) {
         if (e == cudaSuccess && t->nnz)
             e = launch_apply_outliers(t->row_ptr, t->entries, t->vals, out, N, K, st);
     } else if (t->dtype == POX_I8) {
-        e = launch_dequant_i8(t->tiled, t->w, t->i8_scale, out, N, K, st);
+        e = launch_dequant_i8(t->tiled, t->w, t->i8_scale, t->row_scales, out, N, K, st);
     } else {
         return set_error(POX_ERR_UNSUPPORTED, "dequantization of dtype %d", t->dtype);
     }

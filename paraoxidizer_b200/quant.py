@@ -114,6 +114,23 @@ def quantize_int8_symmetric(weights: np.ndarray):
     return q.view(np.uint8), np.array([scale], np.float32).view(np.uint8)
 
 
+def quantize_int8_rows(weights: np.ndarray, rows: int, cols: int):
+    """Per-output-channel INT8 (an extension; the reference's .pox INT8 is per tensor,
+    kernels.rs:131-154): per row max_abs (floor 1e-4 below 1e-8), scale = max_abs / 127 stored as f16
+    (round to nearest even), q = round(w / s) half away from zero, clamped to +-127, with s the f16
+    scale read back. -> (q u8 [i8 bits], rows x 2 bytes of f16 scales)."""
+    w = np.ascontiguousarray(weights, np.float32).reshape(rows, cols)
+    a = np.abs(w)
+    a = np.where(np.isnan(a), np.float32(0), a)
+    max_abs = a.max(axis=1).astype(np.float32) if cols else np.zeros(rows, np.float32)
+    max_abs = np.where(max_abs < np.float32(1e-8), np.float32(1e-4), max_abs).astype(np.float32)
+    sh = (max_abs / np.float32(127.0)).astype(np.float32).astype(np.float16)
+    s = sh.astype(np.float32)[:, None]
+    with np.errstate(invalid="ignore", divide="ignore"):
+        q = _round_clamp_cast((w / s).astype(np.float32), -127.0, 127.0).astype(np.int8)
+    return q.reshape(-1).view(np.uint8), sh.view(np.uint8).reshape(-1)
+
+
 def extract_and_zero_outliers(weights: np.ndarray, policy: str = "automatic"):
     """outlier.rs:57-85. `weights` (f32, contiguous) is zeroed in place at the outliers.
     Returns (indices u32, f16 value bits) or None."""

@@ -816,20 +816,19 @@ static int ensure_pinned(float** host, float** dev, size_t* have, size_t need) {
 }
 
 // Host x in, host y out, synchronous. Caller holds ctx->mu.
-// Tiled tensors: x is copied into pinned staging on the host and from there by one DMA copy into
-// device memory; the GEMV writes y straight into pinned, device-mapped staging (each element once).
-// One stream sync. The raw-layout kernels get x and y in device memory.
+// Tiled tensors: x is copied into pinned, device-mapped staging on the host and read from there over
+// PCIe by the x preparation (once; the GEMV kernels read only the prepared x), and the GEMV writes y
+// straight into pinned, device-mapped staging (each element once): no DMA copies, one stream sync.
+// The raw-layout kernels re-read x for every row, so they get x and y in device memory.
 static int gemv_host_locked(pox_cuda_ctx* ctx, const pox_tensor* t, const float* x, size_t batch, float* y) {
     if (t->rows == 0 || t->cols == 0 || batch == 0) return POX_OK;
     const size_t xb = batch * t->cols * sizeof(float), yb = batch * t->rows * sizeof(float);
     if (t->tiled) {
         int rc = ensure_pinned(&ctx->pin_x, &ctx->pin_x_dev, &ctx->pin_x_bytes, xb);
         if (!rc) rc = ensure_pinned(&ctx->pin_y, &ctx->pin_y_dev, &ctx->pin_y_bytes, yb);
-        if (!rc) rc = ensure_scratch(ctx, xb, 0);
         if (rc) return rc;
         std::memcpy(ctx->pin_x, x, xb);
-        CK(cudaMemcpyAsync(ctx->scratch_x, ctx->pin_x, xb, cudaMemcpyHostToDevice, ctx->stream), "cudaMemcpy(x)");
-        rc = gemv_launch(ctx, t, (const float*)ctx->scratch_x, batch, ctx->pin_y_dev, ctx->stream);
+        rc = gemv_launch(ctx, t, ctx->pin_x_dev, batch, ctx->pin_y_dev, ctx->stream);
         if (rc) return rc;
         CK(cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
         std::memcpy(y, ctx->pin_y, yb);

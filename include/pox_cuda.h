@@ -275,6 +275,16 @@ int pox_cuda_model_prefill(pox_model* m, uint32_t rows, const uint32_t* tokens, 
 int pox_cuda_model_decode_device(pox_model* m, uint32_t batch, const uint32_t* tokens_dev,
                                  const uint32_t* positions_dev, const int32_t* block_tables_dev, float* logits_dev,
                                  uint32_t* next_dev, int advance, void* stream);
+/* enable = 1: decode steps of batch 1..4 run every layer in one persistent kernel (one CTA per SM:
+ * eight warps prepare inputs, run the weight tiles and the attention items, one warp streams the
+ * weights in 34 KB bulk copies ahead of them across projections and layers; grid barriers with
+ * bounded waits between the projections) when the model qualifies: one GPU, head_dim 128 with 4..8
+ * query heads per kv head, all projections INT4 with group size 128 and no outliers. Other steps,
+ * and prefill, take one launch per projection. Default 0 (one launch per projection for every step):
+ * on B200 the persistent kernel is not yet the faster of the two. No counterpart in the reference. */
+int pox_cuda_model_set_persistent(pox_model* m, int enable);
+/* 1 if a decode step of `batch` rows of this model runs as the persistent kernel, else 0. */
+int pox_cuda_model_step_persistent(const pox_model* m, uint32_t batch);
 /* Loads a batch state into the model's device buffers without running a step (host arrays:
  * tokens [batch], positions [batch], block_tables [batch][max_blocks_per_seq]); a following
  * pox_cuda_model_decode_device with NULL inputs continues from it. Synchronous. Every page up to

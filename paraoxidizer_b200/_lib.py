@@ -115,6 +115,8 @@ def _declare(L):
         "pox_cuda_model_decode": (i32, [vp, u32, vp, vp, vp, vp, vp]),
         "pox_cuda_model_prefill": (i32, [vp, u32, vp, vp, vp, u32, vp, vp, vp]),
         "pox_cuda_model_decode_device": (i32, [vp, u32, vp, vp, vp, vp, vp, i32, vp]),
+        "pox_cuda_model_set_persistent": (i32, [vp, i32]),
+        "pox_cuda_model_step_persistent": (i32, [vp, u32]),
         "pox_cuda_model_set_state": (i32, [vp, u32, vp, vp, vp]),
         "pox_cuda_model_buffers": (i32, [vp, C.POINTER(vp), C.POINTER(vp), C.POINTER(vp), C.POINTER(vp),
                                          C.POINTER(vp)]),

@@ -16,8 +16,8 @@ CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libpox_cuda.so")
 BUILD_DIR = os.path.join(PKG, "_build")
 
-SOURCES = ["pox_api.cu", "gemv.cu", "gemm_tc05.cu", "gemm_tcq.cu", "engine.cu", "comm.cu", "quantize.cu", "noalloc.cu", "pox_file.cpp"]
-HEADERS = ["common.cuh", "gemv.cuh", "api_internal.h", "model.h", "comm.cuh", "tc05.cuh"]
+SOURCES = ["pox_api.cu", "gemv.cu", "gemm_tc05.cu", "gemm_tcq.cu", "engine.cu", "comm.cu", "quantize.cu", "noalloc.cu", "persist.cu", "pox_file.cpp"]
+HEADERS = ["common.cuh", "gemv.cuh", "api_internal.h", "model.h", "comm.cuh", "tc05.cuh", "attn.cuh", "persist.h"]
 
 
 def _nvcc() -> str:

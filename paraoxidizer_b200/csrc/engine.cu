@@ -26,7 +26,9 @@
 #include "api_internal.h"
 #include "common.cuh"
 #include "gemv.cuh"
+#include "attn.cuh"
 #include "model.h"
+#include "persist.h"
 #include "tc05.cuh"
 
 #ifdef POX_HAVE_NCCL
@@ -81,55 +83,6 @@ __global__ void rope_table_kernel(float2* __restrict__ t, int npos, int hd, floa
     rope_cs((uint32_t)(idx / half), (int)(idx % half), hd, theta, c, s);
     t[idx] = make_float2(c, s);
 }
-__device__ __forceinline__ float2 rope_pair(float a0, float a1, float c, float s) {
-    return make_float2(__fsub_rn(__fmul_rn(a0, c), __fmul_rn(a1, s)), __fadd_rn(__fmul_rn(a0, s), __fmul_rn(a1, c)));
-}
-
-// What the attention kernels do besides attending: the decode step ropes q and appends the row's own
-// k and v; prefill ropes q over pages a separate kernel already filled for every row of the pass;
-// the kernel-level entry point takes q as given over filled pages.
-enum { kAttnDecode = 0, kAttnPrefill = 1, kAttnPlain = 2 };
-
-// q of the CTA's G query heads into shared memory (qs [8][HD]), rotated by RoPE (engine.rs:353-408)
-// from the model's (cos, sin) table unless MODE is kAttnPlain; in kAttnDecode the CTA whose split
-// holds position p also rotates k and appends k and v to the page btab_row[p / 16], slot p % 16 (an
-// entry outside [0, kv_blocks) is reported and nothing is written).
-template <int HD, int MODE>
-__device__ __forceinline__ void load_q_append_kv(const float* row, uint32_t p, const int32_t* btab_row, int kv_blocks,
-                                                 __half* kc, __half* vc, int layer, int L, int nq, int nkv, int h,
-                                                 int G, const float2* rope, int t0, float* qs, int* err) {
-    constexpr int DH = HD / 2;
-    const int tid = threadIdx.x;
-    const float2* rp = MODE != kAttnPlain ? rope + (size_t)p * DH : nullptr;  // (cos, sin) at position p
-    for (int j = tid; j < G * DH; j += blockDim.x) {
-        const int g = j / DH, i = j % DH;
-        const float* q = row + (size_t)(h * G + g) * HD;
-        float2 r = make_float2(q[2 * i], q[2 * i + 1]);
-        if (MODE != kAttnPlain) {
-            const float2 cs = rp[i];
-            r = rope_pair(r.x, r.y, cs.x, cs.y);
-        }
-        qs[g * HD + 2 * i] = r.x;
-        qs[g * HD + 2 * i + 1] = r.y;
-    }
-    if (MODE == kAttnDecode && (int)p < t0 + kSplitTok) {  // this split holds the new position: append k, v
-        const int blk = btab_row[p / kPage];
-        if (blk < 0 || blk >= kv_blocks) {
-            if (h == 0 && tid == 0) atomicOr(err, kErrAttnPage);
-            return;
-        }
-        const size_t off = ((((size_t)blk * L + layer) * nkv + h) * kPage + p % kPage) * HD;
-        const float* k = row + (size_t)(nq + h) * HD;
-        const float* v = row + (size_t)(nq + nkv + h) * HD;
-        for (int i = tid; i < DH; i += blockDim.x) {
-            const float2 cs = rp[i];
-            const float2 r = rope_pair(k[2 * i], k[2 * i + 1], cs.x, cs.y);
-            *reinterpret_cast<__half2*>(kc + off + 2 * i) = __floats2half2_rn(r.x, r.y);
-            *reinterpret_cast<__half2*>(vc + off + 2 * i) = __floats2half2_rn(v[2 * i], v[2 * i + 1]);
-        }
-    }
-}
-
 // ---- paged GQA decode attention (engine.rs:580-641), split over the context, RoPE and the KV
 // append fused in ----
 // CTA (split, kv head, batch row) takes tokens [64 split, min(ctx, 64 split + 64)) for the G query
@@ -167,7 +120,7 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const float* __restric
     __shared__ float acc_s[4][8][HD];
     const float* row = qkv + (size_t)b * qkv_rows;
     load_q_append_kv<HD, MODE>(row, p, btab + (size_t)b * mbps, kv_blocks, kc, vc, layer, L, nq, nkv, h, G,
-                                rope, t0, &qs[0][0], err);
+                                rope, t0, &qs[0][0], err, (int)threadIdx.x, (int)blockDim.x);
     __syncthreads();
 
     // this warp's page: tokens t0 + 16 warp .. + 15 (t0 is a multiple of 64, pages hold 16)
@@ -299,25 +252,6 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const float* __restric
 // |q| >= 2^-4, an absolute error under 2^-24 below), then
 // O = P V with P likewise split. Fragments come from ldmatrix (V transposed); rows of a page past
 // the context are zero.
-__device__ __forceinline__ void ldsm_x4(uint32_t a, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-                 : "r"(a));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t a, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-                 : "r"(a));
-}
-// (hi, lo) f16 pairs of (x0, x1): hi = f16(x), lo = f16(x - hi)
-__device__ __forceinline__ void split_f16x2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
-    const __half2 h = __floats2half2_rn(x0, x1);
-    const float2 hf = __half22float2(h);
-    const __half2 l = __floats2half2_rn(x0 - hf.x, x1 - hf.y);
-    hi = *reinterpret_cast<const uint32_t*>(&h);
-    lo = *reinterpret_cast<const uint32_t*>(&l);
-}
-
 template <int HD, int MODE>
 __global__ void __launch_bounds__(128) attn_decode_tc_kernel(const float* __restrict__ qkv, int qkv_rows,
                                                              const uint32_t* __restrict__ pos,
@@ -328,7 +262,6 @@ __global__ void __launch_bounds__(128) attn_decode_tc_kernel(const float* __rest
                                                              const float2* __restrict__ rope,
                                                              float* __restrict__ apart, int* __restrict__ err) {
     static_assert(HD == 128, "head_dim 128");
-    constexpr int RS = HD + 8;  // staged row stride in halves (272 B: ldmatrix rows in distinct banks)
     pdl_launch_dependents();
     pdl_wait();
     const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -337,135 +270,11 @@ __global__ void __launch_bounds__(128) attn_decode_tc_kernel(const float* __rest
         if (split == 0 && h == 0 && threadIdx.x == 0) atomicOr(err, kErrAttnPos);
         return;
     }
-    const int ctx = (int)p + 1;
-    const int t0 = split * kSplitTok;
-    if (t0 >= ctx) return;  // the combine kernel reads only ceil(ctx / 64) splits
-    const int nt = min(ctx - t0, kSplitTok);
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    __shared__ float qs[8][HD];
-    __shared__ float red_m[4][8], red_l[4][8];
-    __shared__ __align__(16) __half kv_s[2][4][16][RS];  // [K, V][warp][token][dim]; then the warps' outputs
-    float (*acc_s)[8][HD] = reinterpret_cast<float (*)[8][HD]>(&kv_s[0][0][0][0]);
-    const float* row = qkv + (size_t)b * qkv_rows;
-    load_q_append_kv<HD, MODE>(row, p, btab + (size_t)b * mbps, kv_blocks, kc, vc, layer, L, nq, nkv, h, G,
-                                rope, t0, &qs[0][0], err);
-    __syncthreads();
-
-    // this warp's page (tokens t0 + 16 warp ..) staged in shared memory, rows past the context zero
-    int nw = max(0, min(16, nt - 16 * warp));
-    {
-        size_t page = 0;
-        if (nw > 0) {
-            const int blk = btab[(size_t)b * mbps + (t0 + 16 * warp) / kPage];
-            if (blk < 0 || blk >= kv_blocks) {  // invalid page: reported, its tokens left out (rows zero)
-                if (lane == 0) atomicOr(err, kErrAttnPage);
-                nw = 0;
-            } else {
-                page = (((size_t)blk * L + layer) * nkv + h) * kPage * HD;
-            }
-        }
-#pragma unroll
-        for (int u = 0; u < 16 * (HD / 8) / 32; u++) {
-            const int idx = lane + 32 * u, r = idx / (HD / 8), c = idx % (HD / 8);
-            uint4 kv = make_uint4(0u, 0u, 0u, 0u), vv = kv;
-            if (r < nw) {
-                kv = __ldcg(reinterpret_cast<const uint4*>(kc + page + (size_t)r * HD) + c);
-                vv = __ldcg(reinterpret_cast<const uint4*>(vc + page + (size_t)r * HD) + c);
-            }
-            *reinterpret_cast<uint4*>(&kv_s[0][warp][r][8 * c]) = kv;
-            *reinterpret_cast<uint4*>(&kv_s[1][warp][r][8 * c]) = vv;
-        }
-    }
-    __syncwarp();
-
-    const int g = lane >> 2, t = lane & 3, mi = lane >> 3, mr = lane & 7;
-    // S = Q K^T: A rows = query heads (g < G; rows g + 8 are padding), B = the staged K rows
-    float sacc[2][4];
-#pragma unroll
-    for (int nb = 0; nb < 2; nb++) sacc[nb][0] = sacc[nb][1] = sacc[nb][2] = sacc[nb][3] = 0.f;
-    const uint32_t kbase = smem_u32(&kv_s[0][warp][0][0]), vbase = smem_u32(&kv_s[1][warp][0][0]);
-#pragma unroll
-    for (int ks = 0; ks < HD / 16; ks++) {
-        uint32_t qh0, ql0, qh1, ql1;
-        const int c0 = 16 * ks + 2 * t;
-        split_f16x2(g < G ? qs[g][c0] : 0.f, g < G ? qs[g][c0 + 1] : 0.f, qh0, ql0);
-        split_f16x2(g < G ? qs[g][c0 + 8] : 0.f, g < G ? qs[g][c0 + 9] : 0.f, qh1, ql1);
-        uint32_t b00, b01, b10, b11;  // tokens 0-7: (b00, b01), tokens 8-15: (b10, b11)
-        ldsm_x4(kbase + (uint32_t)(((8 * (mi >> 1) + mr) * RS + 16 * ks + 8 * (mi & 1)) * 2), b00, b01, b10, b11);
-        mma_16816(sacc[0], qh0, 0u, qh1, 0u, b00, b01);
-        mma_16816(sacc[0], ql0, 0u, ql1, 0u, b00, b01);
-        mma_16816(sacc[1], qh0, 0u, qh1, 0u, b10, b11);
-        mma_16816(sacc[1], ql0, 0u, ql1, 0u, b10, b11);
-    }
-    // scores of head g: tokens 8 nb + 2 t + e of this page
-    const float scale = 1.0f / sqrtf(fmaxf((float)HD, 1.0f));
-    float sc[2][2];
-    float m = -INFINITY;
-#pragma unroll
-    for (int nb = 0; nb < 2; nb++)
-#pragma unroll
-        for (int e = 0; e < 2; e++) {
-            const int jj = 8 * nb + 2 * t + e;
-            sc[nb][e] = (g < G && jj < nw) ? sacc[nb][e] * scale : -INFINITY;
-            m = fmaxf(m, sc[nb][e]);
-        }
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
-    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
-    if (t == 0 && g < G) red_m[warp][g] = m;
-    __syncthreads();
-    float mx = g < G ? fmaxf(fmaxf(red_m[0][g], red_m[1][g]), fmaxf(red_m[2][g], red_m[3][g])) : 0.f;
-    if (!isfinite(mx)) mx = 0.f;
-    float pv[2][2], l = 0.f;
-#pragma unroll
-    for (int nb = 0; nb < 2; nb++)
-#pragma unroll
-        for (int e = 0; e < 2; e++) {
-            float v = 0.f;
-            if (g < G && 8 * nb + 2 * t + e < nw) {
-                v = expf(sc[nb][e] - mx);
-                if (!isfinite(v)) v = 0.f;
-            }
-            pv[nb][e] = v;
-            l += v;
-        }
-    l += __shfl_xor_sync(0xffffffffu, l, 1);
-    l += __shfl_xor_sync(0xffffffffu, l, 2);
-    if (t == 0 && g < G) red_l[warp][g] = l;
-    // O = P V: A = P (tokens 2t, 2t+1 | 2t+8, 2t+9 of head g), B = V rows through ldmatrix.trans
-    uint32_t ph0, pl0, ph1, pl1;
-    split_f16x2(pv[0][0], pv[0][1], ph0, pl0);
-    split_f16x2(pv[1][0], pv[1][1], ph1, pl1);
-    float oacc[HD / 8][4];
-#pragma unroll
-    for (int nd = 0; nd < HD / 8; nd++) oacc[nd][0] = oacc[nd][1] = oacc[nd][2] = oacc[nd][3] = 0.f;
-#pragma unroll
-    for (int j = 0; j < HD / 16; j++) {
-        uint32_t v00, v01, v10, v11;  // dims 16 j ..: (v00, v01), dims 16 j + 8 ..: (v10, v11)
-        ldsm_x4_t(vbase + (uint32_t)(((8 * (mi & 1) + mr) * RS + 16 * j + 8 * (mi >> 1)) * 2), v00, v01, v10, v11);
-        mma_16816(oacc[2 * j], ph0, 0u, ph1, 0u, v00, v01);
-        mma_16816(oacc[2 * j], pl0, 0u, pl1, 0u, v00, v01);
-        mma_16816(oacc[2 * j + 1], ph0, 0u, ph1, 0u, v10, v11);
-        mma_16816(oacc[2 * j + 1], pl0, 0u, pl1, 0u, v10, v11);
-    }
-    __syncthreads();  // every warp is done with the staged pages (acc_s reuses them) and red_l is complete
-    if (g < G)
-#pragma unroll
-        for (int nd = 0; nd < HD / 8; nd++) {
-            acc_s[warp][g][8 * nd + 2 * t] = oacc[nd][0];
-            acc_s[warp][g][8 * nd + 2 * t + 1] = oacc[nd][1];
-        }
-    __syncthreads();
+    if (split * kSplitTok >= (int)p + 1) return;  // the combine kernel reads only ceil(ctx / 64) splits
+    __shared__ AttnTcSmem sm;
     float* out = apart + ((((size_t)b * nkv + h) * max_splits + split) * G) * (HD + 2);
-    for (int i = tid; i < G * HD; i += 128) {
-        const int gg = i / HD, d = i % HD;
-        out[(size_t)gg * (HD + 2) + 2 + d] = (acc_s[0][gg][d] + acc_s[1][gg][d]) + (acc_s[2][gg][d] + acc_s[3][gg][d]);
-    }
-    if (tid < G) {
-        float mt = fmaxf(fmaxf(red_m[0][tid], red_m[1][tid]), fmaxf(red_m[2][tid], red_m[3][tid]));
-        if (!isfinite(mt)) mt = 0.f;
-        out[(size_t)tid * (HD + 2)] = mt;
-        out[(size_t)tid * (HD + 2) + 1] = (red_l[0][tid] + red_l[1][tid]) + (red_l[2][tid] + red_l[3][tid]);
-    }
+    attn_tc_item<MODE>(qkv + (size_t)b * qkv_rows, p, btab + (size_t)b * mbps, kv_blocks, kc, vc, layer, L, nq, nkv,
+                       h, G, rope, split, out, err, sm, (int)threadIdx.x, 0);
 }
 
 // Combines the splits of the attention output and prepares it as the o projection's input:
@@ -822,7 +631,9 @@ static int forward_step(pox_model* m, int B, cudaStream_t st, bool prefill, int 
     PrepOp norm;
     norm.mode = kPrepNorm;
     norm.eps = m->cfg.rms_eps;
-    for (int l = 0; l < m->L; l++) {
+    const bool persistent = !prefill && persist_supported(m, B);
+    if (persistent && (rc = persist_launch(m, B, st))) return rc;
+    for (int l = 0; l < m->L && !persistent; l++) {
         const LayerW& w = m->layers[l];
         if (!w.qkv) return set_error(POX_ERR_INVALID, "layer %d has no weights", l);
         norm.norm_w = w.attn_norm;
@@ -960,6 +771,7 @@ extern "C" int pox_cuda_model_create_tp(pox_cuda_ctx* ctx, const pox_llama_confi
     m->max_blocks_per_seq = max_blocks_per_seq;
     m->max_splits = (int)((max_blocks_per_seq * kPage + kSplitTok - 1) / kSplitTok);
     m->layers.resize(m->L);
+    m->pready.assign(m->L, 0);
     const size_t B = max_batch;
     const size_t kv_elems = (size_t)kv_blocks * m->L * m->nkv * kPage * m->hd;
     struct A { void** p; size_t bytes; } allocs[] = {
@@ -979,6 +791,10 @@ extern "C" int pox_cuda_model_create_tp(pox_cuda_ctx* ctx, const pox_llama_confi
         {(void**)&m->rope, (size_t)max_blocks_per_seq * kPage * (m->hd / 2) * sizeof(float2)},
         {(void**)&m->sel, B * 4},
         {(void**)&m->xsel, B * m->H * 4},
+        {(void**)&m->players, (size_t)m->L * sizeof(PLayer)},
+        {(void**)&m->ptickets, B * m->nkv * 4},
+        {(void**)&m->pbar, 4 * sizeof(unsigned)},
+        {(void**)&m->pssq, (size_t)(m->H / 16) * 2 * kPMaxB * 4},
     };
     for (auto& a : allocs) {
         e = cudaMalloc(a.p, a.bytes);
@@ -997,6 +813,9 @@ extern "C" int pox_cuda_model_create_tp(pox_cuda_ctx* ctx, const pox_llama_confi
             return rc;
         }
     }
+    cudaMemsetAsync(m->players, 0, (size_t)m->L * sizeof(PLayer), ctx->stream);
+    cudaMemsetAsync(m->ptickets, 0, B * m->nkv * 4, ctx->stream);
+    cudaMemsetAsync(m->pbar, 0, 4 * sizeof(unsigned), ctx->stream);
     cudaMemsetAsync(m->kc, 0, kv_elems * 2, ctx->stream);
     cudaMemsetAsync(m->vc, 0, kv_elems * 2, ctx->stream);
     {
@@ -1038,7 +857,8 @@ static void destroy_model(pox_model* m) {
     }
     free_tensor(ctx, m->lm_head);
     void* bufs[] = {m->embed, m->final_norm, m->kc, m->vc, m->x, m->qkv, m->att, m->gu, m->logits, m->apart,
-                    m->amax, m->tok, m->pos, m->next, m->btab, m->rope, m->sel, m->xsel};
+                    m->amax, m->tok, m->pos, m->next, m->btab, m->rope, m->sel, m->xsel,
+                    m->players, m->ptickets, m->pbar, m->pssq};
     for (void* p : bufs) cudaFree(p);
     comm_free(m->comm);
     delete m;
@@ -1082,6 +902,7 @@ extern "C" int pox_cuda_model_set_layer(pox_model* m, uint32_t layer, const pox_
                              proj[i].cols, want[i][0], want[i][1]);
     pox_cuda_ctx* ctx = m->ctx;
     LayerW& w = m->layers[layer];
+    m->pready[layer] = 0;
     free_tensor(ctx, w.qkv);
     free_tensor(ctx, w.o);
     free_tensor(ctx, w.gu);
@@ -1106,6 +927,7 @@ extern "C" int pox_cuda_model_set_layer(pox_model* m, uint32_t layer, const pox_
     w.attn_norm = w.mlp_norm = nullptr;
     rc = upload_f16(attn_norm, H, &w.attn_norm, ctx->stream);
     if (!rc) rc = upload_f16(mlp_norm, H, &w.mlp_norm, ctx->stream);
+    if (!rc) rc = persist_set_layer(m, (int)layer);
     return rc;
 }
 
@@ -1126,6 +948,7 @@ extern "C" int pox_cuda_model_set_layer_tensors(pox_model* m, uint32_t layer, po
     }
     pox_cuda_ctx* ctx = m->ctx;
     LayerW& lw = m->layers[layer];
+    m->pready[layer] = 0;
     free_tensor(ctx, lw.qkv);
     free_tensor(ctx, lw.o);
     free_tensor(ctx, lw.gu);
@@ -1141,7 +964,18 @@ extern "C" int pox_cuda_model_set_layer_tensors(pox_model* m, uint32_t layer, po
     lw.attn_norm = lw.mlp_norm = nullptr;
     int rc = upload_f16(attn_norm, H, &lw.attn_norm, ctx->stream);
     if (!rc) rc = upload_f16(mlp_norm, H, &lw.mlp_norm, ctx->stream);
+    if (!rc) rc = persist_set_layer(m, (int)layer);
     return rc;
+}
+
+extern "C" int pox_cuda_model_set_persistent(pox_model* m, int enable) {
+    if (!m) return set_error(POX_ERR_INVALID, "model is NULL");
+    m->persist = enable ? 1 : 0;
+    return POX_OK;
+}
+
+extern "C" int pox_cuda_model_step_persistent(const pox_model* m, uint32_t batch) {
+    return m && persist_supported(m, (int)batch) ? 1 : 0;
 }
 
 extern "C" int pox_cuda_model_decode_device(pox_model* m, uint32_t batch, const uint32_t* tokens_dev,

@@ -18,6 +18,7 @@ constexpr int kXBlock = 128;      // k per x quantization block
 constexpr int kXLimbMax = 16383;  // |X| bound of the 15-bit x quantization
 
 enum { kErrWaitRing = 1, kErrWaitX = 2, kErrWaitEnt = 4 };  // bits of the kernel error flag
+enum { kErrPersist = 256 };  // the persistent decode kernel: a grid-barrier or ring wait expired
 // Bits for invalid input found on the device (reported as POX_ERR_INVALID rather than a timeout): a
 // decode position at or beyond 16 x max_blocks_per_seq, a block-table entry outside [0, kv_blocks).
 enum { kErrAttnPos = 64, kErrAttnPage = 128, kErrInputMask = kErrAttnPos | kErrAttnPage };

@@ -17,6 +17,14 @@ constexpr int kPage = 16;       // tokens per KV page (paged_cache.rs DEFAULT_BL
 constexpr int kSplitTok = 64;   // context tokens per attention CTA (4 pages)
 constexpr int kArgmaxParts = 64;  // max blocks per row of the argmax's first pass
 
+// One layer's projections as the persistent decode kernel reads them (persist.cu): the INT4 tile
+// blobs of qkv, o, gate_up and down, and the two f16 norm weights.
+struct PLayer {
+    const uint8_t* w[4];
+    const uint16_t* attn_norm;
+    const uint16_t* mlp_norm;
+};
+
 struct LayerW {
     pox_tensor* qkv = nullptr;
     pox_tensor* o = nullptr;
@@ -57,4 +65,12 @@ struct pox_model {
     float* xsel = nullptr;    // [B][H] prefill: those rows of x
     int max_splits = 0;
     pox::TpComm comm;
+    // persistent decode kernel (persist.cu): per-layer tile pointers, (sequence, kv head) combine
+    // tickets [max_batch][nkv], grid-barrier words [4]; persist = 1 runs qualifying decode steps on it
+    pox::PLayer* players = nullptr;
+    uint32_t* ptickets = nullptr;
+    unsigned* pbar = nullptr;
+    float* pssq = nullptr;       // [H / 16][2][4] sums of squares of the residual rows
+    std::vector<uint8_t> pready;  // layer l's entry of players is current
+    int persist = 0;
 };

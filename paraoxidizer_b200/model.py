@@ -107,6 +107,15 @@ class CudaModel:
     def set_comm_mode(self, mode: str) -> None:
         L.check(L.lib().pox_cuda_model_comm_mode(self.handle, {"nccl": L.POX_COMM_NCCL, "peer": L.POX_COMM_PEER}[mode]))
 
+    def set_persistent(self, enable: bool) -> None:
+        """True: decode steps of batch 1-4 run every layer as one persistent kernel when the model
+        qualifies (pox_cuda_model_set_persistent); False (the default) keeps one launch per projection."""
+        L.check(L.lib().pox_cuda_model_set_persistent(self.handle, 1 if enable else 0))
+
+    def step_persistent(self, batch: int) -> bool:
+        """Whether a decode step of `batch` rows runs as the persistent kernel."""
+        return bool(L.lib().pox_cuda_model_step_persistent(self.handle, batch))
+
     def close(self) -> None:
         if self.handle:
             L.lib().pox_cuda_model_destroy(self.handle)

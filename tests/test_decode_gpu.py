@@ -89,6 +89,55 @@ def test_decode_matches_forward_token(be, name, outliers, nseq):
     model.close()
 
 
+@pytest.mark.parametrize("name,nseq", [("l8", 1), ("l8", 2), ("l8", 4), ("l70", 1), ("l70", 3)])
+def test_persistent_decode_matches_forward_token(be, name, nseq):
+    """Batch 1-4 without outliers runs every layer as one persistent kernel (grid barriers between the
+    projections, attention items combined by the last split of each kv head). Contexts up to 170
+    positions put 3 attention splits in a sequence; every step is checked against the oracle, and the
+    per-projection launches of the same model (persistent kernel off) agree within 5e-3."""
+    cfg = CONFIGS[name]
+    w = make_llama(cfg, seed=23, norm_jitter=0.1)
+    model = CudaModel(be, cfg, max_batch=8, kv_blocks=32 * nseq, max_blocks_per_seq=16)
+    load_into(model, w)
+    assert not model.step_persistent(nseq)  # opt-in
+    model.set_persistent(True)
+    assert model.step_persistent(nseq)
+    ow = oracle_weights(w)
+    rng = np.random.default_rng(40 + nseq)
+    lens = (150, 7, 70, 33)[:nseq]
+    prompts = [list(rng.integers(0, cfg["vocab"], n)) for n in lens]
+    steps = 20
+    oracles = [O.OracleModel(cfg, ow, max_seq=256, kv_f16=True) for _ in prompts]
+    seqs = [model.new_sequence() for _ in prompts]
+    feeds = [list(p) for p in prompts]
+    horizon = max(len(p) for p in prompts) + steps
+    outs = {}
+    for t in range(horizon):
+        active = [i for i in range(nseq) if t < len(prompts[i]) + steps]
+        tokens = [int(feeds[i][t]) for i in active]
+        logits, nxt = model.decode(tokens, [seqs[i] for i in active])
+        for j, i in enumerate(active):
+            ref = oracles[i].forward_token(tokens[j], t)
+            err = float(np.max(np.abs(logits[j] - ref)))
+            assert err <= E2E_TOL, (name, nseq, i, t, err)
+            outs[(i, t)] = logits[j].copy()
+            if t + 1 >= len(prompts[i]):
+                feeds[i].append(int(np.argmax(ref)))
+    # the per-projection launches on the same weights and inputs: the same logits up to the order of
+    # the RMSNorm sums and of the partial reductions
+    model.set_persistent(False)
+    assert not model.step_persistent(nseq)
+    seqs2 = [model.new_sequence() for _ in prompts]
+    worst = 0.0
+    for t in range(horizon):
+        active = [i for i in range(nseq) if t < len(prompts[i]) + steps]
+        logits, _ = model.decode([int(feeds[i][t]) for i in active], [seqs2[i] for i in active])
+        for j, i in enumerate(active):
+            worst = max(worst, float(np.max(np.abs(logits[j] - outs[(i, t)]))))
+    assert worst <= 5e-3, worst
+    model.close()
+
+
 # The Llama-3-8B widths (d 4096, 32 / 8 heads of 128, FFN 14336, vocab 128256, f16 embedding and
 # lm_head), two layers so the oracle's scalar forward_token stays within seconds per token.
 LLAMA8B_2L = {"hidden": 4096, "inter": 14336, "layers": 2, "n_heads": 32, "n_kv_heads": 8, "vocab": 128256,

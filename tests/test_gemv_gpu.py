@@ -222,3 +222,19 @@ def test_registered_host_slices_reuse_resident_copy(be):
     assert np.array_equal(y, t.gemv_host(x))
     assert max_rel(y, O.gemv_int4(packed, scales, gs, rows, cols, None, x)) <= GEMV_TOL
     t.free()
+
+
+def test_host_slice_calls_replay_as_one_graph(be):
+    """From the second host-slice call of a batch on, the x preparation and GEMV are replayed as one
+    CUDA graph on the same staging buffers: every call's y must follow that call's x, across batch
+    changes (a new batch is launched directly, then cached) and a larger x that regrows the staging."""
+    rows, cols, gs = 1024, 2048, 128
+    packed, scales, tab, ob = i4_case(rows, cols, gs, seed=31, hot_cols=6, policy="automatic")
+    t = be.upload_int4(packed, scales, rows, cols, gs, ob)
+    for i, batch in enumerate((1, 1, 1, 3, 3, 1, 8, 8, 1)):
+        x = make_x(cols, batch, seed=40 + i)
+        y = np.asarray(t.gemv_host(x, batch)).reshape(batch, rows)
+        for b in range(batch):
+            ref = O.gemv_int4(packed, scales, gs, rows, cols, tab, x[b * cols:(b + 1) * cols])
+            assert max_rel(y[b], ref) <= GEMV_TOL, (i, batch, b)
+    t.free()

@@ -211,8 +211,8 @@ int pox_oracle_dequantize_int8_symmetric(const uint8_t* q, size_t n, const uint8
     return ORACLE_OK;
 }
 
-/* Per-output-channel INT8 (the extension BASELINE-style configurations ask for; the reference's .pox
- * INT8 is per tensor, kernels.rs:131-154): the reference's rules applied to each row -- max_abs of the
+/* Per-output-channel INT8 (an f16 scale per output row; the reference's .pox INT8 is per tensor,
+ * kernels.rs:131-154): the reference's rules applied to each row -- max_abs of the
  * row (floor 1e-4 below 1e-8), scale = max_abs / 127 (f32), stored as f16 (round to nearest even);
  * q = round(w / s) clamped to +-127 with s = the f16 scale read back as f32, so that q * s is the
  * value the stored table dequantizes to. scale_out: rows x 2 bytes LE. */

@@ -15,6 +15,7 @@
 #include "common.cuh"
 #include "gemv.cuh"
 #include "model.h"
+#include "tc05.cuh"
 
 namespace pox {
 
@@ -90,6 +91,111 @@ __device__ __forceinline__ void split_f16x2(float x0, float x1, uint32_t& hi, ui
     const __half2 l = __floats2half2_rn(x0 - hf.x, x1 - hf.y);
     hi = *reinterpret_cast<const uint32_t*>(&h);
     lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+// Where the attention's combined output also goes as the o projection's prepared input (one 128-k
+// block per query head of 128): the GEMV path's limbs and meta (cols / meta, strides Kp / nxbs), the
+// integer small-M path's swizzled limbs and meta (xl / xm, padded batch Bp), or the f16 small-M
+// path's swizzled halves (xs, row scale 1 in xscale). All NULL: att only.
+struct OPrep {
+    uint8_t* cols = nullptr;
+    float2* meta = nullptr;
+    int Kp = 0, nxbs = 0;
+    uint8_t* xs = nullptr;
+    float* xscale = nullptr;
+    uint8_t* xl = nullptr;
+    float2* xm = nullptr;
+    int Bp = 0;
+};
+
+// The split combine fused into the attention kernel: the item that finishes a (sequence, kv head)
+// last (a ticket per pair, zero between launches) combines its splits.
+struct AttnFuse {
+    uint32_t* tickets = nullptr;  // [B][nkv]; NULL: the combine is a kernel of its own
+    float* att = nullptr;         // [B][nq * 128]
+    OPrep op;
+};
+
+// att of the G query heads of kv head h, sequence b, from its ns split partials (base: [splits][G][130]
+// floats of (max, sum, acc[128])): att = sum_s e^(m_s - M) acc_s / sum_s e^(m_s - M) l_s, 0 when the
+// sum is <= 1e-9 (engine.rs:620-641). 128 threads: warp w takes heads w and w + 4, lane l dims
+// 4 l .. 4 l + 3; the (max, sum) pairs and accumulators of 16 splits are loaded in one round (read
+// from L2: other CTAs wrote them) with M and the sum carried exactly across rounds. Also writes the
+// o projection's prepared input of those heads (op), xprep_int_kernel's arithmetic per 128-block.
+__device__ __forceinline__ void attn_combine_heads(const float* base, int ns, int G, int b, int h, float* att_b,
+                                                   const OPrep& op, int tid) {
+    const int w = tid >> 5, lane = tid & 31;
+    const size_t sstride = (size_t)G * 130;
+    for (int gq = w; gq < G; gq += 4) {
+        const float* hb = base + (size_t)gq * 130;
+        float4 num = make_float4(0.f, 0.f, 0.f, 0.f);
+        float M = -INFINITY, den = 0.f;
+        for (int s0 = 0; s0 < ns; s0 += 16) {
+            const int n = min(16, ns - s0);
+            const float2 ml = lane < n ? __ldcg(reinterpret_cast<const float2*>(hb + (s0 + lane) * sstride))
+                                       : make_float2(-INFINITY, 0.f);
+            float2 v[16][2];
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                const float* pp = hb + (s0 + min(j, n - 1)) * sstride;
+                v[j][0] = __ldcg(reinterpret_cast<const float2*>(pp + 2 + 4 * lane));
+                v[j][1] = __ldcg(reinterpret_cast<const float2*>(pp + 4 + 4 * lane));
+            }
+            const float Mc = fmaxf(M, warp_max(ml.x));
+            const float sc = M == -INFINITY ? 0.f : expf(M - Mc);
+            const float wl = lane < n ? expf(ml.x - Mc) : 0.f;
+            den = fmaf(den, sc, warp_sum(wl * ml.y));
+            num.x *= sc, num.y *= sc, num.z *= sc, num.w *= sc;
+#pragma unroll
+            for (int j = 0; j < 16; j++) {
+                const float wt = __shfl_sync(0xffffffffu, wl, j);  // 0 past the round's splits
+                num.x = fmaf(wt, v[j][0].x, num.x);
+                num.y = fmaf(wt, v[j][0].y, num.y);
+                num.z = fmaf(wt, v[j][1].x, num.z);
+                num.w = fmaf(wt, v[j][1].y, num.w);
+            }
+            M = Mc;
+        }
+        const float inv = den > 1e-9f ? 1.0f / den : 0.f;
+        const float4 o = make_float4(num.x * inv, num.y * inv, num.z * inv, num.w * inv);
+        const int blk = h * G + gq, e = blk * 128 + 4 * lane;
+        *reinterpret_cast<float4*>(att_b + e) = o;
+        if (op.cols || op.xl) {
+            const float m = warp_max(fmaxf(fmaxf(fabsf(o.x), fabsf(o.y)), fmaxf(fabsf(o.z), fabsf(o.w))));
+            const float sm = warp_sum((o.x + o.y) + (o.z + o.w));
+            const float qi = m > 0.f ? (float)kXLimbMax / m : 0.f;
+            const int X[4] = {__float2int_rn(o.x * qi), __float2int_rn(o.y * qi), __float2int_rn(o.z * qi),
+                              __float2int_rn(o.w * qi)};
+            uint32_t hi = 0, lo = 0;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int q = max(-kXLimbMax, min(kXLimbMax, X[i]));
+                hi |= ((uint32_t)(q >> 7) & 0xFFu) << (8 * i);
+                lo |= ((uint32_t)q & 0x7Fu) << (8 * i);
+            }
+            const float2 mt = make_float2(m > 0.f ? m / (float)kXLimbMax : 0.f, sm);
+            if (op.cols) {
+                *reinterpret_cast<uint32_t*>(op.cols + (size_t)(2 * b) * op.Kp + e) = hi;
+                *reinterpret_cast<uint32_t*>(op.cols + (size_t)(2 * b + 1) * op.Kp + e) = lo;
+                if (lane == 0) op.meta[(size_t)b * op.nxbs + blk] = mt;
+            } else {
+                uint8_t* tile = op.xl + (size_t)blk * (2 * op.Bp) * 128;
+                *reinterpret_cast<uint32_t*>(tile + sw128_off(2 * b, lane >> 2) + ((4 * lane) & 15)) = hi;
+                *reinterpret_cast<uint32_t*>(tile + sw128_off(2 * b + 1, lane >> 2) + ((4 * lane) & 15)) = lo;
+                if (lane == 0) op.xm[(size_t)blk * op.Bp + b] = mt;
+            }
+        } else if (op.xs) {
+            const int kk = 4 * lane;
+            const size_t off = ((size_t)blk * 2 + (kk >> 6)) * (size_t)op.Bp * 128 + sw128_off(b, (kk & 63) >> 3) +
+                               2 * (kk & 7);
+            const __half2 h01 = __floats2half2_rn(o.x, o.y), h23 = __floats2half2_rn(o.z, o.w);
+            uint2 hv;
+            hv.x = *reinterpret_cast<const uint32_t*>(&h01);
+            hv.y = *reinterpret_cast<const uint32_t*>(&h23);
+            *reinterpret_cast<uint2*>(op.xs + off) = hv;
+            if (blk == 0 && lane == 0) op.xscale[b] = 1.0f;
+        }
+    }
 }
 
 // Shared memory of one tensor-core attention item (head_dim 128, 128 threads).

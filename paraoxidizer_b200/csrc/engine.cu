@@ -252,6 +252,9 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const float* __restric
 // |q| >= 2^-4, an absolute error under 2^-24 below), then
 // O = P V with P likewise split. Fragments come from ldmatrix (V transposed); rows of a page past
 // the context are zero.
+// With fz.tickets the split combine runs here: the CTA that finishes a (sequence, kv head) last
+// combines its splits into att and o_proj's prepared input (attn_combine_heads), so the combine
+// needs no launch of its own.
 template <int HD, int MODE>
 __global__ void __launch_bounds__(128) attn_decode_tc_kernel(const float* __restrict__ qkv, int qkv_rows,
                                                              const uint32_t* __restrict__ pos,
@@ -260,21 +263,41 @@ __global__ void __launch_bounds__(128) attn_decode_tc_kernel(const float* __rest
                                                              __half* __restrict__ vc, int layer, int L, int nq,
                                                              int nkv, int G, int max_splits,
                                                              const float2* __restrict__ rope,
-                                                             float* __restrict__ apart, int* __restrict__ err) {
+                                                             float* __restrict__ apart, int* __restrict__ err,
+                                                             AttnFuse fz) {
     static_assert(HD == 128, "head_dim 128");
     pdl_launch_dependents();
     pdl_wait();
     const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
     const uint32_t p = pos[b];
+    const float* base = apart + (((size_t)b * nkv + h) * max_splits) * G * (HD + 2);
     if (p >= (uint32_t)mbps * kPage) {  // beyond the block table (invalid input): reported, nothing read
         if (split == 0 && h == 0 && threadIdx.x == 0) atomicOr(err, kErrAttnPos);
+        if (fz.tickets && split == 0)  // output 0, as the combine kernel writes for no splits
+            attn_combine_heads(base, 0, G, b, h, fz.att + (size_t)b * nq * HD, fz.op, (int)threadIdx.x);
         return;
     }
-    if (split * kSplitTok >= (int)p + 1) return;  // the combine kernel reads only ceil(ctx / 64) splits
+    const int ns = min(max_splits, (int)((p + kSplitTok) / kSplitTok));
+    if (split >= ns) return;  // the combine reads only ceil(ctx / 64) splits
     __shared__ AttnTcSmem sm;
+    __shared__ int s_last;
     float* out = apart + ((((size_t)b * nkv + h) * max_splits + split) * G) * (HD + 2);
     attn_tc_item<MODE>(qkv + (size_t)b * qkv_rows, p, btab + (size_t)b * mbps, kv_blocks, kc, vc, layer, L, nq, nkv,
                        h, G, rope, split, out, err, sm, (int)threadIdx.x, 0);
+    if (!fz.tickets) return;
+    __syncthreads();  // this split's partial is written
+    if (threadIdx.x == 0) {
+        __threadfence();
+        uint32_t* tk = fz.tickets + (size_t)b * nkv + h;
+        const int last = atomicAdd(tk, 1u) == (uint32_t)(ns - 1);
+        if (last) {
+            atomicExch(tk, 0u);
+            __threadfence();
+        }
+        s_last = last;
+    }
+    __syncthreads();
+    if (s_last) attn_combine_heads(base, ns, G, b, h, fz.att + (size_t)b * nq * HD, fz.op, (int)threadIdx.x);
 }
 
 // Combines the splits of the attention output and prepares it as the o projection's input:
@@ -287,16 +310,6 @@ __global__ void __launch_bounds__(128) attn_decode_tc_kernel(const float* __rest
 //    128-byte-swizzled [2 Bp][128 B] tile, and the block's (max/16383, sum) at [block][b];
 //  * xs (f16 small-M path): f16(att) in the 128-byte-swizzled k-block-major layout, row scale 1
 //    (|att| <= max|v| <= 65504, the f16 range, so no scaling is needed).
-struct OPrep {
-    uint8_t* cols = nullptr;
-    float2* meta = nullptr;
-    int Kp = 0, nxbs = 0;
-    uint8_t* xs = nullptr;
-    float* xscale = nullptr;
-    uint8_t* xl = nullptr;
-    float2* xm = nullptr;
-    int Bp = 0;
-};
 __global__ void __launch_bounds__(128) attn_combine_kernel(const uint32_t* __restrict__ pos, uint32_t max_pos, int nq,
                                                            int nkv, int G, int hd, int max_splits,
                                                            const float* __restrict__ apart, float* __restrict__ att,
@@ -455,14 +468,21 @@ struct AttnLaunch {
     const float2* rope = nullptr;
     float* apart = nullptr;
     int* err = nullptr;
+    AttnFuse fuse;  // tickets set: the tensor-core kernel combines the splits itself
 };
+// Whether the split combine runs inside the attention kernel (the tensor-core layout).
+static bool attention_combines(const AttnLaunch& a) { return a.hd == 128 && a.G >= 4; }
 template <int MODE>
 static cudaError_t launch_attention_t(const AttnLaunch& a, int B, cudaStream_t st) {
     const dim3 grid(a.max_splits, a.nkv, B), block(128);
+    if (a.hd == 128 && a.G >= 4)
+        return launch_pdl(attn_decode_tc_kernel<128, MODE>, grid, block, 0, st, a.qkv, a.qkv_rows, a.pos, a.btab,
+                          a.mbps, a.kv_blocks, a.kc, a.vc, a.layer, a.L, a.nq, a.nkv, a.G, a.max_splits, a.rope,
+                          a.apart, a.err, a.fuse);
     if (a.hd == 128)
-        return launch_pdl(a.G >= 4 ? attn_decode_tc_kernel<128, MODE> : attn_decode_kernel<128, MODE>, grid, block,
-                          0, st, a.qkv, a.qkv_rows, a.pos, a.btab, a.mbps, a.kv_blocks, a.kc, a.vc, a.layer, a.L, a.nq,
-                          a.nkv, a.G, a.max_splits, a.rope, a.apart, a.err);
+        return launch_pdl(attn_decode_kernel<128, MODE>, grid, block, 0, st, a.qkv, a.qkv_rows, a.pos, a.btab, a.mbps,
+                          a.kv_blocks, a.kc, a.vc, a.layer, a.L, a.nq, a.nkv, a.G, a.max_splits, a.rope, a.apart,
+                          a.err);
     if (a.hd == 64)
         return launch_pdl(attn_decode_kernel<64, MODE>, grid, block, 0, st, a.qkv, a.qkv_rows, a.pos, a.btab, a.mbps,
                           a.kv_blocks, a.kc, a.vc, a.layer, a.L, a.nq, a.nkv, a.G, a.max_splits, a.rope, a.apart,
@@ -663,8 +683,6 @@ static int forward_step(pox_model* m, int B, cudaStream_t st, bool prefill, int 
                            (const uint32_t*)m->pos, (const int32_t*)m->btab, (int)m->max_blocks_per_seq,
                            (int)m->kv_blocks, m->kc, m->vc, l, m->L, m->nq, m->nkv, m->hd, (const float2*)m->rope,
                            ctx->err_dev);
-        if (e == cudaSuccess) e = launch_attention(al, B, prefill ? kAttnPrefill : kAttnDecode, st);
-        if (e != cudaSuccess) return cuda_error(e, "attention launch");
         // the combine writes the o projection's prepared input when that tensor takes one
         OPrep op;
         XTarget xt;
@@ -682,10 +700,21 @@ static int forward_step(pox_model* m, int B, cudaStream_t st, bool prefill, int 
             op.xm = xt.xm;
             op.Bp = xt.Bp;
         }
-        e = launch_pdl(attn_combine_kernel, dim3((m->nq * m->hd + 127) / 128, B), dim3(128), 0, st,
-                       (const uint32_t*)m->pos, (uint32_t)(m->max_blocks_per_seq * kPage), m->nq, m->nkv, m->G, m->hd,
-                       m->max_splits, (const float*)m->apart, m->att, op);
-        if (e != cudaSuccess) return cuda_error(e, "attention combine launch");
+        // the tensor-core attention combines its splits itself (tickets shared with the persistent
+        // kernel: the two never run at once); other layouts launch the combine kernel
+        if (attention_combines(al)) {
+            al.fuse.tickets = m->ptickets;
+            al.fuse.att = m->att;
+            al.fuse.op = op;
+        }
+        if (e == cudaSuccess) e = launch_attention(al, B, prefill ? kAttnPrefill : kAttnDecode, st);
+        if (e != cudaSuccess) return cuda_error(e, "attention launch");
+        if (!attention_combines(al)) {
+            e = launch_pdl(attn_combine_kernel, dim3((m->nq * m->hd + 127) / 128, B), dim3(128), 0, st,
+                           (const uint32_t*)m->pos, (uint32_t)(m->max_blocks_per_seq * kPage), m->nq, m->nkv, m->G,
+                           m->hd, m->max_splits, (const float*)m->apart, m->att, op);
+            if (e != cudaSuccess) return cuda_error(e, "attention combine launch");
+        }
         if ((rc = row_split_gemv(m, w.o, m->att, B, 2 * l, nullptr, st, fuse))) return rc;
         norm.norm_w = w.mlp_norm;
         if ((rc = gemv_launch(ctx, w.gu, m->x, B, m->gu, st, &norm))) return rc;

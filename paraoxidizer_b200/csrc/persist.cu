@@ -63,9 +63,6 @@ __device__ __forceinline__ bool cons_sync_and(bool p) {
         : "memory");
     return r != 0;
 }
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
 
 // Grid barrier of the persistent kernel, run by the consumer warps of every CTA: bar[0] counts the
 // arrivals of this launch (the k-th barrier of a launch completes at (k + 1) x grid arrivals; the

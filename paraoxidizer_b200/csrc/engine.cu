@@ -470,8 +470,11 @@ struct AttnLaunch {
     int* err = nullptr;
     AttnFuse fuse;  // tickets set: the tensor-core kernel combines the splits itself
 };
-// Whether the split combine runs inside the attention kernel (the tensor-core layout).
-static bool attention_combines(const AttnLaunch& a) { return a.hd == 128 && a.G >= 4; }
+// Whether the split combine runs inside the attention kernel: the tensor-core layout, and at most
+// 16 splits (contexts up to 1024), which the last CTA of a (sequence, kv head) loads in one round.
+// Longer contexts measured faster with the combine kernel's parallel merge (70B at context 4096,
+// two GPUs, batch 16: 616 against 682 tok/s).
+static bool attention_combines(const AttnLaunch& a) { return a.hd == 128 && a.G >= 4 && a.max_splits <= 16; }
 template <int MODE>
 static cudaError_t launch_attention_t(const AttnLaunch& a, int B, cudaStream_t st) {
     const dim3 grid(a.max_splits, a.nkv, B), block(128);

@@ -138,6 +138,34 @@ def test_persistent_decode_matches_forward_token(be, name, nseq):
     model.close()
 
 
+@pytest.mark.parametrize("name", ["l8", "l70"])
+def test_decode_long_context_capacity(be, name):
+    """A model whose block tables reach 1280 positions (20 attention splits) merges the splits in the
+    combine kernel; up to 16 splits the tensor-core attention merges them itself. Both against the
+    oracle, at batch 2."""
+    cfg = CONFIGS[name]
+    w = make_llama(cfg, seed=29, norm_jitter=0.1)
+    model = CudaModel(be, cfg, max_batch=2, kv_blocks=40, max_blocks_per_seq=80)
+    load_into(model, w)
+    ow = oracle_weights(w)
+    rng = np.random.default_rng(31)
+    prompts = [list(rng.integers(0, cfg["vocab"], n)) for n in (140, 9)]
+    steps = 6
+    oracles = [O.OracleModel(cfg, ow, max_seq=256, kv_f16=True) for _ in prompts]
+    seqs = [model.new_sequence() for _ in prompts]
+    feeds = [list(p) for p in prompts]
+    for t in range(max(len(p) for p in prompts) + steps):
+        active = [i for i in range(2) if t < len(prompts[i]) + steps]
+        tokens = [int(feeds[i][t]) for i in active]
+        logits, _ = model.decode(tokens, [seqs[i] for i in active])
+        for j, i in enumerate(active):
+            ref = oracles[i].forward_token(tokens[j], t)
+            assert float(np.max(np.abs(logits[j] - ref))) <= E2E_TOL, (name, i, t)
+            if t + 1 >= len(prompts[i]):
+                feeds[i].append(int(np.argmax(ref)))
+    model.close()
+
+
 # The Llama-3-8B widths (d 4096, 32 / 8 heads of 128, FFN 14336, vocab 128256, f16 embedding and
 # lm_head), two layers so the oracle's scalar forward_token stays within seconds per token.
 LLAMA8B_2L = {"hidden": 4096, "inter": 14336, "layers": 2, "n_heads": 32, "n_kv_heads": 8, "vocab": 128256,

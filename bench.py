@@ -18,6 +18,7 @@ restatement of quant::gemv_int4, single-threaded as the reference is) on the hos
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import re
@@ -678,8 +679,10 @@ def run_ours(args):
     xh = np.ascontiguousarray(x, dtype=np.float32)
     e2e_steps = min(args.steps, 2000)
     fn = L.lib().pox_cuda_gemv_int4_outliers
-    call_args = [(be.ctx, p.ctypes.data, p.size, s.ctypes.data, s.size, GS, ROWS, COLS, o.ctypes.data, o.size,
-                  xh.ctypes.data, xh.size, yh.ctypes.data, yh.size) for p, s, o in copies]
+    vp, sz = ctypes.c_void_p, ctypes.c_size_t  # converted once, as a compiled caller holds them
+    call_args = [(vp(be.ctx), vp(p.ctypes.data), sz(p.size), vp(s.ctypes.data), sz(s.size), sz(GS), sz(ROWS),
+                  sz(COLS), vp(o.ctypes.data), sz(o.size), vp(xh.ctypes.data), sz(xh.size), vp(yh.ctypes.data),
+                  sz(yh.size)) for p, s, o in copies]
     for i in range(10):
         p, s, o = copies[i % NCOPY]
         be.gemv_int4_outliers(p, s, GS, ROWS, COLS, o, x, yh)  # the wrapper's checks, once per copy

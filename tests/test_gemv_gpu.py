@@ -238,3 +238,23 @@ def test_host_slice_calls_replay_as_one_graph(be):
             ref = O.gemv_int4(packed, scales, gs, rows, cols, tab, x[b * cols:(b + 1) * cols])
             assert max_rel(y[b], ref) <= GEMV_TOL, (i, batch, b)
     t.free()
+
+
+def test_replayed_host_graph_reads_each_calls_x(be):
+    """Host-slice calls from the second on replay one graph over the same mapped staging. Six calls
+    in a row with a new x each, for INT4 (integer x preparation), INT8 and F16 (the f16 hi / lo
+    preparation): every y must follow its own call's x, never the previous call's."""
+    rows, cols = 512, 4096
+    rng = np.random.default_rng(77)
+    w = make_w(rows, cols, 78)
+    packed, scales = Q.quantize_int4_group(w, 128)
+    q8, s8 = Q.quantize_int8_symmetric(w)
+    wb = w.astype(np.float16).view(np.uint16)
+    cases = [(be.upload_int4(packed, scales, rows, cols, 128), lambda x: O.gemv_int4(packed, scales, 128, rows, cols, None, x)),
+             (be.upload_int8(q8, s8, rows, cols), lambda x: O.gemv_int8(q8, s8, rows, cols, x)),
+             (be.upload_f16(wb, rows, cols), lambda x: O.gemv_f16(wb, rows, cols, x))]
+    for t, ref in cases:
+        for i in range(6):
+            x = rng.standard_normal(cols, dtype=np.float32) * np.float32(1 + i)
+            assert max_rel(t.gemv_host(x), ref(x)) <= GEMV_TOL, (t, i)
+        t.free()

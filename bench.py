@@ -677,7 +677,9 @@ def run_ours(args):
     # numpy checks of the Python wrapper are not part of the call)
     yh = np.zeros(ROWS, np.float32)
     xh = np.ascontiguousarray(x, dtype=np.float32)
-    e2e_steps = min(args.steps, 2000)
+    # 2000 calls whatever --steps (about 60 ms): the per-call cost in steady state; the first calls
+    # of a run are about 2 us slower, which a 20-call average would carry
+    e2e_steps = 2000
     fn = L.lib().pox_cuda_gemv_int4_outliers
     vp, sz = ctypes.c_void_p, ctypes.c_size_t  # converted once, as a compiled caller holds them
     call_args = [(vp(be.ctx), vp(p.ctypes.data), sz(p.size), vp(s.ctypes.data), sz(s.size), sz(GS), sz(ROWS),

@@ -3,7 +3,7 @@ decode step, checked against the oracle.
 
 * Every shard of an INT4 tensor with outliers dequantizes bit-exactly to the same slice of the
   whole tensor's dequantization (kernels.rs:85-128 + outlier.rs:88-95).
-* world_size-2 gloo ranks run forward_token (engine.rs:411-716) split the way the CUDA decode step
+* 2, 4 and 8 gloo ranks run forward_token (engine.rs:411-716) split the way the CUDA decode step
   splits it -- column-split q/k/v/gate/up/lm_head, row-split o/down summed by an allreduce after
   each, the greedy pick over the ranks' (logit, token) pairs -- through the oracle's primitives,
   and match the oracle's unsplit forward_token: logits within 1e-4 and the same greedy tokens.
@@ -21,7 +21,10 @@ from paraoxidizer_b200.synth import make_llama, oracle_weights
 
 CFG = {"hidden": 256, "inter": 512, "layers": 2, "n_heads": 8, "n_kv_heads": 2, "vocab": 1000,
        "rms_eps": 1e-5, "rope_theta": 500000.0}
-CFGS = {2: CFG, 4: dict(CFG, hidden=512, n_kv_heads=4)}  # 4 ranks: one kv head and 128 columns of o/down each
+CFGS = {2: CFG, 4: dict(CFG, hidden=512, n_kv_heads=4),  # 4 ranks: one kv head and 128 columns of o/down each
+        # 8 ranks: the shapes of the benchmark's 8-rank tp_check (two query heads of 64 and one kv
+        # head per rank, 128 columns of o and 256 of down per rank)
+        8: dict(CFG, hidden=1024, inter=2048, n_heads=16, n_kv_heads=8)}
 
 
 def _dequant(t):
@@ -41,7 +44,7 @@ def _tensor(rows, cols, seed):
             "outlier_bytes": Q.outliers_to_bytes(*tab)}
 
 
-@pytest.mark.parametrize("tp", [2, 4])
+@pytest.mark.parametrize("tp", [2, 4, 8])
 def test_shards_dequantize_to_slices(tp):
     t = _tensor(64, 1024, 7)
     assert t["outliers"] is not None and len(t["outliers"][0]) > 10
@@ -138,7 +141,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_tp_gloo_matches_oracle(tmp_path, world):
     import torch.multiprocessing as mp
 

@@ -78,6 +78,20 @@ def test_gemv_int4_metal_entry_4096x4096(be):
     assert max_rel(y, ref) <= 2.5e-4
 
 
+def test_gemv_int4_metal_backend_case(be):
+    """The reference's own test of its GPU GEMV (metal_backend.rs:226-246), through the call that
+    mirrors MetalBackend::gemv_int4: 32 x 64 weights sin(0.05 i), x = cos(0.1 i), INT4 groups of
+    32. The reference asserts sum |y| > 0.01; here y is also held to the oracle."""
+    rows, cols, gs = 32, 64, 32
+    w = np.sin(np.arange(rows * cols, dtype=np.float32) * np.float32(0.05)).astype(np.float32)
+    x = np.cos(np.arange(cols, dtype=np.float32) * np.float32(0.1)).astype(np.float32)
+    packed, scales = Q.quantize_int4_group(w, gs)
+    y = np.zeros(rows, np.float32)
+    be.gemv_int4(packed, scales, rows, cols, gs, x, y)
+    assert float(np.sum(np.abs(y))) > 0.01
+    assert max_rel(y, O.gemv_int4(packed, scales, gs, rows, cols, None, x)) <= GEMV_TOL
+
+
 def test_gemv_int4_outliers_4096x14336(be):
     # workload: 4096x14336 INT4 g128, 0.5% of input channels x20, 3.5-sigma extraction
     rows, cols = 4096, 14336

@@ -165,3 +165,23 @@ def test_gemv_int4_matches_dequant_dot():
     O.outliers_apply(tab[0], tab[1], d)
     for r in range(rows):
         assert y[r] == np.float32(O.dot_product_simd(d[r * cols:(r + 1) * cols], x))
+
+
+def metal_test_case():
+    """Inputs of the reference's own GEMV backend test (metal_backend.rs:226-246): 32 x 64 weights
+    sin(0.05 i), x = cos(0.1 i), INT4 groups of 32."""
+    rows, cols, gs = 32, 64, 32
+    w = np.sin(np.arange(rows * cols, dtype=np.float32) * np.float32(0.05)).astype(np.float32)
+    x = np.cos(np.arange(cols, dtype=np.float32) * np.float32(0.1)).astype(np.float32)
+    return rows, cols, gs, w, x
+
+
+def test_metal_backend_case_kat():
+    # metal_backend.rs:226-246: quantize_int4_group(&weights, 32), gemv_int4, then "sum |y| > 0.01"
+    rows, cols, gs, w, x = metal_test_case()
+    p, s = O.quantize_int4_group(w, gs)
+    y = O.gemv_int4(p, s, gs, rows, cols, None, x)
+    assert float(np.sum(np.abs(y))) > 0.01
+    d = O.dequantize_int4_group(p, s, gs, rows * cols)
+    for r in range(rows):
+        assert y[r] == np.float32(O.dot_product_simd(d[r * cols:(r + 1) * cols], x))

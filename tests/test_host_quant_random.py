@@ -3,9 +3,9 @@ with the oracle's C restatement of the same reference functions, bit for bit:
 quantize_int4_group (kernels.rs:26-82), quantize_int8_symmetric (kernels.rs:131-154) and
 extract_and_zero_outliers (outlier.rs:57-85). Inputs mix the cases the reference's loops treat
 specially: exact .5 ties, +0 / -0, subnormals, values near the f16 range, NaN and +-inf."""
-import numpy as np
 import warnings
 
+import numpy as np
 from hypothesis import given, settings, strategies as st
 
 from oracle import oracle as O

@@ -80,3 +80,18 @@ def test_rms_norm_and_swiglu_match_float64():
     u = rng.standard_normal(g.size).astype(np.float32)
     gd = g.astype(np.float64)
     assert rel(O.swiglu(g, u), gd / (1 + np.exp(-gd)) * u.astype(np.float64)) <= 2e-6
+
+
+@pytest.mark.parametrize("rows,cols", [(64, 4096), (33, 100)])
+def test_gemv_int8_and_f16_match_float64(rows, cols):
+    # kernels.rs:229-255 (INT8: q * scale per element, f32 dot) and engine.rs:235-250 (F16 rows)
+    rng = np.random.default_rng(rows + cols)
+    w = rng.standard_normal(rows * cols).astype(np.float32) * np.float32(0.02)
+    x = rng.standard_normal(cols).astype(np.float32)
+    q, s = O.quantize_int8_symmetric(w)
+    wq = O.dequantize_int8_symmetric(q, s).astype(np.float64).reshape(rows, cols)
+    # f32 sums of up to 4096 products: a few 1e-6 of max |y| (measured 2.2e-6 at 4096)
+    assert rel(O.gemv_int8(q, s, rows, cols, x), wq @ x.astype(np.float64)) <= 1e-5
+    wb = w.astype(np.float16).view(np.uint16)
+    ref = wb.view(np.float16).astype(np.float64).reshape(rows, cols) @ x.astype(np.float64)
+    assert rel(O.gemv_f16(wb, rows, cols, x), ref) <= 1e-5

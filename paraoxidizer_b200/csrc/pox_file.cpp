@@ -182,12 +182,39 @@ struct JsonParser {
         }
         return true;
     }
+    // One UTF-8 sequence whose lead byte c (>= 0x80) was just read, validated as Rust's
+    // str::from_utf8 does (RFC 3629: no overlong forms, no surrogates, nothing above U+10FFFF).
+    bool utf8_seq(unsigned char c, std::string& o) {
+        int n;
+        unsigned char lo = 0x80, hi = 0xBF;  // range of the first continuation byte
+        if (c >= 0xC2 && c <= 0xDF) n = 1;
+        else if (c == 0xE0) n = 2, lo = 0xA0;
+        else if ((c >= 0xE1 && c <= 0xEC) || c == 0xEE || c == 0xEF) n = 2;
+        else if (c == 0xED) n = 2, hi = 0x9F;
+        else if (c == 0xF0) n = 3, lo = 0x90;
+        else if (c >= 0xF1 && c <= 0xF3) n = 3;
+        else if (c == 0xF4) n = 3, hi = 0x8F;
+        else return fail("invalid UTF-8 in a string");
+        if (end - p < n) return fail("invalid UTF-8 in a string");
+        o += (char)c;
+        for (int i = 0; i < n; i++) {
+            const unsigned char d = (unsigned char)p[i];
+            if (d < (i ? 0x80 : lo) || d > (i ? 0xBF : hi)) return fail("invalid UTF-8 in a string");
+            o += (char)d;
+        }
+        p += n;
+        return true;
+    }
     bool string(std::string& o) {
         if (p >= end || *p != '"') return fail("expected a string");
         p++;
         while (p < end && *p != '"') {
             const unsigned char c = (unsigned char)*p++;
             if (c < 0x20) return fail("control character in a string");
+            if (c >= 0x80) {
+                if (!utf8_seq(c, o)) return false;
+                continue;
+            }
             if (c != '\\') {
                 o += (char)c;
                 continue;
@@ -206,7 +233,9 @@ struct JsonParser {
                 case 'u': {
                     uint32_t c1;
                     if (!hex4(c1)) return false;
-                    if (c1 >= 0xD800 && c1 < 0xDC00 && end - p >= 6 && p[0] == '\\' && p[1] == 'u') {
+                    if (c1 >= 0xDC00 && c1 < 0xE000) return fail("lone trailing surrogate in a \\u escape");
+                    if (c1 >= 0xD800 && c1 < 0xDC00) {  // a high surrogate needs a \\u low surrogate next
+                        if (end - p < 6 || p[0] != '\\' || p[1] != 'u') return fail("lone leading surrogate in a \\u escape");
                         p += 2;
                         uint32_t c2;
                         if (!hex4(c2)) return false;

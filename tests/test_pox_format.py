@@ -157,3 +157,79 @@ def test_ffi_symbols_declared():
                  "pox_file_verify_integrity", "pox_file_tensor_shard", "pox_cuda_model_load"):
         assert name in L.declared_symbols()
         assert hasattr(L.lib(), name)
+
+
+def _named_container(name: str) -> bytes:
+    meta = {"model_config": model_config_dict(CFG), "total_parameters": 0, "quantized_by": "t", "timestamp_utc": 0,
+            "original_format": "t", "base_model_name": "t"}
+    w = PoxWriter(meta, {"default_precision": "F16", "group_size": 0, "outlier_strategy": "Disabled",
+                         "layer_assignments": {}}, "r")
+    w.add_tensor(name, (4,), L.POX_F16, 0, np.arange(4, dtype=np.uint16))
+    return w.write_to_bytes()
+
+
+def test_json_strings_follow_the_reference_parser():
+    """The container's JSON is read as serde_json::from_slice reads it (pox.rs:184-226): strings
+    are UTF-8 (multibyte names kept), a \\u surrogate pair decodes to one character, and invalid
+    UTF-8 or a lone surrogate is a format error rather than a name with stray bytes."""
+    b = _named_container("w.层.XXXXXXXXXXXX")
+    assert PoxFile.from_bytes(b).tensors[0]["name"] == "w.层.XXXXXXXXXXXX"
+    pair = b.replace(b"XXXXXXXXXXXX", b"\\ud835\\udd38")  # same length: offsets stay valid
+    assert PoxFile.from_bytes(pair).tensors[0]["name"] == "w.层.\U0001d538"
+    bad = {"invalid UTF-8": b.replace("层".encode(), b"\xff\xfe\xfd"),
+           "overlong": b.replace("层".encode(), b"\xe0\x80\xaf"),
+           "encoded surrogate": b.replace("层".encode(), b"\xed\xa0\x80"),
+           "lone trailing surrogate": b.replace(b"XXXXXXXXXXXX", b"\\udd38\\ud835"),
+           "lone leading surrogate": b.replace(b"XXXXXXXXXXXX", b"\\ud835abcdef")}
+    for what, data in bad.items():
+        assert len(data) == len(b), what
+        with pytest.raises(L.PoxError) as ei:
+            PoxFile.from_bytes(data)
+        assert ei.value.code == L.POX_ERR_FORMAT, what
+
+
+def test_mutated_containers_open_or_fail_cleanly():
+    """Seeded corruption of a small container (bytes overwritten, header fields set to extremes,
+    truncation): every file either opens, with every accessor, shard and verify_integrity then
+    returning data or an error, or is rejected with a PoxError. Nothing reads out of bounds."""
+    import random
+
+    cfg = dict(CFG, layers=1, vocab=64)
+    b = llama_pox_bytes(cfg, make_llama(cfg, seed=1, outlier_policy="automatic"))
+    rng = random.Random(7)
+    opened = 0
+    for _ in range(300):
+        d = bytearray(b)
+        kind = rng.randrange(3)
+        if kind == 0:
+            for _ in range(rng.randrange(1, 8)):
+                d[rng.randrange(len(d))] = rng.randrange(256)
+        elif kind == 1:
+            d = d[:rng.randrange(len(d))]
+        else:
+            struct.pack_into("<Q", d, 16 + 8 * rng.randrange(12),
+                             rng.choice([0, 1, 2**63, 2**64 - 1, len(b), rng.randrange(2**64)]))
+        try:
+            f = PoxFile.from_bytes(bytes(d))
+        except L.PoxError:
+            continue
+        opened += 1
+        for t in f.tensors:
+            for fn in (f.get_tensor_data, f.get_scale_data, f.get_outlier_data):
+                try:
+                    v = fn(t["name"])
+                    if v is not None and v.size:
+                        _ = int(v[0]) + int(v[-1])
+                except L.PoxError:
+                    pass
+            try:
+                f.shard(t["name"], 1, 1, 2)
+            except L.PoxError:
+                pass
+        for call in (f.model_config, f.verify_integrity):
+            try:
+                call()
+            except L.PoxError:
+                pass
+        f.close()
+    assert opened > 0

@@ -14,9 +14,11 @@
 
 #include <algorithm>
 #include <atomic>
+#include <cmath>
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
+#include <initializer_list>
 #include <map>
 #include <memory>
 #include <string>
@@ -257,6 +259,7 @@ struct JsonParser {
         if (p < end && *p == '-') p++;
         if (p >= end || *p < '0' || *p > '9') return fail("bad number");
         bool integer = true;
+        if (*p == '0' && p + 1 < end && p[1] >= '0' && p[1] <= '9') return fail("bad number (leading zero)");
         while (p < end && *p >= '0' && *p <= '9') p++;
         if (p < end && *p == '.') {
             integer = false;
@@ -274,7 +277,10 @@ struct JsonParser {
         const std::string lit(s, p);
         v.kind = Json::Num;
         v.num = strtod(lit.c_str(), nullptr);
-        if (integer && lit[0] != '-' && lit.size() <= 20) {
+        if (integer && lit == "-0") {  // serde_json reads -0 as the integer 0
+            v.is_uint = true;
+            v.u = 0;
+        } else if (integer && lit[0] != '-' && lit.size() <= 20) {
             uint64_t u = 0;
             bool ok = true;
             for (char c : lit) {
@@ -291,10 +297,10 @@ struct JsonParser {
         return true;
     }
     bool value(Json& v) {
-        if (++depth > 64) return fail("nesting too deep");
         ws();
         if (p >= end) return fail("unexpected end of JSON");
         bool ok = true;
+        if ((*p == '{' || *p == '[') && ++depth > 128) return fail("recursion limit exceeded");  // serde_json's
         if (*p == '{') {
             p++;
             v.kind = Json::Obj;
@@ -358,7 +364,7 @@ struct JsonParser {
         } else {
             ok = number(v);
         }
-        depth--;
+        if (v.kind == Json::Obj || v.kind == Json::Arr) depth--;
         return ok;
     }
     bool parse(const uint8_t* b, size_t n, Json& out) {
@@ -394,6 +400,113 @@ int dtype_code(const std::string& s) {
 bool u64_of(const Json* j, uint64_t& v) {
     if (!j || j->kind != Json::Num || !j->is_uint) return false;
     v = j->u;
+    return true;
+}
+
+// The typed structs the reference deserializes each JSON section into (serde derive, unknown
+// fields ignored): PoxMetadata / PoxQuantPlanRecord / PoxManifest / PoxSignatureBlock
+// (pox.rs:119-158), ModelConfig (crates/paraoxidizer-core/src/arch.rs:94-112) and TensorMeta
+// (crates/paraoxidizer-core/src/tensor.rs:114-128). A section that would not deserialize is a
+// format error here as it is an Err there: a missing or repeated field, a wrong JSON type, an
+// integer field given a fraction, exponent, sign or out-of-range value, an unknown enum variant.
+// (serde would also take a struct written as a JSON array of its fields in order; such a file is
+// rejected here.)
+enum class FT { Str, OptStr, U64, U32, F64, Bool, MapStr, Arch, DType, Group, Shape, Config };
+struct Field {
+    const char* key;
+    FT type;
+    bool required;
+};
+const Field kConfig[] = {{"architecture", FT::Arch, true},         {"hidden_size", FT::U64, true},
+                         {"intermediate_size", FT::U64, true},     {"num_hidden_layers", FT::U64, true},
+                         {"num_attention_heads", FT::U64, true},   {"num_key_value_heads", FT::U64, true},
+                         {"vocab_size", FT::U64, true},            {"max_position_embeddings", FT::U64, true},
+                         {"rms_norm_eps", FT::F64, true},          {"rope_theta", FT::F64, true},
+                         {"tie_word_embeddings", FT::Bool, true},  {"eos_token_id", FT::U32, false},
+                         {"bos_token_id", FT::U32, false}};
+const Field kMetadata[] = {{"model_config", FT::Config, true}, {"total_parameters", FT::U64, true},
+                           {"quantized_by", FT::Str, true},    {"timestamp_utc", FT::U64, true},
+                           {"original_format", FT::Str, true}, {"base_model_name", FT::Str, true}};
+const Field kTensorMeta[] = {{"name", FT::Str, true},         {"shape", FT::Shape, true},
+                             {"dtype", FT::DType, true},      {"group_size", FT::Group, true},
+                             {"data_offset", FT::U64, true},  {"data_len", FT::U64, true},
+                             {"scale_offset", FT::U64, true}, {"scale_len", FT::U64, true},
+                             {"outlier_offset", FT::U64, true}, {"outlier_len", FT::U64, true},
+                             {"sha256", FT::Str, true}};
+const Field kQuantPlan[] = {{"default_precision", FT::Str, true},
+                            {"group_size", FT::U64, true},
+                            {"outlier_strategy", FT::Str, true},
+                            {"layer_assignments", FT::MapStr, true}};
+const Field kManifest[] = {{"run_id", FT::Str, true},          {"source_model_sha256", FT::Str, true},
+                           {"calibration_sha256", FT::OptStr, false}, {"compiler_version", FT::Str, true},
+                           {"target_arch", FT::Str, true},     {"tensor_hashes", FT::MapStr, true},
+                           {"artifact_sha256", FT::Str, true}};
+const Field kSignature[] = {{"public_key_hex", FT::Str, true}, {"signature_hex", FT::Str, true}};
+
+bool one_of(const std::string& s, std::initializer_list<const char*> names) {
+    for (const char* n : names)
+        if (s == n) return true;
+    return false;
+}
+
+template <size_t N>
+bool check_struct(const Json& v, const Field (&fields)[N], std::string& err);
+
+bool check_field(const Json& j, FT t, std::string& err) {
+    switch (t) {
+        case FT::Str: return j.kind == Json::Str;
+        case FT::OptStr: return j.kind == Json::Str || j.kind == Json::Null;
+        case FT::U64: return j.kind == Json::Num && j.is_uint;
+        case FT::U32: return j.kind == Json::Num && j.is_uint && j.u <= 0xFFFFFFFFull;
+        case FT::F64: return j.kind == Json::Num && std::isfinite(j.num);
+        case FT::Bool: return j.kind == Json::Bool;
+        case FT::MapStr:
+            if (j.kind != Json::Obj) return false;
+            for (const auto& kv : j.obj)
+                if (kv.second.kind != Json::Str) return false;
+            return true;
+        case FT::Arch: return j.kind == Json::Str && one_of(j.s, {"Llama", "Qwen", "Mistral", "Gemma", "Phi", "Custom"});
+        case FT::DType:
+            return j.kind == Json::Str && one_of(j.s, {"F32", "F16", "BF16", "I8", "I4", "F8E4M3", "F8E5M2"});
+        case FT::Group: return j.kind == Json::Str && one_of(j.s, {"None", "G32", "G64", "G128", "G256"});
+        case FT::Shape:
+            if (j.kind != Json::Arr) return false;
+            for (const Json& d : j.arr)
+                if (d.kind != Json::Num || !d.is_uint) return false;
+            return true;
+        case FT::Config: return check_struct(j, kConfig, err);
+    }
+    return false;
+}
+
+template <size_t N>
+bool check_struct(const Json& v, const Field (&fields)[N], std::string& err) {
+    if (v.kind != Json::Obj) {
+        err = "expected a JSON object";
+        return false;
+    }
+    for (const Field& f : fields) {
+        const Json* found = nullptr;
+        for (const auto& kv : v.obj) {
+            if (kv.first != f.key) continue;
+            if (found) {
+                err = std::string("duplicate field `") + f.key + "`";
+                return false;
+            }
+            found = &kv.second;
+        }
+        if (!found) {
+            if (f.required) {
+                err = std::string("missing field `") + f.key + "`";
+                return false;
+            }
+            continue;
+        }
+        if (!check_field(*found, f.type, err)) {
+            if (err.empty()) err = std::string("invalid type or value for `") + f.key + "`";
+            return false;
+        }
+    }
     return true;
 }
 
@@ -452,14 +565,22 @@ int parse_container(pox_file* f) {
     f->flags = rd32(b + 8);
     for (int i = 0; i < 12; i++) f->header[i] = rd64(b + 16 + 8 * i);
     // header order: metadata, tensor index, quant plan, data, manifest, signature (offset, len each)
+    std::string why;
     if (!parse_json(f, f->header[0], f->header[1], "Metadata", f->metadata)) return POX_ERR_FORMAT;
+    if (!check_struct(f->metadata, kMetadata, why)) return set_error(POX_ERR_FORMAT, "Metadata: %s", why.c_str());
     Json index;
     if (!parse_json(f, f->header[2], f->header[3], "Tensor index", index)) return POX_ERR_FORMAT;
+    if (index.kind != Json::Arr) return set_error(POX_ERR_FORMAT, "tensor index is not a JSON array");
+    for (const Json& t : index.arr)
+        if (!check_struct(t, kTensorMeta, why)) return set_error(POX_ERR_FORMAT, "Tensor index: %s", why.c_str());
     if (!parse_json(f, f->header[4], f->header[5], "Quant plan", f->quant_plan)) return POX_ERR_FORMAT;
+    if (!check_struct(f->quant_plan, kQuantPlan, why)) return set_error(POX_ERR_FORMAT, "Quant plan: %s", why.c_str());
     if (!parse_json(f, f->header[8], f->header[9], "Manifest", f->manifest)) return POX_ERR_FORMAT;
+    if (!check_struct(f->manifest, kManifest, why)) return set_error(POX_ERR_FORMAT, "Manifest: %s", why.c_str());
     if (f->header[11] > 0) {
         Json sig;
         if (!parse_json(f, f->header[10], f->header[11], "Signature", sig)) return POX_ERR_FORMAT;
+        if (!check_struct(sig, kSignature, why)) return set_error(POX_ERR_FORMAT, "Signature: %s", why.c_str());
     }
     if (!f->metadata.get("model_config") || f->metadata.get("model_config")->kind != Json::Obj)
         return set_error(POX_ERR_FORMAT, "metadata has no model_config");

@@ -233,3 +233,104 @@ def test_mutated_containers_open_or_fail_cleanly():
                 pass
         f.close()
     assert opened > 0
+
+
+def _container(edit=None, replace=()) -> bytes:
+    """A one-tensor container; edit(writer) changes its sections before writing, then each
+    (old, new) byte replacement of equal length is applied (offsets stay valid)."""
+    meta = {"model_config": model_config_dict(CFG), "total_parameters": 0, "quantized_by": "t",
+            "timestamp_utc": 10, "original_format": "t", "base_model_name": "t"}
+    w = PoxWriter(meta, {"default_precision": "F16", "group_size": 0, "outlier_strategy": "Disabled",
+                         "layer_assignments": {}}, "r")
+    w.add_tensor("a", (4,), L.POX_F16, 0, np.arange(4, dtype=np.uint16))
+    if edit:
+        edit(w)
+    b = w.write_to_bytes()
+    for old, new in replace:
+        assert len(old) == len(new) and old in b
+        b = b.replace(old, new)
+    return b
+
+
+def _opens(b: bytes) -> bool:
+    try:
+        PoxFile.from_bytes(b).close()
+        return True
+    except L.PoxError as e:
+        assert e.code == L.POX_ERR_FORMAT
+        return False
+
+
+def test_sections_deserialize_like_the_reference_structs():
+    """Each JSON section must deserialize into the reference's typed struct (pox.rs:119-158,
+    arch.rs:94-112, tensor.rs:114-128; serde derive): required fields present and unique, integers
+    as non-negative integer literals, enums by variant name; unknown fields are ignored, optional
+    fields may be absent or null."""
+    def meta(key, value=None, drop=False):
+        def f(w):
+            if drop:
+                del w.metadata[key]
+            else:
+                w.metadata[key] = value
+        return f
+
+    def cfg(key, value=None, drop=False):
+        def f(w):
+            if drop:
+                del w.metadata["model_config"][key]
+            else:
+                w.metadata["model_config"][key] = value
+        return f
+
+    def man(key, value):
+        def f(w):
+            w.manifest[key] = value
+        return f
+
+    def tensor(key, value):
+        def f(w):
+            w.tensors[0][key] = value
+        return f
+
+    def sig(value):
+        def f(w):
+            w.signature = value
+        return f
+
+    accepted = {
+        "as written": _container(),
+        "unknown fields": _container(meta("extra", {"x": [1, 2]})),
+        "optional ids absent": _container(lambda w: [w.metadata["model_config"].pop(k) for k in ("eos_token_id",
+                                                                                                 "bos_token_id")]),
+        "u32 at its maximum": _container(cfg("eos_token_id", 2**32 - 1)),
+        "f64 given an integer": _container(cfg("rms_norm_eps", 0)),
+        "calibration hash null": _container(man("calibration_sha256", None)),
+        "calibration hash absent": _container(lambda w: w.manifest.pop("calibration_sha256")),
+        "calibration hash string": _container(man("calibration_sha256", "ab")),
+        "signature block": _container(sig({"public_key_hex": "ab", "signature_hex": "cd"})),
+        "integer -0": _container(replace=[(b'"timestamp_utc":10', b'"timestamp_utc":-0')]),
+        "duplicate unknown field": _container(lambda w: w.tensors[0].update(zzzz=1, yyyy=1),
+                                              [(b'"yyyy":1', b'"zzzz":1')]),
+    }
+    for what, b in accepted.items():
+        assert _opens(b), what
+    rejected = {
+        "metadata field missing": _container(meta("quantized_by", drop=True)),
+        "config field missing": _container(cfg("vocab_size", drop=True)),
+        "integer given a fraction": _container(meta("total_parameters", 1000.0)),
+        "integer given a sign": _container(meta("timestamp_utc", -1)),
+        "leading zero": _container(replace=[(b'"timestamp_utc":10', b'"timestamp_utc":01')]),
+        "u32 overflow": _container(cfg("eos_token_id", 2**32)),
+        "string given a number": _container(meta("quantized_by", 5)),
+        "bool given a number": _container(cfg("tie_word_embeddings", 0)),
+        "unknown architecture": _container(cfg("architecture", "Llama2")),
+        "unknown group size": _container(tensor("group_size", "G16")),
+        "duplicate tensor field": _container(tensor("data_lex", 5), [(b'"data_lex"', b'"data_len"')]),
+        "shape of floats": _container(tensor("shape", [4.0])),
+        "calibration hash number": _container(man("calibration_sha256", 5)),
+        "tensor hash not a string": _container(man("tensor_hashes", {"a": 1})),
+        "quant plan group size string": _container(lambda w: w.quant_plan.update(group_size="G32")),
+        "signature field missing": _container(sig({"public_key_hex": "ab"})),
+    }
+    for what, b in rejected.items():
+        assert not _opens(b), what

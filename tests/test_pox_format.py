@@ -130,7 +130,7 @@ def test_payload_past_the_end_is_none():
     assert ei.value.code == L.POX_ERR_FORMAT and "Missing data" in str(ei.value)
 
 
-@pytest.mark.parametrize("tp", [2, 4])
+@pytest.mark.parametrize("tp", [2, 4, 8])
 def test_shards_equal_tp_py(model, tp):
     w, b = model
     f = PoxFile.from_bytes(b)

@@ -13,7 +13,8 @@ Multi-GPU: each rank runs its own GEMV stream on its own weights (the path has n
 step: weak scaling, no data-path collective); the time is the max over ranks.
 
 `--impl reference` times the reference's CPU path for the same workload (the oracle's C
-restatement of quant::gemv_int4, single-threaded as the reference is) on the host cores.
+restatement of quant::gemv_int4, single-threaded per call as the reference is) on every host
+thread this process may use, one row slice per thread.
 """
 from __future__ import annotations
 
@@ -259,13 +260,22 @@ def run_reference(args):
     full = algorithmic_bytes(nnz)
     from oracle import oracle as O
 
-    rows_per_step = 64
-    rb, sb = COLS // 2, (COLS // GS) * 4
-    tables = _slice_tables(tab, rows_per_step)
+    import concurrent.futures as cf
 
-    def step(r0):
-        O.gemv_int4(packed[r0 * rb:(r0 + rows_per_step) * rb], scales[r0 * sb:(r0 + rows_per_step) * sb], GS,
-                    rows_per_step, COLS, tables[r0], x)
+    rows_per_slice = 64
+    rb, sb = COLS // 2, (COLS // GS) * 4
+    tables = _slice_tables(tab, rows_per_slice)
+    # every host thread this process may use runs its own row slice through the reference's
+    # single-threaded loop (the oracle's C calls release the GIL): one step = one slice per thread
+    threads = host_cpu()[1]
+    pool = cf.ThreadPoolExecutor(threads)
+
+    def one(r0):
+        O.gemv_int4(packed[r0 * rb:(r0 + rows_per_slice) * rb], scales[r0 * sb:(r0 + rows_per_slice) * sb], GS,
+                    rows_per_slice, COLS, tables[r0], x)
+
+    def step(i):
+        list(pool.map(one, [((i * threads + j) * rows_per_slice) % ROWS for j in range(threads)]))
 
     # bound the run: at most ~90 s of timed CPU work whatever K is
     t0 = time.perf_counter()
@@ -273,23 +283,26 @@ def run_reference(args):
     per_step = time.perf_counter() - t0
     steps = max(1, min(args.steps, int(90.0 / max(per_step, 1e-6))))
     for i in range(min(args.warmup, 3)):
-        step(((i + 1) * rows_per_step) % ROWS)
+        step(i + 1)
     t0 = time.perf_counter()
     for i in range(steps):
-        step((i * rows_per_step) % ROWS)
+        step(i)
     dt = time.perf_counter() - t0
-    bytes_per_step = full * rows_per_step / ROWS
+    pool.shutdown()
+    bytes_per_step = full * rows_per_slice * threads / ROWS
     gbs = bytes_per_step * steps / dt / 1e9
-    sample = (f"{steps} steps of quant::gemv_int4 (oracle C restatement) over {rows_per_step} rows x {COLS} cols "
-              f"each, with the full {nnz}-entry outlier table scanned per row as the reference does; bytes counted "
-              f"pro rata of one {ROWS}x{COLS} GEMV")
+    sample = (f"{steps} steps, each {threads} concurrent slices (one per host thread) of quant::gemv_int4 (oracle "
+              f"C restatement, single-threaded per call as the reference) over {rows_per_slice} rows x {COLS} cols, "
+              f"with the full {nnz}-entry outlier table scanned per row as the reference does; bytes counted pro "
+              f"rata of one {ROWS}x{COLS} GEMV")
     line = {"metric": METRIC, "value": round(gbs, 4), "unit": "GB/s", "impl": "reference", "n_gpus": world,
             "steps": steps, "warmup": min(args.warmup, 3), "ms_per_step": dt / steps * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded N(0,0.02) weights, N(0,1) f16 x)",
             "config": {"workload": WORKLOAD, "rows": ROWS, "cols": COLS, "group_size": GS, "batch": 1,
                        "outliers": nnz},
-            "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": 1, "kind": "port", "sample": sample},
+            "cpu_baseline": {"value": round(gbs, 4), "unit": "GB/s", "cores": threads, "kind": "port",
+                             "cpu_model": host_cpu()[0], "sample": sample},
             "e2e": {"value": round(gbs, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0

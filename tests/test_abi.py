@@ -52,3 +52,39 @@ def test_null_handles_are_rejected():
     assert lib.pox_cuda_tensor_gemv(None, None, None, 1, None, None) == L.POX_ERR_INVALID
     assert lib.pox_cuda_gemv_int4(None, None, 0, None, 0, 4, 4, 4, None, 0, None, 0) == L.POX_ERR_INVALID
     assert lib.pox_cuda_tensor_free(None, None) == L.POX_OK
+
+
+def _prototypes():
+    """{name: [parameter declarations]} of every function include/pox_cuda.h declares."""
+    import re
+
+    with open(L.HEADER) as f:
+        src = re.sub(r"/\*.*?\*/", "", f.read(), flags=re.S)
+    out = {}
+    for m in re.finditer(r"(?:^|\n)\s*(?:const )?[a-z_0-9]+\s*\**\s*(pox_(?:cuda|file)_\w+)\s*\(([^;]*?)\);", src):
+        params = " ".join(m.group(2).split())
+        out[m.group(1)] = [] if params in ("", "void") else [p.strip() for p in params.split(",")]
+    return out
+
+
+def test_ctypes_declarations_match_the_header():
+    """Every function the Python binding declares has the header's number of parameters, and a
+    pointer (or array) parameter is bound as a pointer type, a scalar as a scalar: the binding
+    cannot drift from the C ABI unnoticed."""
+    import ctypes as C
+
+    protos = _prototypes()
+    assert set(protos) == set(L.declared_symbols())
+    lib = L.lib()
+    scalars = (C.c_int, C.c_uint32, C.c_int32, C.c_size_t, C.c_float, C.c_uint64)
+    checked = 0
+    for name, params in protos.items():
+        argtypes = getattr(getattr(lib, name), "argtypes", None)
+        if argtypes is None:
+            continue
+        assert len(argtypes) == len(params), name
+        for decl, t in zip(params, argtypes):
+            is_ptr = "*" in decl or "[" in decl
+            assert (t not in scalars) == is_ptr, (name, decl, t)
+        checked += 1
+    assert checked >= 50, checked

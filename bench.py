@@ -597,6 +597,17 @@ def run_decode_only(args):
     return 0
 
 
+def _section(name, fn):
+    """Runs one optional part of the benchmark line (batched GEMV, decode, the checks, the CPU
+    baseline). A failure there is recorded in the line and on stderr, and the GEMV measurement
+    already taken is still printed."""
+    try:
+        return fn()
+    except Exception as e:  # noqa: BLE001 -- any failure of an optional part
+        print(f"bench: {name} failed: {e!r}", file=sys.stderr, flush=True)
+        return {"error": f"{type(e).__name__}: {e}"[:400]}
+
+
 def run_ours(args):
     import torch
 
@@ -717,34 +728,38 @@ def run_ours(args):
 
     batched = None
     if world == 1 and not args.no_decode:
-        batched = batched_gemv_bench(be)
+        batched = _section("batched_gemv", lambda: batched_gemv_bench(be))
 
     decode = None
     if not args.no_decode:
-        decode = decode_bench(be, batches=decode_batches(args), steps=args.decode_steps, world=world, rank=rank,
-                              **decode_kwargs(args))
+        decode = _section("decode", lambda: decode_bench(be, batches=decode_batches(args), steps=args.decode_steps,
+                                                         world=world, rank=rank, **decode_kwargs(args)))
 
     tpc = None
     decode70 = None
     if world > 1 and not args.no_decode:
-        tpc = tp_check(be, world, rank)
+        tpc = _section("tp_check", lambda: tp_check(be, world, rank))
         if not args.no_decode_70b and args.decode_model != "llama70b":
             # the Llama-3-70B configuration is quoted tensor-parallel on 2 / 4 / 8 GPUs
             a70 = argparse.Namespace(**vars(args))
             a70.decode_model, a70.decode_prefill = "llama70b", None
-            decode70 = decode_bench(be, batches=(1, 16, 64), steps=args.decode_steps_70b, world=world, rank=rank,
-                                    **decode_kwargs(a70))
+            decode70 = _section("decode_70b", lambda: decode_bench(be, batches=(1, 16, 64), steps=args.decode_steps_70b,
+                                                                   world=world, rank=rank, **decode_kwargs(a70)))
+
+    def cpu_leg():
+        cgbs, crows, ct = cpu_baseline_sample(packed, scales, tab)
+        cmodel, ncores = host_cpu()
+        c = {"value": round(cgbs, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+             "cpu_model": cmodel, "host_cores": ncores,
+             "sample": f"{crows} rows ({crows / ROWS:.2f} GEMVs) of the same workload in {ct:.1f} s through the "
+                       f"oracle's quant::gemv_int4 (single-threaded, as the reference)"}
+        if not args.no_decode:
+            c["decode"] = _section("cpu decode", lambda: cpu_decode_baseline(be))
+        return c
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cgbs, crows, ct = cpu_baseline_sample(packed, scales, tab)
-        cmodel, ncores = host_cpu()
-        cpu = {"value": round(cgbs, 4), "unit": "GB/s", "cores": 1, "kind": "port",
-               "cpu_model": cmodel, "host_cores": ncores,
-               "sample": f"{crows} rows ({crows / ROWS:.2f} GEMVs) of the same workload in {ct:.1f} s through the "
-                         f"oracle's quant::gemv_int4 (single-threaded, as the reference)"}
-        if not args.no_decode:
-            cpu["decode"] = cpu_decode_baseline(be)
+        cpu = _section("cpu_baseline", cpu_leg)
 
     if rank == 0:
         line = {"metric": METRIC, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -769,7 +784,7 @@ def run_ours(args):
                 "gpu_launches": launches_per_step * args.steps, "clocks": clocks, "check_max_rel": rel,
                 "cpu_baseline": cpu, "batched_gemv": batched, "decode": decode}
         if tpc is not None:
-            line["tp_check_max_abs"] = tpc["max_abs_logit_diff"]
+            line["tp_check_max_abs"] = tpc.get("max_abs_logit_diff")
             line["tp_check"] = tpc
         if decode70 is not None:
             line["decode_70b"] = decode70

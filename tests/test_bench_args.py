@@ -43,3 +43,13 @@ def test_tp_check_models_shard_at_their_rank_counts():
     for world, cfg in bench.TP_CHECK_CFGS.items():
         TP.check_tp(cfg, world)
         assert cfg["n_kv_heads"] >= world and (cfg["hidden"] // cfg["n_heads"]) * cfg["n_heads"] // world % 128 == 0
+
+
+def test_optional_sections_record_failures():
+    assert bench._section("ok", lambda: {"a": 1}) == {"a": 1}
+
+    def boom():
+        raise RuntimeError("device lost")
+
+    r = bench._section("decode", boom)
+    assert r == {"error": "RuntimeError: device lost"}
